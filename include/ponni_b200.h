@@ -1,0 +1,212 @@
+/*
+ * libponni_b200 -- C ABI of the B200-native PONNI batched-inference path.
+ *
+ * A model is a flat list of layer descriptors (the lowered form of PONNI's
+ * compile-time layer tuple).  All data is feature-major [features, batch]
+ * with the batch index contiguous, exactly as PONNI's LayoutRight Views.
+ * Every entry point returns a ponni_b200_status; the text of the last error
+ * on a model is available from ponni_b200_last_error().
+ *
+ * Plain pointers and sizes only: no CUDA, Kokkos or torch types appear in the
+ * signatures.  Streams are passed as opaque `void*` (a cudaStream_t; NULL
+ * means the model's own stream, so the legacy default stream is passed as
+ * cudaStreamLegacy, (void*)0x1).
+ *
+ * Reference interfaces replaced (paths inside mrnorman/ponni):
+ *   ponni_b200_model_create        <- ponni::create_inference_model[_single|_double|_half|_bhalf_precision]
+ *                                     src/ponni_create_model.h:21-98, Inference ctor src/ponni_Inference.h:159
+ *   ponni_b200_model_validate      <- Inference::validate            src/ponni_Inference.h:719-737
+ *   ponni_b200_forward             <- Inference::forward_batch_parallel(input,output)
+ *                                     src/ponni_Inference.h:352-389 (async on the model's stream)
+ *   ponni_b200_forward_host        <- forward_batch_parallel(create_device_copy(in)) + create_host_copy(out)
+ *                                     src/ponni_Inference.h:339-346, src/utils/ponni_view_ops.h:12-37
+ *   ponni_b200_reallocate_internal_state / ponni_b200_internal_state_capacity
+ *                                  <- src/ponni_Inference.h:169-180, 197-199
+ *   ponni_b200_planned_temporary_size / ponni_b200_saved_state_size
+ *                                  <- get_planned_temporary_size / get_saved_state_size
+ *                                     src/ponni_Inference.h:93-122, 204-223
+ *   ponni_b200_num_trainable_parameters, _set/_get_trainable_parameters
+ *                                  <- src/ponni_Inference.h:245-253, 689-716
+ *   ponni_b200_weight_schema_fingerprint <- src/ponni_Inference.h:270-288
+ *   ponni_b200_model_save_weights / _load_weights
+ *                                  <- Inference::save_weights / load_weights src/ponni_Inference.h:295-333
+ *                                     (.ponni Safetensors profile, src/utils/ponni_safetensors.h:175-407)
+ *   ponni_b200_read_ponni_tensor   <- load_ponni_tensor<N> src/utils/ponni_safetensors.h:409-444
+ *   ponni_b200_model_summary       <- Inference::print src/ponni_Inference.h:671-683
+ */
+#ifndef PONNI_B200_H
+#define PONNI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define PONNI_B200_ABI_VERSION 1
+
+typedef enum {
+  PONNI_B200_OK = 0,
+  PONNI_B200_ERR_INVALID_ARGUMENT = 1, /* bad pointer / size / layer list */
+  PONNI_B200_ERR_VALIDATION = 2,       /* layer dimension mismatch (reference aborts) */
+  PONNI_B200_ERR_UNSUPPORTED = 3,      /* layer combination no kernel supports */
+  PONNI_B200_ERR_CUDA = 4,             /* CUDA runtime error */
+  PONNI_B200_ERR_IO = 5,               /* .ponni file open/read/write/format error */
+  PONNI_B200_ERR_MISMATCH = 6,         /* .ponni fingerprint/dtype/shape mismatch */
+  PONNI_B200_ERR_DEVICE = 7            /* device-side error flag (bounded wait gave up) */
+} ponni_b200_status;
+
+/* Arithmetic type of the model (`real` in ponni::Inference). */
+typedef enum {
+  PONNI_B200_F32 = 0,  /* create_inference_model / _single_precision */
+  PONNI_B200_F64 = 1,  /* _double_precision */
+  PONNI_B200_F16 = 2,  /* _half_precision  (Kokkos::Experimental::half_t) */
+  PONNI_B200_BF16 = 3  /* _bhalf_precision (Kokkos::Experimental::bhalf_t) */
+} ponni_b200_dtype;
+
+/* Layer kinds; labels in the comments are each layer's get_label(). */
+typedef enum {
+  PONNI_B200_MATVEC = 0,             /* "Matvec"   params W[in][out] row-major       src/layers/ponni_Matvec.h */
+  PONNI_B200_BIAS = 1,               /* "Bias"     params b[n]                       src/layers/ponni_Bias.h */
+  PONNI_B200_RELU = 2,               /* "ReLU"                                       src/layers/ponni_Relu.h */
+  PONNI_B200_LEAKY_RELU = 3,         /* "LeakyReLU" scalar0 = negative_slope         src/layers/ponni_LeakyRelu.h */
+  PONNI_B200_ELU = 4,                /* "ELU"      scalar0 = alpha                   src/layers/ponni_Elu.h */
+  PONNI_B200_SELU = 5,               /* "SELU"                                       src/layers/ponni_Selu.h */
+  PONNI_B200_GELU = 6,               /* "GELU"     flags bit1 = approximate (tanh)   src/layers/ponni_Gelu.h */
+  PONNI_B200_SILU = 7,               /* "SiLU"                                       src/layers/ponni_Silu.h */
+  PONNI_B200_SIGMOID = 8,            /* "Sigmoid"                                    src/layers/ponni_Sigmoid.h */
+  PONNI_B200_TANH = 9,               /* "Tanh"                                       src/layers/ponni_Tanh.h */
+  PONNI_B200_SOFTPLUS = 10,          /* "Softplus" scalar0 = beta                    src/layers/ponni_Softplus.h */
+  PONNI_B200_HARD_SIGMOID = 11,      /* "HardSigmoid" scalar0 = alpha, scalar1 = beta src/layers/ponni_HardSigmoid.h */
+  PONNI_B200_HARD_SWISH = 12,        /* "HardSwish"                                  src/layers/ponni_HardSwish.h */
+  PONNI_B200_MISH = 13,              /* "Mish"                                       src/layers/ponni_Mish.h */
+  PONNI_B200_LAYER_NORM = 14,        /* "LayerNorm" params gamma[n] then beta[n]; scalar0 = epsilon */
+  PONNI_B200_MIN_MAX_NORM = 15,      /* "MinMaxNorm" scalar0 = out_min, scalar1 = out_max, scalar2 = epsilon */
+  PONNI_B200_SOFTMAX = 16,           /* "Softmax"                                    src/layers/ponni_Softmax.h */
+  PONNI_B200_LOG_SOFTMAX = 17,       /* "LogSoftmax"                                 src/layers/ponni_LogSoftmax.h */
+  PONNI_B200_SAVE_STATE = 18,        /* "Save_State" save_index = ISAVE              src/layers/ponni_Save_State.h */
+  PONNI_B200_BINOP_ADD = 19,         /* "Binop_Add"  save_index = ISAVE              src/layers/ponni_Binop_Add.h */
+  PONNI_B200_BINOP_CONCATENATE = 20, /* "Binop_Concatenate" flags bit2 = after; num_outputs = n1 + n2 */
+  PONNI_B200_BINOP_PROJECTION_ADD = 21 /* "Binop_Projection_Add" params W[nsave][nin] then bias[nin];
+                                          num_outputs = nin, aux = nsave */
+} ponni_b200_layer_kind;
+
+#define PONNI_B200_FLAG_TRAINABLE 0x1   /* parameters take part in the trainable vector */
+#define PONNI_B200_FLAG_APPROXIMATE 0x2 /* GELU tanh approximation */
+#define PONNI_B200_FLAG_AFTER 0x4       /* Binop_Concatenate: saved state goes after the input */
+
+typedef struct {
+  int32_t kind;        /* ponni_b200_layer_kind */
+  int32_t num_inputs;  /* layer get_num_inputs() */
+  int32_t num_outputs; /* layer get_num_outputs() */
+  int32_t save_index;  /* Save_State / Binop_* template ISAVE, else -1 */
+  int32_t aux;         /* Binop_Projection_Add: number of saved inputs; else 0 */
+  int32_t flags;       /* PONNI_B200_FLAG_* */
+  double scalar[3];    /* per-kind scalars (see kinds), rounded to the model dtype */
+  const void* params;  /* host pointer, model dtype, canonical flattened order; NULL if none */
+} ponni_b200_layer_desc;
+
+typedef struct ponni_b200_model ponni_b200_model;
+
+/* Library / device information. */
+int ponni_b200_abi_version(void);
+ponni_b200_status ponni_b200_device_count(int* count);
+
+/* Create a model for `device` (CUDA ordinal).  Parameters are copied; the
+ * descriptor array and its params may be freed afterwards.  No CUDA call is
+ * made until the first forward, so models can be built, validated and
+ * (de)serialised on a machine without a GPU. */
+ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, int num_layers,
+                                          ponni_b200_dtype dtype, int device,
+                                          ponni_b200_model** out_model);
+void ponni_b200_model_destroy(ponni_b200_model* model);
+const char* ponni_b200_last_error(const ponni_b200_model* model);
+/* Error text of the last failed ponni_b200_model_create on this thread. */
+const char* ponni_b200_create_error(void);
+
+/* Layer-by-layer size checks, reference Inference::validate. */
+ponni_b200_status ponni_b200_model_validate(ponni_b200_model* model);
+
+int ponni_b200_num_inputs(const ponni_b200_model* model);
+int ponni_b200_num_outputs(const ponni_b200_model* model);
+int ponni_b200_num_layers(const ponni_b200_model* model);
+ponni_b200_dtype ponni_b200_model_dtype(const ponni_b200_model* model);
+
+/* The model's own CUDA stream (cudaStream_t as void*); `stream` arguments of
+ * NULL below mean this stream, matching the reference's stored execution
+ * space instance. */
+void* ponni_b200_model_stream(const ponni_b200_model* model);
+ponni_b200_status ponni_b200_model_set_stream(ponni_b200_model* model, void* stream);
+ponni_b200_status ponni_b200_model_synchronize(ponni_b200_model* model);
+
+/* Device-resident forward: input [num_inputs, batch] with row stride in_ld
+ * elements, output [num_outputs, batch] with row stride out_ld, both device
+ * pointers in the model dtype.  Enqueued on `stream`; returns without a fence
+ * (reference forward_batch_parallel semantics).  batch == 0 is an error. */
+ponni_b200_status ponni_b200_forward(ponni_b200_model* model, const void* input, int64_t in_ld,
+                                     void* output, int64_t out_ld, int64_t batch, void* stream);
+
+/* Host-resident forward: copies host input to the device, runs the model and
+ * copies the result back, pipelined in column chunks over two streams.
+ * Synchronous: returns when `output` holds the result.  Pinned host memory
+ * gives full PCIe bandwidth; pageable memory works too. */
+ponni_b200_status ponni_b200_forward_host(ponni_b200_model* model, const void* input, int64_t in_ld,
+                                          void* output, int64_t out_ld, int64_t batch);
+
+/* Scratch capacity, reference semantics: grows on demand to the largest batch
+ * seen, shrinks exactly on an explicit call, 0 releases. */
+ponni_b200_status ponni_b200_reallocate_internal_state(ponni_b200_model* model, int64_t batch);
+int64_t ponni_b200_internal_state_capacity(const ponni_b200_model* model);
+/* Planned feature extents of the reference's tmp1 (which=0) / tmp2 (which=1)
+ * ping-pong buffers and of saved state `index`; 0 = not needed. */
+int ponni_b200_planned_temporary_size(const ponni_b200_model* model, int which);
+int ponni_b200_saved_state_size(const ponni_b200_model* model, int index);
+int ponni_b200_num_saved_states(const ponni_b200_model* model);
+/* Bytes of device scratch currently allocated (0: every supported program
+ * keeps its intermediate states on chip). */
+int64_t ponni_b200_scratch_bytes(const ponni_b200_model* model);
+
+/* Trainable parameters in tuple (declaration) order, model dtype, host memory. */
+int64_t ponni_b200_num_trainable_parameters(const ponni_b200_model* model);
+ponni_b200_status ponni_b200_set_trainable_parameters(ponni_b200_model* model, const void* host,
+                                                      int64_t count);
+ponni_b200_status ponni_b200_get_trainable_parameters(ponni_b200_model* model, void* host,
+                                                      int64_t count);
+
+/* "fnv1a64:%016x" of the reference's template schema text; buf >= 25 bytes. */
+ponni_b200_status ponni_b200_weight_schema_fingerprint(const ponni_b200_model* model, char* buf,
+                                                       size_t len);
+ponni_b200_status ponni_b200_model_save_weights(ponni_b200_model* model, const char* path);
+ponni_b200_status ponni_b200_model_load_weights(ponni_b200_model* model, const char* path);
+
+/* Read one F32/F64 tensor of any .ponni file as float, after the full
+ * structural, schema-fingerprint and checksum checks of the reference's
+ * PonniFile::load.  `shape` receives up to 4 extents, `rank` the rank; `out`
+ * (capacity elements) may be NULL to query the shape.  `err` receives the
+ * reason on failure. */
+ponni_b200_status ponni_b200_read_ponni_tensor(const char* path, const char* name, float* out, size_t capacity,
+                                               int64_t* shape, int* rank, char* err, size_t err_len);
+
+/* Model summary text, reference Inference::print. */
+ponni_b200_status ponni_b200_model_summary(const ponni_b200_model* model, char* buf, size_t len);
+
+/* Synthetic input generator for benchmarks and shards: fills a device
+ * [rows, cols] block (row stride ld, model-dtype elements) with a
+ * counter-based hash RNG keyed by (seed, row, col0 + col), so any GPU can
+ * regenerate any column range.  dist 0 = N(0,1), 1 = U(lo, hi). */
+ponni_b200_status ponni_b200_fill_synthetic(ponni_b200_dtype dtype, void* device_ptr, int64_t rows,
+                                            int64_t cols, int64_t ld, int64_t col0, uint64_t seed,
+                                            int dist, double lo, double hi, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PONNI_B200_H */

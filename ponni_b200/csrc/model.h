@@ -1,0 +1,63 @@
+// Internal model object behind the libponni_b200 C ABI.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/ponni_b200.h"
+#include "program.h"
+
+namespace ponni_b200 {
+
+struct Layer {
+  ponni_b200_layer_desc d;            // params pointer cleared; data lives in `params`
+  std::vector<unsigned char> params;  // canonical parameters, model dtype
+  int64_t num_params() const;         // all parameters the layer owns (elements)
+  int64_t num_trainable() const;      // reference get_num_trainable_parameters()
+};
+
+size_t dtype_bytes(ponni_b200_dtype t);
+double round_to_dtype(ponni_b200_dtype t, double v);
+double load_scalar(ponni_b200_dtype t, const unsigned char* p);
+void store_scalar(ponni_b200_dtype t, unsigned char* p, double v);
+const char* layer_label(int kind);
+bool is_dense(int kind);
+bool is_pointwise(int kind);
+bool overwrites_input(int kind);
+bool is_save(int kind);
+bool is_binop(int kind);
+
+}  // namespace ponni_b200
+
+struct ponni_b200_model {
+  ponni_b200_dtype dtype;
+  int device = 0;
+  cudaStream_t stream = nullptr;       // current stream (own or user-set)
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t copy_stream = nullptr;  // second stream of forward_host
+  std::vector<ponni_b200::Layer> layers;
+  std::string last_error;
+
+  // Execution plan (built lazily on the first forward after a change).
+  bool planned = false;
+  bool params_dirty = true;
+  ponni_b200::Program prog;
+  size_t smem_bytes = 0;
+  int grid = 0;
+  std::vector<unsigned char> packed_host;  // packed parameters (model dtype)
+  void* packed_dev = nullptr;
+  size_t packed_dev_bytes = 0;
+  int num_sms = 0;
+
+  int64_t capacity = 0;  // reference internal_state_capacity()
+  void* stage_dev = nullptr;  // forward_host staging buffers
+  size_t stage_bytes = 0;
+};
+
+// Helpers shared by the C ABI translation units.
+ponni_b200_status pb_fail(ponni_b200_model* m, ponni_b200_status s, const std::string& msg);
+ponni_b200_status pb_validate(ponni_b200_model* m);
+ponni_b200_status pb_plan(ponni_b200_model* m);
+ponni_b200_status pb_ensure_cuda(ponni_b200_model* m);
+std::string pb_schema_fingerprint(const ponni_b200_model* m);

@@ -1,0 +1,156 @@
+// Host-buffer forward pipeline and the synthetic input generator.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "model.h"
+
+using namespace ponni_b200;
+
+namespace {
+
+// Counter-based generator: a splitmix64-style finaliser over
+// (seed, row, column), so any GPU can regenerate any column of any shard and
+// the 1-GPU and N-GPU runs see identical inputs.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * UINT64_C(0xbf58476d1ce4e5b9);
+  z = (z ^ (z >> 27)) * UINT64_C(0x94d049bb133111eb);
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ double unit_open(uint64_t h) {  // (0, 1)
+  return ((double)(h >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+}
+
+template <class T> __device__ __forceinline__ T from_double(double v);
+template <> __device__ __forceinline__ float from_double<float>(double v) { return (float)v; }
+template <> __device__ __forceinline__ double from_double<double>(double v) { return v; }
+template <> __device__ __forceinline__ __half from_double<__half>(double v) { return __float2half_rn((float)v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_double<__nv_bfloat16>(double v) {
+  return __float2bfloat16_rn((float)v);
+}
+
+template <class T>
+__global__ void fill_kernel(T* out, int64_t rows, int64_t cols, int64_t ld, int64_t col0, uint64_t seed, int dist,
+                            double lo, double hi) {
+  const int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const uint64_t key = mix64(seed ^ mix64(((uint64_t)r << 40) ^ (uint64_t)(col0 + c)));
+    const double u1 = unit_open(key);
+    double v;
+    if (dist == 0) {  // Box-Muller
+      const double u2 = unit_open(mix64(key + UINT64_C(0x9e3779b97f4a7c15)));
+      v = sqrt(-2.0 * log(u1)) * cospi(2.0 * u2);
+    } else {
+      v = lo + (hi - lo) * u1;
+    }
+    out[r * ld + c] = from_double<T>(v);
+  }
+}
+
+ponni_b200_status cuda_status(ponni_b200_model* m, cudaError_t e, const char* what) {
+  return pb_fail(m, PONNI_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" {
+
+ponni_b200_status ponni_b200_fill_synthetic(ponni_b200_dtype dtype, void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                                            int64_t col0, uint64_t seed, int dist, double lo, double hi,
+                                            void* stream) {
+  if (!ptr || rows < 0 || cols < 0 || ld < cols) return PONNI_B200_ERR_INVALID_ARGUMENT;
+  if (rows == 0 || cols == 0) return PONNI_B200_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t total = rows * cols;
+  const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  switch (dtype) {
+    case PONNI_B200_F32:
+      fill_kernel<float><<<blocks, 256, 0, s>>>((float*)ptr, rows, cols, ld, col0, seed, dist, lo, hi);
+      break;
+    case PONNI_B200_F64:
+      fill_kernel<double><<<blocks, 256, 0, s>>>((double*)ptr, rows, cols, ld, col0, seed, dist, lo, hi);
+      break;
+    case PONNI_B200_F16:
+      fill_kernel<__half><<<blocks, 256, 0, s>>>((__half*)ptr, rows, cols, ld, col0, seed, dist, lo, hi);
+      break;
+    case PONNI_B200_BF16:
+      fill_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((__nv_bfloat16*)ptr, rows, cols, ld, col0, seed, dist, lo, hi);
+      break;
+    default: return PONNI_B200_ERR_INVALID_ARGUMENT;
+  }
+  return cudaGetLastError() == cudaSuccess ? PONNI_B200_OK : PONNI_B200_ERR_CUDA;
+}
+
+// Host-memory forward: column chunks alternate between two streams, each with
+// its own device staging slot, so the H2D copy of one chunk, the kernel of
+// the previous one and the D2H copy of the one before overlap (the copy
+// engines of each direction and the SMs work concurrently).
+ponni_b200_status ponni_b200_forward_host(ponni_b200_model* m, const void* input, int64_t in_ld, void* output,
+                                          int64_t out_ld, int64_t batch) {
+  if (!m) return PONNI_B200_ERR_INVALID_ARGUMENT;
+  if (batch <= 0) return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "Inference requires a nonzero batch size");
+  if (!input || !output) return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "input/output pointer is NULL");
+  if (in_ld < batch || out_ld < batch)
+    return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "row stride smaller than the batch size");
+  ponni_b200_status st = pb_plan(m);
+  if (st) return st;
+  cudaError_t e = cudaSuccess;
+  if (!m->copy_stream) {
+    e = cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_status(m, e, "cudaStreamCreate");
+  }
+  const size_t esz = dtype_bytes(m->dtype);
+  const int nin = ponni_b200_num_inputs(m), nout = ponni_b200_num_outputs(m);
+  const size_t col_bytes = (size_t)(nin + nout) * esz;
+  int64_t chunk = (int64_t)((size_t)64 << 20) / (int64_t)col_bytes;
+  chunk = std::max<int64_t>(128, chunk / 128 * 128);
+  chunk = std::min<int64_t>(chunk, (batch + 127) / 128 * 128);
+  const size_t slot_bytes = (size_t)chunk * col_bytes;
+  if (m->stage_bytes < 2 * slot_bytes) {
+    if (m->stage_dev) {
+      cudaStreamSynchronize(m->stream);
+      cudaStreamSynchronize(m->copy_stream);
+      cudaFree(m->stage_dev);
+    }
+    m->stage_dev = nullptr;
+    m->stage_bytes = 0;
+    e = cudaMalloc(&m->stage_dev, 2 * slot_bytes);
+    if (e != cudaSuccess) return cuda_status(m, e, "cudaMalloc(staging)");
+    m->stage_bytes = 2 * slot_bytes;
+  }
+  cudaStream_t streams[2] = {m->stream, m->copy_stream};
+  // Work queued by the caller on the model stream comes first.
+  cudaEvent_t ev;
+  cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  cudaEventRecord(ev, m->stream);
+  cudaStreamWaitEvent(m->copy_stream, ev, 0);
+  int idx = 0;
+  for (int64_t c0 = 0; c0 < batch; c0 += chunk, idx ^= 1) {
+    const int64_t n = std::min(chunk, batch - c0);
+    cudaStream_t s = streams[idx];
+    unsigned char* din = static_cast<unsigned char*>(m->stage_dev) + idx * slot_bytes;
+    unsigned char* dout = din + (size_t)nin * chunk * esz;
+    e = cudaMemcpy2DAsync(din, (size_t)chunk * esz, static_cast<const unsigned char*>(input) + c0 * esz,
+                          (size_t)in_ld * esz, (size_t)n * esz, nin, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) break;
+    st = ponni_b200_forward(m, din, chunk, dout, chunk, n, s);
+    if (st) break;
+    e = cudaMemcpy2DAsync(static_cast<unsigned char*>(output) + c0 * esz, (size_t)out_ld * esz, dout,
+                          (size_t)chunk * esz, (size_t)n * esz, nout, cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) break;
+  }
+  cudaError_t e1 = cudaStreamSynchronize(streams[0]);
+  cudaError_t e2 = cudaStreamSynchronize(streams[1]);
+  cudaEventDestroy(ev);
+  if (st) return st;
+  if (e == cudaSuccess) e = e1 != cudaSuccess ? e1 : e2;
+  if (e != cudaSuccess) return cuda_status(m, e, "forward_host");
+  return PONNI_B200_OK;
+}
+
+}  // extern "C"
