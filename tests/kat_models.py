@@ -1,0 +1,185 @@
+"""Known-answer networks and metrics shared by the CPU (oracle) and GPU tests.
+
+Each KAT restates a known-answer test of the reference (values derived from
+the reference test's own closed forms):
+  ones_network      unit/core/test_core_unit.cpp:200-238   -> 4, 4
+  four_block        unit/core/test_core_unit.cpp:258-325   closed form, tol 1e-4
+  softmax_mixed     unit/core/test_core_unit.cpp:328-377   -> tanh(1), 0
+  activations       unit/core/test_core_unit.cpp:627-700   values at x = -1, 0, 2
+  layer KATs        unit/core/test_core_unit.cpp:714-852   LayerNorm mean 0, MinMaxNorm -1/1,
+                                                           Projection_Add 5.1/7.2/7.8
+  readme_mlp        README.md:30-80                        -> 0.7 for all-ones input
+  perf_benchmark    unit/performance_benchmark/performance_benchmark.cpp:18-53 -> mean 15.4
+  pytorch_resnet    unit/pytorch_resnet/{generate_pytorch_resnet_data.py,test_pytorch_resnet.cpp:35-79}
+                    fixture tests/golden/pytorch_resnet.ponni, abs tol 1e-5
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+import numpy as np
+
+import ponni_b200 as pb
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def ones_network():
+    return [pb.Matvec(np.ones((2, 2))), pb.Bias(np.ones(2)), pb.LeakyRelu(2, 0.1)]
+
+
+def four_block():
+    return [pb.Matvec(np.ones((2, 5))), pb.Bias(np.full(5, 0.5)), pb.Relu(5), pb.Tanh(5),
+            pb.Matvec(np.ones((5, 3))), pb.Bias(np.full(3, -0.25)), pb.Sigmoid(3),
+            pb.Matvec(np.ones((3, 7))), pb.Bias(np.full(7, 0.1)), pb.LeakyRelu(7, 0.2),
+            pb.Matvec(np.ones((7, 2))), pb.Bias(np.full(2, -0.2)), pb.HardSwish(2)]
+
+
+def four_block_input():
+    return np.array([[1.0, -2.0, 0.0], [2.0, 0.5, 0.0]], dtype=np.float32)
+
+
+def four_block_expected(x):
+    s = x[0].astype(np.float64) + x[1]
+    h1 = np.tanh(np.maximum(0.0, s + 0.5))
+    d2 = 5.0 * h1 - 0.25
+    h2 = 1.0 / (1.0 + np.exp(-d2))
+    d3 = 3.0 * h2 + 0.1
+    h3 = np.where(d3 > 0, d3, 0.2 * d3)
+    d4 = 7.0 * h3 - 0.2
+    e = np.where(d4 <= -3.0, 0.0, np.where(d4 >= 3.0, d4, d4 * (d4 + 3.0) / 6.0))
+    return np.stack([e, e])
+
+
+def softmax_mixed():
+    return [pb.Matvec(np.ones((2, 3))), pb.Bias([0.0, 1.0, 2.0]), pb.Relu(3), pb.Softmax(3),
+            pb.Matvec(np.ones((3, 2))), pb.Bias([0.0, -1.0]), pb.Tanh(2)]
+
+
+def readme_mlp():
+    return [pb.Matvec(np.full((2, 3), 0.25)), pb.Bias(np.full(3, 0.10)), pb.Relu(3),
+            pb.Matvec(np.full((3, 1), 0.50)), pb.Bias(np.full(1, -0.20))]
+
+
+def perf_benchmark():
+    n = 8
+    return [pb.Matvec(np.ones((n, n))), pb.Bias(np.ones(n)), pb.LeakyRelu(n, 0.1),
+            pb.Matvec(np.ones((n, n))), pb.Bias(np.ones(n)), pb.LeakyRelu(n, 0.1)]
+
+
+def activation_kats():
+    """(layer, expected at x = [-1, 0, 2], tolerance) of test_core_unit.cpp:627-700."""
+    sa, ss = 1.6732632423543772848, 1.0507009873554804934
+    sm = math.exp(-3.0) + math.exp(-2.0) + 1.0
+    lse = math.log(sm) + 2.0
+    return [
+        (pb.Relu(3), [0.0, 0.0, 2.0], 1e-5),
+        (pb.LeakyRelu(3, 0.1), [-0.1, 0.0, 2.0], 1e-5),
+        (pb.Elu(3), [math.exp(-1.0) - 1.0, 0.0, 2.0], 1e-5),
+        (pb.Selu(3), [ss * sa * (math.exp(-1.0) - 1.0), 0.0, ss * 2.0], 2e-5),
+        (pb.Gelu(3), [-0.5 * (1.0 - math.erf(1.0 / math.sqrt(2.0))), 0.0, 1.0 * (1.0 + math.erf(math.sqrt(2.0)))],
+         2e-5),
+        (pb.Gelu(3, True), [-0.158808, 0.0, 1.954598], 2e-5),
+        (pb.Silu(3), [-1.0 / (1.0 + math.exp(1.0)), 0.0, 2.0 / (1.0 + math.exp(-2.0))], 2e-5),
+        (pb.Sigmoid(3), [1.0 / (1.0 + math.exp(1.0)), 0.5, 1.0 / (1.0 + math.exp(-2.0))], 2e-5),
+        (pb.Tanh(3), [math.tanh(-1.0), 0.0, math.tanh(2.0)], 1e-5),
+        (pb.Softmax(3), [math.exp(-3.0) / sm, math.exp(-2.0) / sm, 1.0 / sm], 1e-5),
+        (pb.LogSoftmax(3), [-1.0 - lse, -lse, 2.0 - lse], 1e-5),
+        (pb.Softplus(3, 2.0), [0.5 * math.log(1.0 + math.exp(-2.0)), 0.5 * math.log(2.0),
+                               0.5 * math.log(1.0 + math.exp(4.0))], 2e-5),
+        (pb.HardSigmoid(3, 0.2, 0.5), [0.3, 0.5, 0.9], 1e-5),
+        (pb.HardSwish(3), [-2.0 / 6.0, 0.0, 10.0 / 6.0], 1e-5),
+        (pb.Mish(3), [-math.tanh(math.log(1.0 + math.exp(-1.0))), 0.0,
+                      2.0 * math.tanh(math.log(1.0 + math.exp(2.0)))], 2e-5),
+    ]
+
+
+def projection_add_model():
+    """Save_State(2) -> Matvec to 3 -> Projection_Add(saved 2 -> 3); with the
+    Matvec chosen so that the main state entering the projection is
+    (1, 2, 3) for input (4, 5) -> outputs (5.1, 7.2, 7.8) as in
+    test_core_unit.cpp:799-852 (cur = (1,2,3), sav = (4,5))."""
+    # main = M^T x with x = (4, 5): choose M so that main = (1, 2, 3)
+    m = np.array([[0.25, 0.0, 0.5], [0.0, 0.4, 0.2]])
+    w = np.array([[1.0, 0.0, 0.5], [0.0, 1.0, 0.5]])
+    b = np.array([0.1, 0.2, 0.3])
+    return [pb.Save_State(2, 0), pb.Matvec(m), pb.Binop_Projection_Add(w, b, True, 0)]
+
+
+def read_tensor(path, name):
+    L = pb._abi.lib()
+    shape = (ctypes.c_int64 * 4)()
+    rank = ctypes.c_int()
+    err = ctypes.create_string_buffer(512)
+    st = L.ponni_b200_read_ponni_tensor(path.encode(), name.encode(), None, 0, shape, ctypes.byref(rank), err, 512)
+    if st != 0:
+        raise pb.PonniError(st, err.value.decode())
+    dims = [shape[i] for i in range(rank.value)]
+    out = np.empty(int(np.prod(dims)), dtype=np.float32)
+    st = L.ponni_b200_read_ponni_tensor(path.encode(), name.encode(), out.ctypes.data, out.size, shape,
+                                        ctypes.byref(rank), err, 512)
+    if st != 0:
+        raise pb.PonniError(st, err.value.decode())
+    return out.reshape(dims)
+
+
+def pytorch_resnet():
+    """Model + (input, expected output) of the reference's pytorch_resnet fixture
+    (layer list of unit/pytorch_resnet/test_pytorch_resnet.cpp:35-56)."""
+    path = os.path.join(GOLDEN, "pytorch_resnet.ponni")
+    t = lambda n: read_tensor(path, n)  # noqa: E731
+    layers = [pb.Matvec(t("fc1.weight")), pb.Bias(t("fc1.bias")), pb.Silu(5), pb.Save_State(5, 0)]
+    for i in (2, 3, 4):
+        layers += [pb.Matvec(t(f"fc{i}.weight")), pb.Bias(t(f"fc{i}.bias")), pb.Silu(5), pb.Binop_Add(5, 0)]
+        if i < 4:
+            layers.append(pb.Save_State(5, 0))
+    layers += [pb.Matvec(t("fc5.weight")), pb.Bias(t("fc5.bias"))]
+    return layers, t("test.input"), t("test.output")
+
+
+def rel_err(y, ref) -> float:
+    """max |y - ref| / max(|ref|, 1e-3 * rms(ref)), elementwise."""
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    if ref.size == 0:
+        return 0.0
+    floor = 1e-3 * np.sqrt(np.mean(ref * ref)) + 1e-300
+    return float(np.max(np.abs(y - ref) / np.maximum(np.abs(ref), floor)))
+
+
+def normwise_err(y, ref) -> float:
+    """max over output features of max|y - ref| / max|ref|."""
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    num = np.max(np.abs(y - ref), axis=1)
+    den = np.maximum(np.max(np.abs(ref), axis=1), 1e-300)
+    return float(np.max(num / den))
+
+
+def fp_parity(y, ref32, ref64, tol=1e-5):
+    """The fp32 parity gate.
+
+    * normwise per output feature: max|y - ref| / max|ref| <= tol against the
+      oracle in the model dtype (the reference's own arithmetic order), and
+    * accuracy no worse than the reference's: rms|y - exact| <=
+      2 * rms|ref - exact| + tol * 1e-3 * rms|exact|, where `exact` is the
+      same network in float64 (checked when there are >= 256 outputs, so that
+      the rms is a stable statistic).
+    The GPU contracts a*b+c into one FMA where the reference's CPU build
+    rounds twice, so elementwise agreement is limited by the cancellation in
+    each dot product; both checks are insensitive to that while still catching
+    any wrong index, weight or layer.
+    Returns (normwise error, accuracy ratio or 0 when not checked)."""
+    y, r, e = (np.asarray(a, dtype=np.float64) for a in (y, ref32, ref64))
+    nw = normwise_err(y, r)
+    if y.size < 256:
+        return nw, 0.0
+    rms = lambda a: float(np.sqrt(np.mean(a * a)))  # noqa: E731
+    ratio = rms(y - e) / (2 * rms(r - e) + tol * 1e-3 * rms(e) + 1e-300)
+    return nw, ratio
+
+
+def as_float(raw, dtype):
+    return pb.from_dtype_bytes(raw, dtype)

@@ -1,0 +1,200 @@
+"""GPU parity: libponni_b200 (through the C ABI) against the CPU oracle.
+
+Tolerances: fp32 -- normwise error per output feature <= 1e-5 against the
+oracle and accuracy no worse than the reference's (kat_models.fp_parity);
+fp64 -- normwise <= 1e-12; fp16/bf16 -- normwise <= 2e-3 against the oracle's
+per-operation-rounded half/bfloat16 arithmetic.
+"""
+import numpy as np
+import pytest
+
+import ponni_b200 as pb
+from ponni_b200 import configs
+from tests import kat_models as K
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL = {pb.F32: 1e-5, pb.F64: 1e-12}
+
+
+def to_torch(x_raw, dtype):
+    if dtype == pb.BF16:
+        return torch.from_numpy(np.ascontiguousarray(x_raw).view(np.int16)).view(torch.bfloat16)
+    return torch.from_numpy(np.ascontiguousarray(x_raw))
+
+
+def from_torch(y, dtype):
+    if dtype == pb.BF16:
+        return y.view(torch.int16).cpu().numpy().view(np.uint16)
+    return y.cpu().numpy()
+
+
+def run_device(layers, dtype, x_raw):
+    m = pb.Inference(layers, dtype=dtype)
+    y = m.forward_batch_parallel(to_torch(x_raw, dtype).cuda())
+    torch.cuda.synchronize()
+    return from_torch(y, dtype)
+
+
+def check(y_raw, ref_raw, dtype, layers=None, x_raw=None):
+    y, ref = K.as_float(y_raw, dtype), K.as_float(ref_raw, dtype)
+    assert np.all(np.isfinite(y))
+    if dtype == pb.F64:
+        nw = K.normwise_err(y, ref)
+        assert nw <= TOL[dtype], f"normwise error {nw:.3e}"
+    elif dtype == pb.F32:
+        from oracle import oracle
+        exact = oracle.forward(layers, pb.F64, K.as_float(x_raw, dtype))
+        nw, ratio = K.fp_parity(y, ref, exact, TOL[dtype])
+        assert nw <= TOL[dtype], f"normwise error {nw:.3e}"
+        assert ratio <= 1.0, f"accuracy ratio {ratio:.3f}"
+    else:
+        e = K.normwise_err(y, ref)
+        assert e <= 2e-3, f"normwise error {e:.3e}"
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+@pytest.mark.parametrize("batch", [1, 3, 129, 4099])
+def test_configs_vs_oracle(name, batch, oracle_lib):
+    cfg = configs.ALL[name](batch=batch)
+    x = configs.host_inputs(cfg, batch)
+    y = run_device(cfg.layers, cfg.dtype, x)
+    ref = oracle_lib.forward(cfg.layers, cfg.dtype, x)
+    check(y, ref, cfg.dtype, cfg.layers, x)
+
+
+def all_kinds_model(rng, n=12):
+    return [pb.Matvec(rng.normal(0, 0.4, (6, n))), pb.Bias(rng.normal(0, 0.1, n)), pb.Elu(n, 0.7),
+            pb.Save_State(n, 0), pb.Selu(n), pb.Softplus(n, 1.5), pb.Matvec(rng.normal(0, 0.3, (n, n))),
+            pb.Gelu(n), pb.Gelu(n, True), pb.Mish(n), pb.LayerNorm(rng.normal(1, 0.1, n), rng.normal(0, 0.1, n)),
+            pb.HardSigmoid(n), pb.HardSwish(n), pb.Binop_Add(n, 0), pb.Save_State(n, 1),
+            pb.Sigmoid(n), pb.Tanh(n), pb.Silu(n), pb.MinMaxNorm(n, -1.0, 2.0),
+            pb.Binop_Concatenate(n, 2 * n, True, 1), pb.Relu(2 * n), pb.LeakyRelu(2 * n, 0.05),
+            pb.Save_State(2 * n, 2), pb.Softmax(2 * n),
+            pb.Binop_Projection_Add(rng.normal(0, 0.2, (2 * n, 2 * n)), rng.normal(0, 0.1, 2 * n), True, 2),
+            pb.LogSoftmax(2 * n), pb.Matvec(rng.normal(0, 0.3, (2 * n, 5))), pb.Bias(rng.normal(0, 0.1, 5))]
+
+
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F64, pb.F16, pb.BF16])
+def test_all_layer_kinds(dtype, oracle_lib):
+    rng = np.random.default_rng(7)
+    layers = all_kinds_model(rng)
+    batch = 1000
+    x = pb.to_dtype_bytes(rng.normal(0, 1, (6, batch)), dtype)
+    y = run_device(layers, dtype, x)
+    check(y, oracle_lib.forward(layers, dtype, x), dtype, layers, x)
+
+
+def test_concatenate_before_and_barrier_first(oracle_lib):
+    rng = np.random.default_rng(3)
+    layers = [pb.Save_State(4, 0), pb.LayerNorm(4), pb.Binop_Concatenate(4, 8, False, 0), pb.Tanh(8),
+              pb.Matvec(rng.normal(0, 0.5, (8, 3)))]
+    x = rng.normal(0, 1, (4, 777)).astype(np.float32)
+    check(run_device(layers, pb.F32, x), oracle_lib.forward(layers, pb.F32, x), pb.F32, layers, x)
+
+
+def test_kats_on_gpu():
+    y = run_device(K.ones_network(), pb.F32, np.array([[1.0], [2.0]], np.float32))
+    assert np.allclose(y, 4.0)
+    x = K.four_block_input()
+    assert np.allclose(run_device(K.four_block(), pb.F32, x), K.four_block_expected(x), atol=1e-4)
+    y = run_device(K.softmax_mixed(), pb.F32, np.full((2, 2), 0.5, np.float32))
+    assert np.allclose(y[0], np.tanh(1.0), atol=1e-5) and np.allclose(y[1], 0.0, atol=1e-5)
+    y = run_device(K.readme_mlp(), pb.F32, np.ones((2, 100000), np.float32))
+    assert np.allclose(y, 0.7, atol=1e-6)
+    y = run_device(K.perf_benchmark(), pb.F32, np.full((8, 1 << 16), 0.1, np.float32))
+    assert abs(float(np.mean(y.astype(np.float64))) - 15.4) <= 1e-3
+    y = run_device(K.projection_add_model(), pb.F32, np.array([[4.0], [5.0]], np.float32))
+    assert np.allclose(y[:, 0], [5.1, 7.2, 7.8], atol=1e-5)
+    for layer, expected, tol in K.activation_kats():
+        y = run_device([layer], pb.F32, np.array([[-1.0], [0.0], [2.0]], np.float32))
+        assert np.allclose(y[:, 0], expected, atol=tol), layer.label
+    layers, xin, xout = K.pytorch_resnet()
+    y = run_device(layers, pb.F32, np.ascontiguousarray(xin))
+    assert np.max(np.abs(y - xout)) <= 1e-5
+
+
+@pytest.mark.parametrize("offset", [0, 1, 3])
+def test_strided_and_misaligned_views(offset, oracle_lib):
+    cfg = configs.cfg2(batch=1000)
+    x = configs.host_inputs(cfg, 1000)
+    ref = oracle_lib.forward(cfg.layers, cfg.dtype, x)
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    big = torch.zeros((30, 1000 + 17), dtype=torch.float32, device="cuda")
+    big[:, offset:offset + 1000] = torch.from_numpy(x).cuda()
+    out_big = torch.full((10, 1000 + 9), float("nan"), device="cuda")
+    out = out_big[:, offset:offset + 1000]
+    m.forward_batch_parallel(big[:, offset:offset + 1000], out)
+    torch.cuda.synchronize()
+    check(out.cpu().numpy(), ref, cfg.dtype, cfg.layers, x)
+    assert torch.isnan(out_big[:, :offset]).all() and torch.isnan(out_big[:, offset + 1000:]).all()
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3"])
+def test_host_pipeline(name, oracle_lib):
+    cfg = configs.ALL[name](batch=300_001)
+    x = configs.host_inputs(cfg, cfg.batch)
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    y = m.forward_batch_parallel(x)
+    check(y, oracle_lib.forward(cfg.layers, cfg.dtype, x), cfg.dtype, cfg.layers, x)
+
+
+def test_capacity_semantics():
+    # unit/core/test_core_unit.cpp:241-256
+    m = pb.create_inference_model(*K.ones_network())
+    assert m.internal_state_capacity() == 0
+    m.forward_batch_parallel(torch.ones((2, 1), device="cuda"))
+    assert m.internal_state_capacity() == 1
+    m.forward_batch_parallel(torch.ones((2, 4), device="cuda"))
+    assert m.internal_state_capacity() == 4
+    m.forward_batch_parallel(torch.ones((2, 1), device="cuda"))
+    assert m.internal_state_capacity() == 4
+    m.reallocate_internal_state(2)
+    assert m.internal_state_capacity() == 2
+    assert m.scratch_bytes() == 0
+
+
+def test_save_load_roundtrip_gpu(tmp_path):
+    m = pb.create_inference_model(*K.ones_network())
+    ok, err = m.save_weights(str(tmp_path / "w.ponni"))
+    assert ok, err
+    x = torch.tensor([[1.0], [2.0]], device="cuda")
+    assert torch.allclose(m.forward_batch_parallel(x), torch.full((2, 1), 4.0, device="cuda"))
+    m.set_trainable_parameters(np.zeros(m.get_num_trainable_parameters()))
+    assert torch.allclose(m.forward_batch_parallel(x), torch.zeros(2, 1, device="cuda"))
+    ok, err = m.load_weights(str(tmp_path / "w.ponni"))
+    assert ok, err
+    assert torch.allclose(m.forward_batch_parallel(x), torch.full((2, 1), 4.0, device="cuda"))
+
+
+def test_errors_leave_context_usable():
+    m = pb.create_inference_model(*K.ones_network())
+    with pytest.raises(pb.PonniError):
+        m.forward_batch_parallel(torch.ones((3, 4), device="cuda"))
+    with pytest.raises(pb.PonniError):
+        m.forward_batch_parallel(torch.ones((2, 0), device="cuda"))
+    assert torch.allclose(m.forward_batch_parallel(torch.tensor([[1.0], [2.0]], device="cuda")),
+                          torch.full((2, 1), 4.0, device="cuda"))
+
+
+def test_full_size_shard_consistency():
+    """At the full cfg2 size: any column slice computed alone equals the same
+    columns of the full-batch result (samples are independent), bit for bit."""
+    cfg = configs.cfg2()
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    x = torch.empty((30, cfg.batch), device="cuda")
+    pb.fill_synthetic(x, configs.INPUT_SEED)
+    y = m.forward_batch_parallel(x)
+    for c0, n in [(0, 4096), (12345, 777), (cfg.batch - 1000, 1000)]:
+        part = torch.empty((30, n), device="cuda")
+        pb.fill_synthetic(part, configs.INPUT_SEED, col0=c0)
+        assert torch.equal(part, x[:, c0:c0 + n])
+        assert torch.equal(m.forward_batch_parallel(part), y[:, c0:c0 + n])
+    assert torch.isfinite(y).all()
+    # and a strided sample of the full batch against the oracle
+    from oracle import oracle
+    cols = torch.arange(0, cfg.batch, 4099, device="cuda")
+    xs = x[:, cols].contiguous().cpu().numpy()
+    ys = y[:, cols].cpu().numpy()
+    check(ys, oracle.forward(cfg.layers, cfg.dtype, xs), cfg.dtype, cfg.layers, xs)
