@@ -1,0 +1,265 @@
+"""Benchmark of the B200 batched-inference hot path (samples/s).
+
+Default workload: the column-physics emulator MLP 30->64->64->64->10 (ReLU,
+fp32), batch 16,777,216 columns per GPU, synthetic inputs N(0,1) generated on
+each device by a counter-based RNG keyed by the global column (weak scaling:
+rank r owns columns [r*B, (r+1)*B)).  A step is one forward_batch_parallel
+over the whole batch; the 2 GB input exceeds the 126 MB L2, so no flush is
+needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfgX] [--impl ours|reference]
+
+Under torchrun (N>1) every rank runs its shard with no collective on the data
+path; timing is CUDA events on each rank's stream, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--config", default="cfg2")
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--batch", type=int, default=0, help="override per-GPU batch (default: the config's)")
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "sm_max_mhz": 1965.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+        sm = [v for v in (num(s[1]) for s in self.samples) if v is not None]
+        mx = [v for v in (num(s[2]) for s in self.samples) if v is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def cpu_reference(cfg, target_seconds=10.0, max_cols=1 << 20):
+    """Time the CPU oracle port on a bounded sample: (samples/s, cores, description, seconds)."""
+    from oracle import oracle
+    from ponni_b200 import configs
+
+    cores = os.cpu_count() or 1
+    n = 4096
+    x = configs.host_inputs(cfg, n)
+    t0 = time.perf_counter()
+    oracle.forward(cfg.layers, cfg.dtype, x, nthreads=cores)
+    dt = max(time.perf_counter() - t0, 1e-6)
+    n = int(min(max_cols, max(4096, n * target_seconds / dt / 2)))
+    x = configs.host_inputs(cfg, n)
+    t0 = time.perf_counter()
+    oracle.forward(cfg.layers, cfg.dtype, x, nthreads=cores)
+    dt = time.perf_counter() - t0
+    return n / dt, cores, f"{n} columns of {cfg.name}, one pass, {cores} OpenMP threads", dt
+
+
+def run_reference(args, cfg, rank, metric, unit, dtype_name):
+    """CPU reference arm: the oracle port of the reference's path on the host cores."""
+    if rank != 0:
+        return
+    steps, info = [], None
+    per_step = min(10.0, 120.0 / max(1, args.warmup + args.steps))
+    for i in range(args.warmup + args.steps):
+        v, cores, sample, _ = cpu_reference(cfg, target_seconds=per_step)
+        if i >= args.warmup:
+            steps.append(v)
+        info = (cores, sample)
+    value = statistics.median(steps)
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": dtype_name, "data": "synthetic",
+        "config": {"workload": cfg.name, "batch_per_gpu": cfg.batch, "sample": info[1]},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": info[0], "kind": "port", "sample": info[1]},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from ponni_b200 import configs
+
+    cfg = configs.ALL[args.config](batch=args.batch) if args.batch else configs.ALL[args.config]()
+    metric, unit = "samples/sec", "samples/s"
+    dtype_name = {0: "f32", 1: "f64", 2: "f16", 3: "bf16"}[cfg.dtype]
+    if args.impl == "reference":
+        run_reference(args, cfg, rank, metric, unit, dtype_name)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import ponni_b200 as pb
+
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    B = cfg.batch
+    nin, nout = cfg.layers[0].num_inputs, cfg.layers[-1].num_outputs
+    model = pb.Inference(cfg.layers, dtype=cfg.dtype, device=local)
+    tdt = model.torch_dtype()
+    x = torch.empty((nin, B), dtype=tdt, device=dev)
+    y = torch.empty((nout, B), dtype=tdt, device=dev)
+    pb.fill_synthetic(x, configs.INPUT_SEED, col0=rank * B, dist=cfg.input_dist, lo=cfg.lo, hi=cfg.hi)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        model.forward_batch_parallel(x, y)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    start.record(stream)
+    for _ in range(args.steps):
+        model.forward_batch_parallel(x, y)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / args.steps
+    value = world * B / (ms_step / 1e3)
+
+    # Roofline of the fused kernel (one launch per step), algorithmic FLOPs or bytes.
+    pk, pk_src = peaks()
+    launch_s = (ms / args.steps) / 1e3
+    sm_mhz = clk.get("sm_mhz") or pk.get("sm_max_mhz", 1965.0)
+    if cfg.bound == "hbm":
+        roof = {"bound": "hbm", "achieved": cfg.bytes_per_sample * B / launch_s / 1e9, "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "peak_source": f"hbm_gbs ({pk_src})"}
+    elif cfg.dtype in (pb.F32, pb.F64):
+        lanes = 128 if cfg.dtype == pb.F32 else 64
+        roof = {"bound": "compute", "achieved": cfg.flops_per_sample * B / launch_s / 1e12,
+                "peak": 148 * lanes * 2 * sm_mhz * 1e6 / 1e12, "unit": "TFLOP/s",
+                "peak_source": f"SIMT FMA peak (148 SMs x {lanes} lanes x 2) at the sampled median SM clock "
+                               f"{sm_mhz:.0f} MHz; no measured fp32 peak exists"}
+    else:
+        roof = {"bound": "tensor", "achieved": cfg.flops_per_sample * B / launch_s / 1e12,
+                "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "peak_source": f"bf16_tflops ({pk_src})"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = None
+    tpath = os.path.join(ROOT, "profiles", f"traffic_{cfg.name}.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tr = json.load(f)
+        roof["traffic"] = tr.get("bytes_per_full_launch")
+        roof["traffic_note"] = tr.get("note")
+
+    # End to end through the host-buffer C-ABI entry point (pinned host memory).
+    e2e = None
+    if args.e2e_steps > 0:
+        xh = torch.empty((nin, B), dtype=tdt, pin_memory=True)
+        yh = torch.empty((nout, B), dtype=tdt, pin_memory=True)
+        xh.copy_(x)
+        model.forward_batch_parallel(xh, yh)  # warm-up (allocates staging)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            model.forward_batch_parallel(xh, yh)
+        e2e_s = (time.perf_counter() - t0) / args.e2e_steps
+        te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        esz = x.element_size()
+        e2e = {"value": world * B / float(te.item()), "unit": unit, "h2d_bytes_per_step": world * nin * B * esz,
+               "d2h_bytes_per_step": world * nout * B * esz,
+               "path": "ponni_b200_forward_host (C ABI), pinned host buffers, chunked copy/compute overlap"}
+        del xh, yh
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample, _ = cpu_reference(cfg)
+        cpu = {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": sample}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps({
+            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": dtype_name, "data": "synthetic",
+            "config": {"workload": cfg.name, "batch_per_gpu": B, "global_batch": world * B, "nin": nin,
+                       "nout": nout, "parallelism": f"column shards x{world}, no collective",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
