@@ -141,7 +141,27 @@ ponni_b200_dtype ponni_b200_model_dtype(const ponni_b200_model* model);
  * space instance. */
 void* ponni_b200_model_stream(const ponni_b200_model* model);
 ponni_b200_status ponni_b200_model_set_stream(ponni_b200_model* model, void* stream);
+/* Waits for the model's stream; reports PONNI_B200_ERR_DEVICE if a kernel
+ * recorded a device-side error (a bounded wait that gave up). */
 ponni_b200_status ponni_b200_model_synchronize(ponni_b200_model* model);
+
+/* Arithmetic / kernel selection (no counterpart in the reference, which has
+ * one Kokkos kernel):
+ *   AUTO      -- tensor cores (tcgen05) for dense chains of fp32 (3xTF32,
+ *                fp32-level accuracy), fp16 and bf16 (fp32 accumulation)
+ *                models that fit the kernel; the tile kernel otherwise;
+ *   REFERENCE -- always the tile kernel: the reference's arithmetic order
+ *                (fp16/bf16 accumulate in the model type, per operation);
+ *   TENSOR    -- require the tensor-core kernel (forward fails otherwise). */
+typedef enum {
+  PONNI_B200_ARITH_AUTO = 0,
+  PONNI_B200_ARITH_REFERENCE = 1,
+  PONNI_B200_ARITH_TENSOR = 2
+} ponni_b200_arithmetic;
+ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* model, int arithmetic);
+/* Kernel the next forward uses (plans the model): 1 = tile kernel (SIMT),
+ * 2 = tensor-core kernel; 0 on a planning error (see last_error). */
+int ponni_b200_model_kernel(ponni_b200_model* model);
 
 /* Device-resident forward: input [num_inputs, batch] with row stride in_ld
  * elements, output [num_outputs, batch] with row stride out_ld, both device

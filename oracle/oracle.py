@@ -31,6 +31,8 @@ def lib():
         h.ponni_oracle_forward.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                            ctypes.c_int]
+        h.ponni_oracle_forward_ex.restype = ctypes.c_int
+        h.ponni_oracle_forward_ex.argtypes = h.ponni_oracle_forward.argtypes + [ctypes.c_int]
         for name in ("ponni_oracle_round_f16", "ponni_oracle_round_bf16"):
             getattr(h, name).restype = ctypes.c_float
             getattr(h, name).argtypes = [ctypes.c_float]
@@ -38,15 +40,16 @@ def lib():
     return _lib
 
 
-def forward(layers, dtype: int, x: np.ndarray, nthreads: int = 0) -> np.ndarray:
-    """x: host array in the model dtype's storage ([nin, batch]; bf16 as uint16 bits)."""
+def forward(layers, dtype: int, x: np.ndarray, nthreads: int = 0, acc32: bool = False) -> np.ndarray:
+    """x: host array in the model dtype's storage ([nin, batch]; bf16 as uint16 bits).
+    acc32: fp32-accumulation semantics (tensor-core path of 16-bit models)."""
     from ponni_b200.inference import build_descriptors
 
     descs, keep = build_descriptors(layers, dtype)
     x = np.ascontiguousarray(x)
     out = np.empty((layers[-1].num_outputs, x.shape[1]), dtype=x.dtype)
-    rc = lib().ponni_oracle_forward(ctypes.cast(descs, ctypes.c_void_p), len(layers), dtype, x.ctypes.data,
-                                    x.shape[1], out.ctypes.data, x.shape[1], x.shape[1], nthreads)
+    rc = lib().ponni_oracle_forward_ex(ctypes.cast(descs, ctypes.c_void_p), len(layers), dtype, x.ctypes.data,
+                                       x.shape[1], out.ctypes.data, x.shape[1], x.shape[1], nthreads, int(acc32))
     if rc != 0:
         raise RuntimeError(f"oracle failed ({rc})")
     del keep

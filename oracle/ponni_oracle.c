@@ -127,6 +127,7 @@ typedef struct {
 
 #define DEFINE_ORACLE(T, SUF, EXP, LOG, TANH, ERF, SQRT)                                                   \
   static inline T rnd_##SUF(int mode, T v) {                                                               \
+    if (mode < 0) return v;                                                                                \
     if (mode == PONNI_B200_F16) return (T)round_f16((float)v);                                             \
     if (mode == PONNI_B200_BF16) return (T)round_bf16((float)v);                                           \
     return v;                                                                                              \
@@ -181,9 +182,11 @@ typedef struct {
     return x;                                                                                              \
   }                                                                                                        \
   /* Run one sample: bufa holds the input; *res points at the result. */                                   \
-  static void sample_##SUF(const OLayer* L, int nl, int mode, T* bufa, T* bufb, T** saved, T** res) {       \
+  static void sample_##SUF(const OLayer* L, int nl, int smode, int acc32, T* bufa, T* bufb, T** saved,      \
+                            T** res) {                                                                     \
     T* cur = bufa;                                                                                         \
     T* nxt = bufb;                                                                                         \
+    const int mode = acc32 ? -1 : smode; /* acc32: no per-operation rounding */                            \
     for (int li = 0; li < nl; ++li) {                                                                      \
       const OLayer* y = &L[li];                                                                            \
       const int n = y->nin;                                                                                \
@@ -275,6 +278,10 @@ typedef struct {
             cur[f] = rnd_##SUF(mode, act_##SUF(y->kind, y->flags, cur[f], (T)y->s[0], (T)y->s[1]));        \
           break;                                                                                           \
       }                                                                                                    \
+      /* acc32: the state is stored (rounded to the model type) where a fused  */                          \
+      /* block ends, i.e. unless the next layer is pointwise.                  */                          \
+      if (acc32 && !(li + 1 < nl && L[li + 1].kind >= PONNI_B200_BIAS && L[li + 1].kind <= PONNI_B200_MISH)) \
+        for (int f = 0; f < y->nout; ++f) cur[f] = rnd_##SUF(smode, cur[f]);                              \
     }                                                                                                      \
     *res = cur;                                                                                            \
   }
@@ -318,13 +325,16 @@ static double round_scalar(int dtype, double v) {
 }
 
 /*
- * out[f][c] = model(in[:, c]) for c in [0, batch).  Same descriptor list and
+ * out[f][c] = model(in[:, c]) for c in [0, batch).  acc32 != 0 selects the
+ * fp32-accumulation semantics of the tensor-core path for 16-bit models:
+ * every operation in float, the state rounded to the model type where each
+ * fused block (dense layer + following pointwise layers, or a barrier) ends.  Same descriptor list and
  * dtype codes as ponni_b200_model_create; in/out are host arrays of the model
  * dtype with row strides in_ld/out_ld.  nthreads <= 0 uses all OpenMP threads.
  * Returns 0 on success.
  */
-int ponni_oracle_forward(const ponni_b200_layer_desc* layers, int n_layers, int dtype, const void* in, int64_t in_ld,
-                         void* out, int64_t out_ld, int64_t batch, int nthreads) {
+int ponni_oracle_forward_ex(const ponni_b200_layer_desc* layers, int n_layers, int dtype, const void* in,
+                            int64_t in_ld, void* out, int64_t out_ld, int64_t batch, int nthreads, int acc32) {
   if (!layers || n_layers <= 0 || batch < 0) return 1;
   for (int i = 0; i < n_layers; ++i)
     if (layers[i].save_index >= MAXSAVE) return 2;
@@ -366,7 +376,7 @@ int ponni_oracle_forward(const ponni_b200_layer_desc* layers, int n_layers, int 
       for (int64_t c = 0; c < batch; ++c) {
         for (int k = 0; k < nin; ++k) a[k] = ((const double*)in)[k * in_ld + c];
         double* r;
-        sample_d(L, n_layers, dtype, a, b, sv, &r);
+        sample_d(L, n_layers, dtype, acc32, a, b, sv, &r);
         for (int f = 0; f < nout; ++f) ((double*)out)[f * out_ld + c] = r[f];
       }
       free(a);
@@ -384,7 +394,7 @@ int ponni_oracle_forward(const ponni_b200_layer_desc* layers, int n_layers, int 
       for (int64_t c = 0; c < batch; ++c) {
         for (int k = 0; k < nin; ++k) a[k] = (float)load_elem(dtype, in, (size_t)(k * in_ld + c));
         float* r;
-        sample_f(L, n_layers, dtype, a, b, sv, &r);
+        sample_f(L, n_layers, dtype, acc32, a, b, sv, &r);
         for (int f = 0; f < nout; ++f) store_elem(dtype, out, (size_t)(f * out_ld + c), r[f]);
       }
       free(a);
@@ -395,4 +405,9 @@ int ponni_oracle_forward(const ponni_b200_layer_desc* layers, int n_layers, int 
   for (int i = 0; i < n_layers; ++i) free(L[i].pd);
   free(L);
   return 0;
+}
+
+int ponni_oracle_forward(const ponni_b200_layer_desc* layers, int n_layers, int dtype, const void* in, int64_t in_ld,
+                         void* out, int64_t out_ld, int64_t batch, int nthreads) {
+  return ponni_oracle_forward_ex(layers, n_layers, dtype, in, in_ld, out, out_ld, batch, nthreads, 0);
 }

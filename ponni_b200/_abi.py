@@ -26,6 +26,9 @@ F32, F64, F16, BF16 = 0, 1, 2, 3
  HARD_SWISH, MISH, LAYER_NORM, MIN_MAX_NORM, SOFTMAX, LOG_SOFTMAX, SAVE_STATE, BINOP_ADD,
  BINOP_CONCATENATE, BINOP_PROJECTION_ADD) = range(22)
 
+ARITH_AUTO, ARITH_REFERENCE, ARITH_TENSOR = 0, 1, 2
+KERNEL_TILE, KERNEL_TENSOR = 1, 2
+
 FLAG_TRAINABLE = 0x1
 FLAG_APPROXIMATE = 0x2
 FLAG_AFTER = 0x4
@@ -64,6 +67,8 @@ SIGNATURES = {
     "ponni_b200_model_stream": (_P, [_P]),
     "ponni_b200_model_set_stream": (_STATUS, [_P, _P]),
     "ponni_b200_model_synchronize": (_STATUS, [_P]),
+    "ponni_b200_model_set_arithmetic": (_STATUS, [_P, _I]),
+    "ponni_b200_model_kernel": (_I, [_P]),
     "ponni_b200_forward": (_STATUS, [_P, _P, _I64, _P, _I64, _I64, _P]),
     "ponni_b200_forward_host": (_STATUS, [_P, _P, _I64, _P, _I64, _I64]),
     "ponni_b200_reallocate_internal_state": (_STATUS, [_P, _I64]),

@@ -17,6 +17,8 @@
 #include <sstream>
 
 #include "model.h"
+#include "tc_kernel.h"
+#include "tc_plan.h"
 #include "tile_kernel.h"
 
 using namespace ponni_b200;
@@ -484,6 +486,36 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
   if (e != cudaSuccess) return cuda_fail(m, e, "parameter upload");
   m->packed_host.swap(packed);
+
+  // Tensor-core dense-chain kernel, when allowed and eligible.
+  m->kernel = 1;
+  m->tc_why.clear();
+  if (m->arithmetic != PONNI_B200_ARITH_REFERENCE) {
+    std::vector<unsigned char> image;
+    if (tc_plan(m, m->tcp, image, m->tc_why)) {
+      if (image.size() > m->tc_image_bytes) {
+        if (m->tc_image_dev) cudaFree(m->tc_image_dev);
+        m->tc_image_dev = nullptr;
+        m->tc_image_bytes = 0;
+        e = cudaMalloc(&m->tc_image_dev, image.size());
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(tensor-core parameters)");
+        m->tc_image_bytes = image.size();
+      }
+      if (!m->err_dev) {
+        e = cudaMalloc(&m->err_dev, sizeof(int));
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(error word)");
+        e = cudaMemsetAsync(m->err_dev, 0, sizeof(int), m->stream);
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMemset(error word)");
+      }
+      e = cudaMemcpyAsync(m->tc_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+      if (e != cudaSuccess) return cuda_fail(m, e, "tensor-core parameter upload");
+      m->tc_grid = m->num_sms;  // one persistent CTA per SM
+      m->kernel = 2;
+    } else if (m->arithmetic == PONNI_B200_ARITH_TENSOR) {
+      return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED, "tensor-core kernel unavailable: " + m->tc_why);
+    }
+  }
   m->planned = true;
   m->params_dirty = false;
   return PONNI_B200_OK;
@@ -602,12 +634,14 @@ ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, i
 
 void ponni_b200_model_destroy(ponni_b200_model* m) {
   if (!m) return;
-  if (m->own_stream || m->packed_dev || m->stage_dev) {
+  if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
     if (m->packed_dev) cudaFree(m->packed_dev);
     if (m->stage_dev) cudaFree(m->stage_dev);
+    if (m->tc_image_dev) cudaFree(m->tc_image_dev);
+    if (m->err_dev) cudaFree(m->err_dev);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
     if (m->own_stream) cudaStreamDestroy(m->own_stream);
   }
@@ -647,7 +681,17 @@ ponni_b200_status ponni_b200_model_synchronize(ponni_b200_model* m) {
   ponni_b200_status st = pb_ensure_cuda(m);
   if (st) return st;
   cudaError_t e = cudaStreamSynchronize(m->stream);
-  return e == cudaSuccess ? PONNI_B200_OK : cuda_fail(m, e, "cudaStreamSynchronize");
+  if (e != cudaSuccess) return cuda_fail(m, e, "cudaStreamSynchronize");
+  if (m->err_dev) {
+    int flag = 0;
+    e = cudaMemcpy(&flag, m->err_dev, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(m, e, "error word read");
+    if (flag) {
+      cudaMemset(m->err_dev, 0, sizeof(int));
+      return pb_fail(m, PONNI_B200_ERR_DEVICE, "a tensor-core wait exceeded its bound; results are invalid");
+    }
+  }
+  return PONNI_B200_OK;
 }
 
 ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int64_t in_ld, void* output,
@@ -663,10 +707,17 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
   // Reference ensure_internal_state_capacity (src/ponni_Inference.h:197-199).
   if (batch > m->capacity) m->capacity = batch;
   cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
-  const int64_t ntiles = (batch + m->prog.bt - 1) / m->prog.bt;
-  const int grid = (int)std::min<int64_t>(m->grid, ntiles);
-  cudaError_t e = launch_tile_forward((int)m->dtype, m->prog, m->packed_dev, input, in_ld, output, out_ld, batch,
-                                      grid, m->smem_bytes, s);
+  cudaError_t e;
+  if (m->kernel == 2) {
+    const int64_t ntiles = (batch + kTcM - 1) / kTcM;
+    const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
+    e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
+  } else {
+    const int64_t ntiles = (batch + m->prog.bt - 1) / m->prog.bt;
+    const int grid = (int)std::min<int64_t>(m->grid, ntiles);
+    e = launch_tile_forward((int)m->dtype, m->prog, m->packed_dev, input, in_ld, output, out_ld, batch, grid,
+                            m->smem_bytes, s);
+  }
   if (e != cudaSuccess) return cuda_fail(m, e, "tile kernel launch");
   return PONNI_B200_OK;
 }
@@ -703,6 +754,21 @@ int ponni_b200_saved_state_size(const ponni_b200_model* m, int index) {
     for (const auto& L : m->layers)
       if (is_save(L.d.kind) && L.d.save_index == index) n = std::max(n, L.d.num_outputs);
   return n;
+}
+
+ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* m, int arithmetic) {
+  if (!m || arithmetic < PONNI_B200_ARITH_AUTO || arithmetic > PONNI_B200_ARITH_TENSOR)
+    return PONNI_B200_ERR_INVALID_ARGUMENT;
+  if (m->arithmetic != arithmetic) {
+    m->arithmetic = arithmetic;
+    m->params_dirty = true;  // re-plan on the next forward
+  }
+  return PONNI_B200_OK;
+}
+
+int ponni_b200_model_kernel(ponni_b200_model* m) {
+  if (!m) return 0;
+  return pb_plan(m) == PONNI_B200_OK ? m->kernel : 0;
 }
 
 int64_t ponni_b200_scratch_bytes(const ponni_b200_model* m) {

@@ -7,6 +7,7 @@
 
 #include "../../include/ponni_b200.h"
 #include "program.h"
+#include "tc_program.h"
 
 namespace ponni_b200 {
 
@@ -49,6 +50,16 @@ struct ponni_b200_model {
   void* packed_dev = nullptr;
   size_t packed_dev_bytes = 0;
   int num_sms = 0;
+
+  // Tensor-core dense-chain kernel (planned when eligible and allowed).
+  int arithmetic = PONNI_B200_ARITH_REFERENCE;  // ponni_b200_arithmetic requested
+  int kernel = 0;       // 1 tile (SIMT) kernel, 2 tensor-core kernel; 0 = not planned yet
+  ponni_b200::TcProgram tcp;
+  void* tc_image_dev = nullptr;
+  size_t tc_image_bytes = 0;
+  int tc_grid = 0;
+  int* err_dev = nullptr;  // device error word (bounded waits that gave up)
+  std::string tc_why;      // why the tensor-core kernel is not used
 
   int64_t capacity = 0;  // reference internal_state_capacity()
   void* stage_dev = nullptr;  // forward_host staging buffers

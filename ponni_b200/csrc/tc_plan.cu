@@ -1,0 +1,173 @@
+// Host side of the tensor-core dense-chain kernel: eligibility, operand
+// packing (the swizzled K-major weight images) and the TcProgram.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "model.h"
+#include "tc_plan.h"
+
+namespace ponni_b200 {
+namespace {
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+bool tc_activation(int k) {
+  return k == PONNI_B200_RELU || k == PONNI_B200_LEAKY_RELU || k == PONNI_B200_SILU || k == PONNI_B200_GELU ||
+         k == PONNI_B200_TANH || k == PONNI_B200_SIGMOID;
+}
+
+// cvt.rna.tf32.f32 on the host: round the 13 dropped mantissa bits to
+// nearest, ties away from zero.
+float tf32_rna(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x;  // inf / nan unchanged
+  u = (u + 0x1000u) & ~0x1fffu;
+  float r;
+  memcpy(&r, &u, 4);
+  return r;
+}
+
+// Place one element into a K-major SW128 operand with `rows` rows.
+void put_kmajor(std::vector<unsigned char>& img, size_t base, int rows, int n, int k, int esz, const void* val) {
+  const int kper = 128 / esz;
+  const int kb = k / kper;
+  const int wb = (k % kper) * esz;
+  const int chunk = wb / 16;
+  const size_t off = base + (size_t)kb * rows * 128 + (size_t)n * 128 + (size_t)((chunk ^ (n & 7)) * 16) + (wb % 16);
+  memcpy(img.data() + off, val, esz);
+}
+
+uint32_t make_idesc(int dtype, int n_pad, bool a_mn_major) {
+  const uint32_t fmt = dtype == PONNI_B200_F32 ? 2u : (dtype == PONNI_B200_BF16 ? 1u : 0u);
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((uint32_t)(n_pad >> 3) << 17) |
+         ((uint32_t)(kTcM >> 4) << 24);
+}
+
+}  // namespace
+
+bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>& image, std::string& why) {
+  memset(&p, 0, sizeof(p));
+  image.clear();
+  const ponni_b200_dtype dt = m->dtype;
+  if (dt != PONNI_B200_F32 && dt != PONNI_B200_F16 && dt != PONNI_B200_BF16) {
+    why = "tensor-core path supports fp32 (3xTF32), fp16 and bf16 models";
+    return false;
+  }
+  const int esz = dt == PONNI_B200_F32 ? 4 : 2;
+  const int kstep = 32 / esz;
+  const size_t msz = dtype_bytes(dt);
+  // Walk [Matvec][Bias]?[activation]? blocks.
+  struct Blk { const Layer* mv; const Layer* bias; const Layer* act; };
+  std::vector<Blk> blocks;
+  const auto& Ls = m->layers;
+  for (size_t i = 0; i < Ls.size();) {
+    if (Ls[i].d.kind != PONNI_B200_MATVEC) {
+      why = std::string("layer ") + layer_label(Ls[i].d.kind) + " is outside a dense chain";
+      return false;
+    }
+    Blk b{&Ls[i], nullptr, nullptr};
+    ++i;
+    if (i < Ls.size() && Ls[i].d.kind == PONNI_B200_BIAS) b.bias = &Ls[i++];
+    if (i < Ls.size() && tc_activation(Ls[i].d.kind)) b.act = &Ls[i++];
+    blocks.push_back(b);
+  }
+  if (blocks.empty() || blocks.size() > (size_t)kTcMaxLayers) {
+    why = "dense chain length out of range";
+    return false;
+  }
+  p.n_layers = (int)blocks.size();
+  p.dtype = (int)dt;
+  p.esz = esz;
+  p.nin = blocks.front().mv->d.num_inputs;
+  p.nout = blocks.back().mv->d.num_outputs;
+  int max_npad = 0, max_w32 = 0;
+  for (size_t l = 0; l < blocks.size(); ++l) {
+    const auto& d = blocks[l].mv->d;
+    if (d.num_inputs > 256 || d.num_outputs > 256) {
+      why = "layer wider than 256";
+      return false;
+    }
+    TcLayer& L = p.layers[l];
+    L.nin = d.num_inputs;
+    L.nout = d.num_outputs;
+    L.k_pad = (int)round_up(d.num_inputs, kstep);
+    L.n_pad = (int)round_up(d.num_outputs, 16);
+    L.act = blocks[l].act ? blocks[l].act->d.kind : EPI_NONE;
+    L.act_flags = blocks[l].act ? blocks[l].act->d.flags : 0;
+    L.s0 = blocks[l].act ? (float)blocks[l].act->d.scalar[0] : 0.f;
+    L.s1 = blocks[l].act ? (float)blocks[l].act->d.scalar[1] : 0.f;
+    L.has_bias = blocks[l].bias ? 1 : 0;
+    L.idesc = make_idesc(dt, L.n_pad, false);
+    L.idesc_mn = make_idesc(dt, L.n_pad, true);
+    max_npad = std::max(max_npad, L.n_pad);
+    if (l + 1 < blocks.size()) max_w32 = std::max(max_w32, (int)round_up(L.n_pad, 32));
+  }
+  // Image: biases first (float, padded to 32 columns), then weights at
+  // 1024-byte aligned offsets.
+  size_t off = 0;
+  for (int l = 0; l < p.n_layers; ++l) {
+    TcLayer& L = p.layers[l];
+    L.bias_off = (uint32_t)off;
+    off += round_up(round_up(L.n_pad, 32) * 4, 16);
+  }
+  off = round_up(off, 1024);
+  for (int l = 0; l < p.n_layers; ++l) {
+    TcLayer& L = p.layers[l];
+    const int nkb = (int)((L.k_pad * esz + 127) / 128);
+    const size_t bytes = (size_t)nkb * L.n_pad * 128;
+    L.w_hi_off = (uint32_t)off;
+    off += round_up(bytes, 1024);
+    if (esz == 4) {
+      L.w_lo_off = (uint32_t)off;
+      off += round_up(bytes, 1024);
+    } else {
+      L.w_lo_off = L.w_hi_off;
+    }
+  }
+  p.image_bytes = (uint32_t)round_up(off, 1024);
+  image.assign(p.image_bytes, 0);
+  for (int l = 0; l < p.n_layers; ++l) {
+    const TcLayer& L = p.layers[l];
+    const Layer& mv = *blocks[l].mv;
+    if (blocks[l].bias) {
+      float* b = reinterpret_cast<float*>(image.data() + L.bias_off);
+      for (int f = 0; f < L.nout; ++f) b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
+    }
+    for (int k = 0; k < L.nin; ++k) {
+      for (int n = 0; n < L.nout; ++n) {
+        const unsigned char* src = mv.params.data() + ((size_t)k * L.nout + n) * msz;  // W[k][n]
+        if (esz == 4) {
+          float w;
+          memcpy(&w, src, 4);
+          const float hi = tf32_rna(w), lo = tf32_rna(w - hi);
+          put_kmajor(image, L.w_hi_off, L.n_pad, n, k, 4, &hi);
+          put_kmajor(image, L.w_lo_off, L.n_pad, n, k, 4, &lo);
+        } else {
+          put_kmajor(image, L.w_hi_off, L.n_pad, n, k, 2, src);
+        }
+      }
+    }
+  }
+  const int k0 = p.layers[0].k_pad;
+  p.stage_bytes = (uint32_t)(k0 / 8) * (uint32_t)esz * 1024;
+  const uint32_t a_kmajor = (uint32_t)((max_w32 * esz + 127) / 128) * kTcM * 128;
+  const uint32_t a_mn = esz == 4 ? (uint32_t)(k0 / 8) * 4096 : 0;
+  p.a_bytes = std::max(std::max(a_kmajor, a_mn), 1024u);
+  uint32_t cols = 32;
+  while ((int)cols < max_npad) cols <<= 1;
+  p.tmem_cols = cols;
+  p.smem_bytes = 1024 + p.image_bytes + p.a_bytes * (esz == 4 ? 2 : 1) + 2 * p.stage_bytes + 64;
+  if (p.smem_bytes > 227 * 1024) {
+    why = "weights and operand tiles exceed shared memory";
+    return false;
+  }
+  return true;
+}
+
+}  // namespace ponni_b200

@@ -1,0 +1,53 @@
+// Program of the tensor-core (tcgen05) dense-chain kernel, shared by the host
+// packer (tc_plan.cu) and the kernel (tc_kernel.cu).
+//
+// A dense chain is Matvec [Bias] [activation] repeated, PONNI's fused dense
+// blocks (reference src/ponni_Inference.h:416-444) without barriers.  Each
+// layer is one UMMA chain D[M=128 batch rows, N=features] +=
+// A[M, K=in features] * B[N, K]^T with the fp32 accumulator in TMEM.
+//
+// Shared-memory operand layouts (128-byte swizzle, "SW128"):
+//  * K-major (weights B, and the activations A of layers >= 1): rows of 128 B
+//    holding 128/esz consecutive K elements; 8-row groups 1024 B apart (SBO);
+//    K beyond one row lives in the next "K block" of rows x 128 B; 16-byte
+//    chunk c of row r is stored at chunk position c ^ (r % 8).
+//  * MN-major (the activations A of layer 0, copied straight from the
+//    batch-contiguous input): atoms of 8 k-rows x 128 B (128/esz batch
+//    columns); atoms along M 1024 B apart (LBO), along K esz*1024 B apart (SBO).
+#pragma once
+#include <stdint.h>
+
+namespace ponni_b200 {
+
+constexpr int kTcMaxLayers = 16;
+constexpr int kTcThreads = 128;  // 4 warps: one TMEM lane quarter each
+constexpr int kTcM = 128;        // batch rows per tile (UMMA M)
+
+struct TcLayer {
+  int32_t nin, nout;     // true widths
+  int32_t k_pad;         // K rounded to the UMMA K step (8 tf32 / 16 f16/bf16)
+  int32_t n_pad;         // N rounded to 16 (UMMA N for M=128)
+  int32_t act, act_flags;
+  float s0, s1;          // activation scalars
+  int32_t has_bias;
+  uint32_t bias_off;     // byte offset of float bias[n_pad] in the staged image
+  uint32_t w_hi_off;     // byte offset of the K-major B operand (hi part for 3xTF32)
+  uint32_t w_lo_off;     // 3xTF32 low part (unused otherwise)
+  uint32_t idesc;        // UMMA instruction descriptor (A K-major)
+  uint32_t idesc_mn;     // same with A MN-major (layer 0)
+};
+
+struct TcProgram {
+  int32_t n_layers;
+  int32_t dtype;         // ponni_b200_dtype (0 f32 -> 3xTF32, 2 f16, 3 bf16)
+  int32_t nin, nout;
+  int32_t esz;           // operand element size (4 tf32, 2 f16/bf16)
+  uint32_t image_bytes;  // staged parameter image (multiple of 16)
+  uint32_t a_bytes;      // one activation operand buffer
+  uint32_t stage_bytes;  // one input staging buffer (MN-major, k_pad0 rows)
+  uint32_t tmem_cols;    // power of two >= 32 and >= every n_pad
+  uint32_t smem_bytes;   // total dynamic shared memory requested (incl. 1 KB alignment slack)
+  TcLayer layers[kTcMaxLayers];
+};
+
+}  // namespace ponni_b200

@@ -110,7 +110,7 @@ def build_descriptors(layers, code: int):
 class Inference:
     """A model on one GPU; mirrors ponni::Inference (src/ponni_Inference.h:13-740)."""
 
-    def __init__(self, layers, dtype=_abi.F32, device: int = 0):
+    def __init__(self, layers, dtype=_abi.F32, device: int = 0, arithmetic: int | None = None):
         self.layers = list(layers)
         self.dtype = dtype_code(dtype)
         self.device = int(device)
@@ -119,6 +119,8 @@ class Inference:
         _check(_abi.lib().ponni_b200_model_create(descs, len(self.layers), self.dtype, self.device,
                                                   ctypes.byref(ptr)))
         self._m = ptr
+        if arithmetic is not None:
+            self.set_arithmetic(arithmetic)
 
     def __del__(self):
         m = getattr(self, "_m", None)
@@ -232,6 +234,19 @@ class Inference:
             raise _abi.PonniError(1, "Inference requires a nonzero batch size")
         _check(_abi.lib().ponni_b200_forward_host(self._m, in_ptr, in_ld, out_ptr, out_ld, batch), self._m)
         return output
+
+    def set_arithmetic(self, mode: int) -> None:
+        """ARITH_AUTO (tensor cores where supported), ARITH_REFERENCE (tile
+        kernel, the reference's operation order), ARITH_TENSOR (require the
+        tensor-core kernel)."""
+        _check(_abi.lib().ponni_b200_model_set_arithmetic(self._m, int(mode)), self._m)
+
+    def kernel(self) -> int:
+        """Kernel the next forward uses: 1 tile kernel, 2 tensor-core kernel (plans the model)."""
+        k = int(_abi.lib().ponni_b200_model_kernel(self._m))
+        if k == 0:
+            raise _abi.PonniError(3, _abi.lib().ponni_b200_last_error(self._m).decode())
+        return k
 
     def synchronize(self) -> None:
         _check(_abi.lib().ponni_b200_model_synchronize(self._m), self._m)

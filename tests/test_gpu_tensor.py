@@ -1,0 +1,104 @@
+"""GPU parity of the tensor-core (tcgen05) dense-chain kernel.
+
+fp32 models run 3xTF32 and must pass the fp32 gate of the tile kernel
+(normwise <= 1e-5 against the oracle, accuracy no worse than the reference's);
+fp16/bf16 models accumulate in fp32 and are checked against the oracle's
+fp32-accumulation mode (normwise <= 2e-3) and must be at least as accurate
+as the reference's per-operation-rounded arithmetic.
+"""
+import numpy as np
+import pytest
+
+import ponni_b200 as pb
+from ponni_b200 import configs
+from tests import kat_models as K
+from tests.test_gpu_parity import check, from_torch, to_torch
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def run_tc(layers, dtype, x_raw):
+    m = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR
+    y = m.forward_batch_parallel(to_torch(x_raw, dtype).cuda())
+    m.synchronize()
+    torch.cuda.synchronize()
+    return from_torch(y, dtype)
+
+
+def check_acc32(y_raw, layers, dtype, x_raw, oracle_lib):
+    y = K.as_float(y_raw, dtype)
+    assert np.all(np.isfinite(y))
+    a32 = K.as_float(oracle_lib.forward(layers, dtype, x_raw, acc32=True), dtype)
+    ref = K.as_float(oracle_lib.forward(layers, dtype, x_raw), dtype)
+    exact = oracle_lib.forward(layers, pb.F64, K.as_float(x_raw, dtype))
+    nw = K.normwise_err(y, a32)
+    assert nw <= 2e-3, f"normwise vs fp32-accumulation oracle {nw:.3e}"
+    assert K.normwise_err(y, exact) <= K.normwise_err(ref, exact) + 2e-3
+
+
+def test_tc_smallest_case(oracle_lib):
+    layers = [pb.Matvec(np.eye(8, 16)), pb.Bias(np.zeros(16)), pb.Matvec(np.ones((16, 4)) * 0.5)]
+    x = np.arange(8 * 5, dtype=np.float32).reshape(8, 5) / 10
+    y = run_tc(layers, pb.F32, x)
+    check(y, oracle_lib.forward(layers, pb.F32, x), pb.F32, layers, x)
+
+
+@pytest.mark.parametrize("batch", [1, 127, 128, 129, 5000])
+def test_tc_cfg2(batch, oracle_lib):
+    cfg = configs.cfg2(batch=batch)
+    x = configs.host_inputs(cfg, batch)
+    y = run_tc(cfg.layers, cfg.dtype, x)
+    check(y, oracle_lib.forward(cfg.layers, cfg.dtype, x), cfg.dtype, cfg.layers, x)
+
+
+@pytest.mark.parametrize("dtype", [pb.F16, pb.BF16])
+@pytest.mark.parametrize("batch", [3, 1000])
+def test_tc_cfg3_16bit(dtype, batch, oracle_lib):
+    cfg = configs.cfg3(batch=batch)
+    x = pb.to_dtype_bytes(K.as_float(configs.host_inputs(cfg, batch), cfg.dtype), dtype)
+    y = run_tc(cfg.layers, dtype, x)
+    check_acc32(y, cfg.layers, dtype, x, oracle_lib)
+
+
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F16, pb.BF16])
+def test_tc_odd_widths_all_activations(dtype, oracle_lib):
+    rng = np.random.default_rng(11)
+    dims = [3, 17, 40, 130, 9, 256, 5]
+    acts = [pb.Relu, pb.Silu, pb.Gelu, pb.Tanh, pb.Sigmoid, lambda n: pb.LeakyRelu(n, 0.2)]
+    layers = []
+    for i in range(len(dims) - 1):
+        layers.append(pb.Matvec(rng.normal(0, 1.0 / np.sqrt(dims[i]), (dims[i], dims[i + 1]))))
+        if i % 2 == 0:
+            layers.append(pb.Bias(rng.normal(0, 0.1, dims[i + 1])))
+        if i < len(dims) - 2:
+            layers.append(acts[i % len(acts)](dims[i + 1]))
+    x = pb.to_dtype_bytes(rng.normal(0, 1, (3, 777)), dtype)
+    y = run_tc(layers, dtype, x)
+    if dtype == pb.F32:
+        check(y, oracle_lib.forward(layers, dtype, x), dtype, layers, x)
+    else:
+        check_acc32(y, layers, dtype, x, oracle_lib)
+
+
+def test_tc_strided_misaligned(oracle_lib):
+    cfg = configs.cfg2(batch=1000)
+    x = configs.host_inputs(cfg, 1000)
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    big = torch.zeros((30, 1000 + 17), dtype=torch.float32, device="cuda")
+    big[:, 3:1003] = torch.from_numpy(x).cuda()
+    out_big = torch.full((10, 1009), float("nan"), device="cuda")
+    m.forward_batch_parallel(big[:, 3:1003], out_big[:, 1:1001])
+    m.synchronize()
+    check(out_big[:, 1:1001].cpu().numpy(), oracle_lib.forward(cfg.layers, cfg.dtype, x), cfg.dtype, cfg.layers, x)
+    assert torch.isnan(out_big[:, 0]).all() and torch.isnan(out_big[:, 1001:]).all()
+
+
+def test_tc_ineligible_falls_back_or_errors():
+    cfg = configs.cfg4(batch=10)  # LayerNorm / residual: tile kernel
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=pb._abi.ARITH_AUTO)
+    assert m.kernel() == pb._abi.KERNEL_TILE
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    with pytest.raises(pb.PonniError):
+        m.kernel()
