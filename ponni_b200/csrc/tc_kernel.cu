@@ -2,8 +2,10 @@
 //
 // One persistent CTA per SM, 4 warps.  Per batch tile of 128 columns:
 //   input  : cp.async (16 B, zero-filled tail) of the batch-contiguous input
-//            rows straight into an MN-major SW128 operand (prefetched one
-//            tile ahead into a second staging buffer);
+//            rows straight into an MN-major SW128 tile (prefetched one tile
+//            ahead into a second staging buffer); 16-bit models use it as the
+//            layer-0 operand directly, fp32 models split it into tf32 hi/lo
+//            K-major operands (the tf32 MMA reads K-major operands here);
 //   layer l: thread 0 issues the UMMA chain D[128 x N] = A[128 x K] B[N x K]^T
 //            (tcgen05.mma, fp32 accumulator in TMEM) and commits it to an
 //            mbarrier; all threads wait (bounded), then each warp reads its 32
@@ -343,24 +345,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     cp_async_commit();
     cp_async_wait_1();
     __syncthreads();
-    uint32_t a0_hi = stage, a0_lo = 0;
     if constexpr (TF32) {
-      // Split the fp32 input tile into tf32 hi/lo operands (same MN-major layout).
+      // Split the fp32 input tile into tf32 hi/lo operands and transpose it
+      // to K-major (the MN-major operand form is used for 16-bit inputs
+      // only): thread m builds row m from column m of the staged tile.
       const int k0 = p.layers[0].k_pad;
-      const int n16 = k0 / 8 * 4096 / 16;
-      const uint4* src = reinterpret_cast<const uint4*>(base_ptr + (stage - base));
-      for (int i = tid; i < n16; i += kTcThreads) {
-        uint4 x = src[i];
-        uint32_t h0 = to_tf32(__uint_as_float(x.x)), h1 = to_tf32(__uint_as_float(x.y));
-        uint32_t h2 = to_tf32(__uint_as_float(x.z)), h3 = to_tf32(__uint_as_float(x.w));
-        st_shared_v4(s_ahi + i * 16, h0, h1, h2, h3);
-        st_shared_v4(s_alo + i * 16, to_tf32(__uint_as_float(x.x) - __uint_as_float(h0)),
-                     to_tf32(__uint_as_float(x.y) - __uint_as_float(h1)),
-                     to_tf32(__uint_as_float(x.z) - __uint_as_float(h2)),
-                     to_tf32(__uint_as_float(x.w) - __uint_as_float(h3)));
+      const unsigned char* st = base_ptr + (stage - base);
+      const uint32_t mo = (uint32_t)(tid >> 5) * 1024 + (uint32_t)(tid & 3) * 4;
+      const uint32_t mc = (uint32_t)(tid & 31) >> 2;
+      for (int f = 0; f < k0; f += 4) {
+        uint32_t h[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t fe = (uint32_t)(f + e);
+          const float x = *reinterpret_cast<const float*>(st + (fe >> 3) * 4096 + mo + (fe & 7) * 128 +
+                                                          ((mc ^ (fe & 7)) << 4));
+          h[e] = to_tf32(x);
+          lo[e] = to_tf32(x - __uint_as_float(h[e]));
+        }
+        const uint32_t off = kmajor_chunk(tid, (uint32_t)f * 4);
+        st_shared_v4(s_ahi + off, h[0], h[1], h[2], h[3]);
+        st_shared_v4(s_alo + off, lo[0], lo[1], lo[2], lo[3]);
       }
-      a0_hi = s_ahi;
-      a0_lo = s_alo;
     }
     for (int l = 0; l < p.n_layers; ++l) {
       const TcLayer& L = p.layers[l];
@@ -377,11 +383,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t b_off = kb * b_block + ks * 32;
           uint64_t ad_hi, ad_lo;
           uint32_t idesc;
-          if (l == 0) {
-            // MN-major: one K step = 32 bytes of K for 128 rows = 4096 bytes.
-            const uint32_t sbo = (uint32_t)p.esz * 1024;
-            ad_hi = smem_desc(a0_hi + (uint32_t)s * 4096, 1024, sbo);
-            ad_lo = smem_desc(a0_lo + (uint32_t)s * 4096, 1024, sbo);
+          if (!TF32 && l == 0) {
+            // 16-bit layer 0 reads the staged input tile as an MN-major
+            // operand: one K step = 32 bytes of K for 128 rows = 4096 bytes.
+            ad_hi = smem_desc(stage + (uint32_t)s * 4096, 1024, (uint32_t)p.esz * 1024);
+            ad_lo = ad_hi;
             idesc = L.idesc_mn;
           } else {
             const uint32_t a_off = kb * (kTcM * 128) + ks * 32;

@@ -155,10 +155,10 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
     }
   }
   const int k0 = p.layers[0].k_pad;
+  if (esz == 4) max_w32 = std::max(max_w32, (int)round_up(k0, 32));  // layer 0 is K-major for tf32
   p.stage_bytes = (uint32_t)(k0 / 8) * (uint32_t)esz * 1024;
   const uint32_t a_kmajor = (uint32_t)((max_w32 * esz + 127) / 128) * kTcM * 128;
-  const uint32_t a_mn = esz == 4 ? (uint32_t)(k0 / 8) * 4096 : 0;
-  p.a_bytes = std::max(std::max(a_kmajor, a_mn), 1024u);
+  p.a_bytes = std::max(a_kmajor, 1024u);
   uint32_t cols = 32;
   while ((int)cols < max_npad) cols <<= 1;
   p.tmem_cols = cols;
