@@ -510,7 +510,11 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       e = cudaMemcpyAsync(m->tc_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
       if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
       if (e != cudaSuccess) return cuda_fail(m, e, "tensor-core parameter upload");
-      m->tc_grid = m->num_sms;  // one persistent CTA per SM
+      // Persistent CTAs; more than one per SM when shared memory and TMEM
+      // allow (co-resident CTAs overlap each other's MMA and epilogue phases).
+      int occ = std::max(1, tc_forward_occupancy(m->tcp));
+      occ = std::min<int>(occ, (int)(512 / m->tcp.tmem_cols));
+      m->tc_grid = m->num_sms * std::max(1, occ);
       m->kernel = 2;
     } else if (m->arithmetic == PONNI_B200_ARITH_TENSOR) {
       return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED, "tensor-core kernel unavailable: " + m->tc_why);

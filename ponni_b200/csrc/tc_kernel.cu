@@ -2,10 +2,10 @@
 //
 // One persistent CTA per SM, 4 warps.  Per batch tile of 128 columns:
 //   input  : cp.async (16 B, zero-filled tail) of the batch-contiguous input
-//            rows straight into an MN-major SW128 tile (prefetched one tile
-//            ahead into a second staging buffer); 16-bit models use it as the
-//            layer-0 operand directly, fp32 models split it into tf32 hi/lo
-//            K-major operands (the tf32 MMA reads K-major operands here);
+//            rows into a staging tile, prefetched one tile ahead into a
+//            second buffer; 16-bit models stage it as an MN-major SW128
+//            operand and use it for layer 0 directly, fp32 models stage it
+//            row-major and split it into K-major bf16 operand parts;
 //   layer l: thread 0 issues the UMMA chain D[128 x N] = A[128 x K] B[N x K]^T
 //            (tcgen05.mma, fp32 accumulator in TMEM) and commits it to an
 //            mbarrier; all threads wait (bounded), then each warp reads its 32
@@ -18,10 +18,14 @@
 // host is byte-for-byte the swizzled operand layout).
 //
 // Arithmetic:
-//   fp32 models: 3xTF32 -- every operand x is split into hi = tf32(x) and
-//     lo = tf32(x - hi) and D accumulates lo*HI + hi*LO + hi*HI (the
-//     error-compensated TF32 scheme; the dropped lo*lo term is below 2^-22
-//     relative), giving fp32-level accuracy on the TF32 tensor pipe;
+//   fp32 models: every operand x is split exactly into three bfloat16 parts
+//     x = b0 + b1 + b2 (b0 = bf16(x), b1 = bf16(x - b0), b2 = x - b0 - b1;
+//     8 + 8 + 8 significand bits cover fp32's 24) and D accumulates the six
+//     products whose parts sum to order <= 2 (a1B1, a0B2, a2B0, a0B1, a1B0,
+//     a0B0, smallest first); the three dropped products are below 2^-24
+//     relative.  Six bf16 MMAs cost the same tensor time as three TF32 ones
+//     and, unlike a two-way TF32 split (22 bits), represent the operands
+//     exactly, so the result is fp32-accurate;
 //   fp16/bf16 models: operands in the model type, fp32 accumulation, states
 //     rounded to the model type where the reference stores them.
 //
@@ -65,13 +69,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase; false when the limit is reached.
+// Bounded wait on an mbarrier phase (try_wait suspends the thread for a
+// hardware-chosen window per attempt); false after about 2^31 cycles.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  for (uint32_t it = 0; it < (1u << 22); ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (it > 32) __nanosleep(64);
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > (1ll << 31)) return false;
   }
-  return false;
+  return true;
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -88,15 +93,6 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 
 // UMMA, A and B from shared memory descriptors, D in TMEM.
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
@@ -128,11 +124,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
-  return r;
-}
 
 // Shared-memory matrix descriptor, SW128, sm_100 version 1.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -156,6 +147,10 @@ template <> struct Store<__nv_bfloat16> {
   static __device__ __forceinline__ __nv_bfloat16 from(float v) { return __float2bfloat16_rn(v); }
 };
 
+// Operand type of a model type: bf16 parts for fp32, else the type itself.
+template <class T> struct OperandOf { using type = T; };
+template <> struct OperandOf<float> { using type = __nv_bfloat16; };
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -165,30 +160,64 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Byte offset of element (row m, column f) of a K-major SW128 operand with
-// 128 rows, for a 16-byte-chunk aligned column group.
-__device__ __forceinline__ uint32_t kmajor_chunk(int m, uint32_t byte_in_row_total) {
-  const uint32_t kb = byte_in_row_total >> 7;  // 128-byte K block
-  const uint32_t chunk = (byte_in_row_total >> 4) & 7;
+// Exact three-way split of fp32 values into bfloat16 parts.
+__device__ __forceinline__ void split3(float x, float& b0, float& b1, float& b2) {
+  b0 = __bfloat162float(__float2bfloat16_rn(x));
+  const float r = x - b0;
+  b1 = __bfloat162float(__float2bfloat16_rn(r));
+  b2 = r - b1;  // exactly representable in bf16 (at most 8 significant bits)
+}
+
+// Byte offset of the 16-byte chunk holding byte `byte` of row m of a K-major
+// SW128 operand with 128 rows.
+__device__ __forceinline__ uint32_t kmajor_chunk(int m, uint32_t byte) {
+  const uint32_t kb = byte >> 7;
+  const uint32_t chunk = (byte >> 4) & 7;
   return kb * (kTcM * 128) + (uint32_t)m * 128 + ((chunk ^ ((uint32_t)m & 7)) << 4);
 }
 
-// Stage input columns [col0, col0+128) into the MN-major SW128 layout.
+// Write 8 consecutive K values (k0 multiple of 8) of row m into the operand
+// part(s).
+template <class T>
+__device__ __forceinline__ void store_row8(const uint32_t* a, int m, int k0, const float* v) {
+  using Op = typename OperandOf<T>::type;
+  const uint32_t off = kmajor_chunk(m, (uint32_t)k0 * 2);
+  if constexpr (sizeof(T) == 4) {
+    float p0[8], p1[8], p2[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split3(v[e], p0[e], p1[e], p2[e]);
+    st_shared_v4(a[0] + off, pack2(p0[0], p0[1], (Op*)0), pack2(p0[2], p0[3], (Op*)0), pack2(p0[4], p0[5], (Op*)0),
+                 pack2(p0[6], p0[7], (Op*)0));
+    st_shared_v4(a[1] + off, pack2(p1[0], p1[1], (Op*)0), pack2(p1[2], p1[3], (Op*)0), pack2(p1[4], p1[5], (Op*)0),
+                 pack2(p1[6], p1[7], (Op*)0));
+    st_shared_v4(a[2] + off, pack2(p2[0], p2[1], (Op*)0), pack2(p2[2], p2[3], (Op*)0), pack2(p2[4], p2[5], (Op*)0),
+                 pack2(p2[6], p2[7], (Op*)0));
+  } else {
+    st_shared_v4(a[0] + off, pack2(v[0], v[1], (Op*)0), pack2(v[2], v[3], (Op*)0), pack2(v[4], v[5], (Op*)0),
+                 pack2(v[6], v[7], (Op*)0));
+  }
+}
+
+// Stage input columns [col0, col0+128).  fp32: row-major [k][128] fp32;
+// 16-bit: MN-major SW128 operand layout.
 template <class T>
 __device__ __forceinline__ void load_input(uint32_t stage, const T* __restrict__ in, int64_t in_ld, int nin,
                                            int64_t col0, int64_t batch, bool vec) {
   constexpr int esz = sizeof(T);
-  constexpr int chunks_per_row = kTcM * esz / 16;  // 32 (fp32) or 16 (16-bit)
-  constexpr uint32_t sbo = esz * 1024;
+  constexpr int per16 = 16 / esz;
+  constexpr int chunks_per_row = kTcM / per16;  // 32 (fp32) or 16 (16-bit)
   if (vec) {
     for (int i = threadIdx.x; i < nin * chunks_per_row; i += kTcThreads) {
       const int f = i / chunks_per_row, j = i - f * chunks_per_row;
-      const int64_t col = col0 + (int64_t)j * (16 / esz);
+      const int64_t col = col0 + (int64_t)j * per16;
       const int64_t valid = batch - col;
-      const int bytes = valid >= 16 / esz ? 16 : (valid > 0 ? (int)valid * esz : 0);
+      const int bytes = valid >= per16 ? 16 : (valid > 0 ? (int)valid * esz : 0);
       const T* src = in + (int64_t)f * in_ld + (bytes > 0 ? col : 0);
-      const uint32_t dst = stage + (uint32_t)(f >> 3) * sbo + (uint32_t)(j >> 3) * 1024 + (uint32_t)(f & 7) * 128 +
-                           ((((uint32_t)j & 7) ^ ((uint32_t)f & 7)) << 4);
+      uint32_t dst;
+      if constexpr (esz == 4) dst = stage + (uint32_t)f * 512 + (uint32_t)j * 16;
+      else
+        dst = stage + (uint32_t)(f >> 3) * 2048 + (uint32_t)(j >> 3) * 1024 + (uint32_t)(f & 7) * 128 +
+              ((((uint32_t)j & 7) ^ ((uint32_t)f & 7)) << 4);
       cp_async16(dst, src, bytes);
     }
   } else {
@@ -196,16 +225,15 @@ __device__ __forceinline__ void load_input(uint32_t stage, const T* __restrict__
       const int f = i / kTcM, m = i - f * kTcM;
       const int64_t col = col0 + m;
       T v = col < batch ? in[(int64_t)f * in_ld + col] : Store<T>::from(0.0f);
-      const uint32_t byte = (uint32_t)m * esz;
-      const uint32_t j = byte >> 4;
-      const uint32_t dst = stage + (uint32_t)(f >> 3) * sbo + (j >> 3) * 1024 + (uint32_t)(f & 7) * 128 +
-                           (((j & 7) ^ ((uint32_t)f & 7)) << 4) + (byte & 15);
       if constexpr (esz == 4) {
-        asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(dst), "r"(__float_as_uint(*reinterpret_cast<float*>(&v)))
+        asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(stage + (uint32_t)f * 512 + (uint32_t)m * 4),
+                     "r"(__float_as_uint(*reinterpret_cast<float*>(&v)))
                      : "memory");
       } else {
-        asm volatile("st.shared.b16 [%0], %1;\n" ::"r"(dst), "h"(*reinterpret_cast<unsigned short*>(&v))
-                     : "memory");
+        const uint32_t byte = (uint32_t)m * 2, j = byte >> 4;
+        const uint32_t dst = stage + (uint32_t)(f >> 3) * 2048 + (j >> 3) * 1024 + (uint32_t)(f & 7) * 128 +
+                             (((j & 7) ^ ((uint32_t)f & 7)) << 4) + (byte & 15);
+        asm volatile("st.shared.b16 [%0], %1;\n" ::"r"(dst), "h"(*reinterpret_cast<unsigned short*>(&v)) : "memory");
       }
     }
   }
@@ -220,19 +248,17 @@ __device__ __forceinline__ float epi_act(float v, const TcLayer& L) {
 // Epilogue of one layer for this thread's TMEM lane (= batch column m).
 template <class T, int ACT>
 __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t tmem_lane, const float* bias,
-                                         uint32_t a_hi, uint32_t a_lo, T* __restrict__ out, int64_t out_ld,
-                                         int64_t col, int64_t batch, int m) {
-  constexpr bool TF32 = sizeof(T) == 4;
+                                         const uint32_t* a, T* __restrict__ out, int64_t out_ld, int64_t col,
+                                         int64_t batch, int m) {
   for (int c0 = 0; c0 < L.n_pad; c0 += 32) {
     float v[32];
     tmem_ld32(tmem_lane + (uint32_t)c0, v);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const int f = c0 + j;
       float x = v[j];
-      if (L.has_bias) x += bias[f];  // bias is zero-padded to the 32-column boundary
+      if (L.has_bias) x += bias[c0 + j];  // bias is zero-padded to the 32-column boundary
       x = epi_act<ACT>(x, L);
-      v[j] = f < L.nout ? x : 0.0f;
+      v[j] = c0 + j < L.nout ? x : 0.0f;
     }
     if (last) {
       if (col < batch) {
@@ -240,38 +266,18 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
         for (int j = 0; j < 32; ++j)
           if (c0 + j < L.nout) out[(int64_t)(c0 + j) * out_ld + col] = Store<T>::from(v[j]);
       }
-    } else if constexpr (TF32) {
-      // 32 fp32 columns = one 128-byte K block row: 8 chunks of 4.
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          h[e] = to_tf32(v[4 * q + e]);
-          l[e] = to_tf32(v[4 * q + e] - __uint_as_float(h[e]));
-        }
-        const uint32_t off = kmajor_chunk(m, (uint32_t)(c0 + 4 * q) * 4);
-        st_shared_v4(a_hi + off, h[0], h[1], h[2], h[3]);
-        st_shared_v4(a_lo + off, l[0], l[1], l[2], l[3]);
-      }
     } else {
-      // 32 16-bit columns = 64 bytes: 4 chunks of 8.
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t off = kmajor_chunk(m, (uint32_t)(c0 + 8 * q) * 2);
-        st_shared_v4(a_hi + off, pack2(v[8 * q], v[8 * q + 1], (T*)nullptr),
-                     pack2(v[8 * q + 2], v[8 * q + 3], (T*)nullptr), pack2(v[8 * q + 4], v[8 * q + 5], (T*)nullptr),
-                     pack2(v[8 * q + 6], v[8 * q + 7], (T*)nullptr));
-      }
+      for (int q = 0; q < 4; ++q) store_row8<T>(a, m, c0 + 8 * q, v + 8 * q);
     }
   }
 }
 
 template <class T>
 __device__ __forceinline__ void epilogue_dispatch(const TcLayer& L, bool last, uint32_t tmem_lane, const float* bias,
-                                                  uint32_t a_hi, uint32_t a_lo, T* __restrict__ out, int64_t out_ld,
+                                                  const uint32_t* a, T* __restrict__ out, int64_t out_ld,
                                                   int64_t col, int64_t batch, int m) {
-#define PONNI_TC_EPI(A) epilogue<T, A>(L, last, tmem_lane, bias, a_hi, a_lo, out, out_ld, col, batch, m)
+#define PONNI_TC_EPI(A) epilogue<T, A>(L, last, tmem_lane, bias, a, out, out_ld, col, batch, m)
   switch (L.act) {
     case EPI_RELU: PONNI_TC_EPI(EPI_RELU); break;
     case EPI_LEAKY_RELU: PONNI_TC_EPI(EPI_LEAKY_RELU); break;
@@ -286,24 +292,25 @@ __device__ __forceinline__ void epilogue_dispatch(const TcLayer& L, bool last, u
 
 // --------------------------------------------------------------- kernel --
 template <class T>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads)
     tc_forward_kernel(const __grid_constant__ TcProgram p, const unsigned char* __restrict__ image,
                       const T* __restrict__ in, int64_t in_ld, T* __restrict__ out, int64_t out_ld, int64_t batch,
                       int in_vec, int* __restrict__ err) {
-  constexpr bool TF32 = sizeof(T) == 4;
+  constexpr bool SPLIT = sizeof(T) == 4;
+  constexpr int NP = SPLIT ? 3 : 1;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // Swizzled operands need 1024-byte aligned atoms.
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* base_ptr = smem_raw + (base - raw);
   const uint32_t s_image = base;
-  const uint32_t s_ahi = s_image + p.image_bytes;
-  const uint32_t s_alo = s_ahi + p.a_bytes;
-  const uint32_t s_stage0 = s_alo + (TF32 ? p.a_bytes : 0u);
+  uint32_t s_a[3];
+#pragma unroll
+  for (int q = 0; q < 3; ++q) s_a[q] = s_image + p.image_bytes + (uint32_t)(q < NP ? q : 0) * p.a_bytes;
+  const uint32_t s_stage0 = s_image + p.image_bytes + (uint32_t)NP * p.a_bytes;
   const uint32_t s_stage1 = s_stage0 + p.stage_bytes;
   const uint32_t s_bar = s_stage1 + p.stage_bytes;
   const uint32_t s_tmem = s_bar + 8;
-  const float* bias_base = reinterpret_cast<const float*>(base_ptr);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(base_ptr + (s_tmem - base));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -335,7 +342,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t phase = 0;
   int cur = 0;
   bool failed = false;
-  const int kstep = 32 / p.esz;  // UMMA K elements per instruction (32 bytes)
 
   for (; tile < ntiles && !failed; tile += gridDim.x) {
     const int64_t col0 = tile * kTcM;
@@ -345,27 +351,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     cp_async_commit();
     cp_async_wait_1();
     __syncthreads();
-    if constexpr (TF32) {
-      // Split the fp32 input tile into tf32 hi/lo operands and transpose it
-      // to K-major (the MN-major operand form is used for 16-bit inputs
-      // only): thread m builds row m from column m of the staged tile.
+    if constexpr (SPLIT) {
+      // Thread m splits column m of the staged fp32 tile into the K-major
+      // bf16 operand parts of layer 0.
       const int k0 = p.layers[0].k_pad;
-      const unsigned char* st = base_ptr + (stage - base);
-      const uint32_t mo = (uint32_t)(tid >> 5) * 1024 + (uint32_t)(tid & 3) * 4;
-      const uint32_t mc = (uint32_t)(tid & 31) >> 2;
-      for (int f = 0; f < k0; f += 4) {
-        uint32_t h[4], lo[4];
+      const float* st = reinterpret_cast<const float*>(base_ptr + (stage - base));
+      for (int f = 0; f < k0; f += 8) {
+        float v[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t fe = (uint32_t)(f + e);
-          const float x = *reinterpret_cast<const float*>(st + (fe >> 3) * 4096 + mo + (fe & 7) * 128 +
-                                                          ((mc ^ (fe & 7)) << 4));
-          h[e] = to_tf32(x);
-          lo[e] = to_tf32(x - __uint_as_float(h[e]));
-        }
-        const uint32_t off = kmajor_chunk(tid, (uint32_t)f * 4);
-        st_shared_v4(s_ahi + off, h[0], h[1], h[2], h[3]);
-        st_shared_v4(s_alo + off, lo[0], lo[1], lo[2], lo[3]);
+        for (int e = 0; e < 8; ++e) v[e] = st[(f + e) * kTcM + m];
+        store_row8<T>(s_a, m, f, v);
       }
     }
     for (int l = 0; l < p.n_layers; ++l) {
@@ -375,34 +370,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncthreads();
       if (tid == 0) {
         tc_fence_after();
-        const int nsteps = L.k_pad / kstep;
-        const uint32_t w_hi = s_image + L.w_hi_off, w_lo = s_image + L.w_lo_off;
+        const int nsteps = L.k_pad / 16;  // UMMA K = 16 for 16-bit operands (32 bytes)
         const uint32_t b_block = (uint32_t)L.n_pad * 128;
         for (int s = 0; s < nsteps; ++s) {
           const uint32_t kb = (uint32_t)s >> 2, ks = (uint32_t)s & 3;
           const uint32_t b_off = kb * b_block + ks * 32;
-          uint64_t ad_hi, ad_lo;
-          uint32_t idesc;
-          if (!TF32 && l == 0) {
-            // 16-bit layer 0 reads the staged input tile as an MN-major
-            // operand: one K step = 32 bytes of K for 128 rows = 4096 bytes.
-            ad_hi = smem_desc(stage + (uint32_t)s * 4096, 1024, (uint32_t)p.esz * 1024);
-            ad_lo = ad_hi;
-            idesc = L.idesc_mn;
+          const uint32_t a_off = kb * (kTcM * 128) + ks * 32;
+          const uint32_t acc = s > 0 ? 1u : 0u;
+          if constexpr (SPLIT) {
+            uint64_t ad[3], bd[3];
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+              ad[q] = smem_desc(s_a[q] + a_off, 16, 1024);
+              bd[q] = smem_desc(s_image + L.w_off[q] + b_off, 16, 1024);
+            }
+            umma_f16(tmem_base, ad[1], bd[1], L.idesc, acc);
+            umma_f16(tmem_base, ad[0], bd[2], L.idesc, 1u);
+            umma_f16(tmem_base, ad[2], bd[0], L.idesc, 1u);
+            umma_f16(tmem_base, ad[0], bd[1], L.idesc, 1u);
+            umma_f16(tmem_base, ad[1], bd[0], L.idesc, 1u);
+            umma_f16(tmem_base, ad[0], bd[0], L.idesc, 1u);
           } else {
-            const uint32_t a_off = kb * (kTcM * 128) + ks * 32;
-            ad_hi = smem_desc(s_ahi + a_off, 16, 1024);
-            ad_lo = smem_desc(s_alo + a_off, 16, 1024);
-            idesc = L.idesc;
-          }
-          const uint64_t bd_hi = smem_desc(w_hi + b_off, 16, 1024);
-          if constexpr (TF32) {
-            const uint64_t bd_lo = smem_desc(w_lo + b_off, 16, 1024);
-            umma_tf32(tmem_base, ad_lo, bd_hi, idesc, s > 0 ? 1u : 0u);
-            umma_tf32(tmem_base, ad_hi, bd_lo, idesc, 1u);
-            umma_tf32(tmem_base, ad_hi, bd_hi, idesc, 1u);
-          } else {
-            umma_f16(tmem_base, ad_hi, bd_hi, idesc, s > 0 ? 1u : 0u);
+            const uint64_t bd = smem_desc(s_image + L.w_off[0] + b_off, 16, 1024);
+            if (l == 0) {
+              // The staged input tile is the MN-major layer-0 operand: one K
+              // step = 32 bytes of K for 128 rows = 4096 bytes.
+              umma_f16(tmem_base, smem_desc(stage + (uint32_t)s * 4096, 1024, 2048), bd, L.idesc_mn, acc);
+            } else {
+              umma_f16(tmem_base, smem_desc(s_a[0] + a_off, 16, 1024), bd, L.idesc, acc);
+            }
           }
         }
         umma_commit(s_bar);
@@ -415,9 +411,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         failed = true;
         break;
       }
-      const bool last = l == p.n_layers - 1;
-      const float* bias = reinterpret_cast<const float*>(reinterpret_cast<const unsigned char*>(bias_base) + L.bias_off);
-      epilogue_dispatch<T>(L, last, tmem_lane, bias, s_ahi, s_alo, out, out_ld, col0 + m, batch, m);
+      const float* bias = reinterpret_cast<const float*>(base_ptr + L.bias_off);
+      epilogue_dispatch<T>(L, l == p.n_layers - 1, tmem_lane, bias, s_a, out, out_ld, col0 + m, batch, m);
     }
     cur ^= 1;
   }
@@ -443,6 +438,21 @@ cudaError_t launch_impl(const TcProgram& p, const void* image, const void* in, i
   return cudaGetLastError();
 }
 
+template <class T>
+int occupancy_impl(size_t smem) {
+  auto kern = tc_forward_kernel<T>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, kTcThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return blocks;
+}
+
 }  // namespace
 
 cudaError_t launch_tc_forward(const TcProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
@@ -453,6 +463,15 @@ cudaError_t launch_tc_forward(const TcProgram& p, const void* image, const void*
     case 3: return launch_impl<__nv_bfloat16>(p, image, in, in_ld, out, out_ld, batch, grid, err, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+int tc_forward_occupancy(const TcProgram& p) {
+  switch (p.dtype) {
+    case 0: return occupancy_impl<float>(p.smem_bytes);
+    case 2: return occupancy_impl<__half>(p.smem_bytes);
+    case 3: return occupancy_impl<__nv_bfloat16>(p.smem_bytes);
+  }
+  return 0;
 }
 
 }  // namespace ponni_b200

@@ -21,18 +21,6 @@ bool tc_activation(int k) {
          k == PONNI_B200_TANH || k == PONNI_B200_SIGMOID;
 }
 
-// cvt.rna.tf32.f32 on the host: round the 13 dropped mantissa bits to
-// nearest, ties away from zero.
-float tf32_rna(float x) {
-  uint32_t u;
-  memcpy(&u, &x, 4);
-  if ((u & 0x7f800000u) == 0x7f800000u) return x;  // inf / nan unchanged
-  u = (u + 0x1000u) & ~0x1fffu;
-  float r;
-  memcpy(&r, &u, 4);
-  return r;
-}
-
 // Place one element into a K-major SW128 operand with `rows` rows.
 void put_kmajor(std::vector<unsigned char>& img, size_t base, int rows, int n, int k, int esz, const void* val) {
   const int kper = 128 / esz;
@@ -44,7 +32,8 @@ void put_kmajor(std::vector<unsigned char>& img, size_t base, int rows, int n, i
 }
 
 uint32_t make_idesc(int dtype, int n_pad, bool a_mn_major) {
-  const uint32_t fmt = dtype == PONNI_B200_F32 ? 2u : (dtype == PONNI_B200_BF16 ? 1u : 0u);
+  // fp32 models run on bf16 operand parts
+  const uint32_t fmt = dtype == PONNI_B200_F16 ? 0u : 1u;
   return (1u << 4) | (fmt << 7) | (fmt << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((uint32_t)(n_pad >> 3) << 17) |
          ((uint32_t)(kTcM >> 4) << 24);
 }
@@ -56,11 +45,12 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   image.clear();
   const ponni_b200_dtype dt = m->dtype;
   if (dt != PONNI_B200_F32 && dt != PONNI_B200_F16 && dt != PONNI_B200_BF16) {
-    why = "tensor-core path supports fp32 (3xTF32), fp16 and bf16 models";
+    why = "tensor-core path supports fp32 (bf16 3-way split), fp16 and bf16 models";
     return false;
   }
-  const int esz = dt == PONNI_B200_F32 ? 4 : 2;
-  const int kstep = 32 / esz;
+  const bool split = dt == PONNI_B200_F32;
+  const int nparts = split ? 3 : 1;
+  const int kstep = 16;  // UMMA K for 16-bit operands
   const size_t msz = dtype_bytes(dt);
   // Walk [Matvec][Bias]?[activation]? blocks.
   struct Blk { const Layer* mv; const Layer* bias; const Layer* act; };
@@ -83,7 +73,7 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   }
   p.n_layers = (int)blocks.size();
   p.dtype = (int)dt;
-  p.esz = esz;
+  p.nparts = nparts;
   p.nin = blocks.front().mv->d.num_inputs;
   p.nout = blocks.back().mv->d.num_outputs;
   int max_npad = 0, max_w32 = 0;
@@ -119,15 +109,11 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   off = round_up(off, 1024);
   for (int l = 0; l < p.n_layers; ++l) {
     TcLayer& L = p.layers[l];
-    const int nkb = (int)((L.k_pad * esz + 127) / 128);
+    const int nkb = (int)((L.k_pad * 2 + 127) / 128);
     const size_t bytes = (size_t)nkb * L.n_pad * 128;
-    L.w_hi_off = (uint32_t)off;
-    off += round_up(bytes, 1024);
-    if (esz == 4) {
-      L.w_lo_off = (uint32_t)off;
-      off += round_up(bytes, 1024);
-    } else {
-      L.w_lo_off = L.w_hi_off;
+    for (int q = 0; q < 3; ++q) {
+      L.w_off[q] = (uint32_t)off;
+      if (q < nparts) off += round_up(bytes, 1024);
     }
   }
   p.image_bytes = (uint32_t)round_up(off, 1024);
@@ -142,27 +128,33 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
     for (int k = 0; k < L.nin; ++k) {
       for (int n = 0; n < L.nout; ++n) {
         const unsigned char* src = mv.params.data() + ((size_t)k * L.nout + n) * msz;  // W[k][n]
-        if (esz == 4) {
+        if (split) {
           float w;
           memcpy(&w, src, 4);
-          const float hi = tf32_rna(w), lo = tf32_rna(w - hi);
-          put_kmajor(image, L.w_hi_off, L.n_pad, n, k, 4, &hi);
-          put_kmajor(image, L.w_lo_off, L.n_pad, n, k, 4, &lo);
+          // exact three-way bf16 split w = b0 + b1 + b2
+          const __nv_bfloat16 b0 = __float2bfloat16_rn(w);
+          const float r = w - __bfloat162float(b0);
+          const __nv_bfloat16 b1 = __float2bfloat16_rn(r);
+          const __nv_bfloat16 b2 = __float2bfloat16_rn(r - __bfloat162float(b1));
+          put_kmajor(image, L.w_off[0], L.n_pad, n, k, 2, &b0);
+          put_kmajor(image, L.w_off[1], L.n_pad, n, k, 2, &b1);
+          put_kmajor(image, L.w_off[2], L.n_pad, n, k, 2, &b2);
         } else {
-          put_kmajor(image, L.w_hi_off, L.n_pad, n, k, 2, src);
+          put_kmajor(image, L.w_off[0], L.n_pad, n, k, 2, src);
         }
       }
     }
   }
   const int k0 = p.layers[0].k_pad;
-  if (esz == 4) max_w32 = std::max(max_w32, (int)round_up(k0, 32));  // layer 0 is K-major for tf32
-  p.stage_bytes = (uint32_t)(k0 / 8) * (uint32_t)esz * 1024;
-  const uint32_t a_kmajor = (uint32_t)((max_w32 * esz + 127) / 128) * kTcM * 128;
+  if (split) max_w32 = std::max(max_w32, (int)round_up(k0, 32));  // fp32 layer 0 is K-major
+  // fp32: row-major [k0][128] fp32 staging; 16-bit: MN-major operand (k0/8 atoms of 2 KB).
+  p.stage_bytes = split ? (uint32_t)k0 * kTcM * 4 : (uint32_t)(k0 / 8) * 2048;
+  const uint32_t a_kmajor = (uint32_t)((max_w32 * 2 + 127) / 128) * kTcM * 128;
   p.a_bytes = std::max(a_kmajor, 1024u);
   uint32_t cols = 32;
   while ((int)cols < max_npad) cols <<= 1;
   p.tmem_cols = cols;
-  p.smem_bytes = 1024 + p.image_bytes + p.a_bytes * (esz == 4 ? 2 : 1) + 2 * p.stage_bytes + 64;
+  p.smem_bytes = 1024 + p.image_bytes + p.a_bytes * (uint32_t)nparts + 2 * p.stage_bytes + 64;
   if (p.smem_bytes > 227 * 1024) {
     why = "weights and operand tiles exceed shared memory";
     return false;

@@ -11,9 +11,11 @@
 //    holding 128/esz consecutive K elements; 8-row groups 1024 B apart (SBO);
 //    K beyond one row lives in the next "K block" of rows x 128 B; 16-byte
 //    chunk c of row r is stored at chunk position c ^ (r % 8).
-//  * MN-major (the activations A of layer 0, copied straight from the
-//    batch-contiguous input): atoms of 8 k-rows x 128 B (128/esz batch
-//    columns); atoms along M 1024 B apart (LBO), along K esz*1024 B apart (SBO).
+//  * MN-major (the layer-0 activations of 16-bit models, copied straight from
+//    the batch-contiguous input): atoms of 8 k-rows x 128 B (64 batch
+//    columns); atoms along M 1024 B apart (LBO), along K 2048 B apart (SBO).
+// All operands are 16-bit (fp16 / bf16); fp32 models split every operand
+// x exactly into three bf16 parts x = b0 + b1 + b2.
 #pragma once
 #include <stdint.h>
 
@@ -31,20 +33,19 @@ struct TcLayer {
   float s0, s1;          // activation scalars
   int32_t has_bias;
   uint32_t bias_off;     // byte offset of float bias[n_pad] in the staged image
-  uint32_t w_hi_off;     // byte offset of the K-major B operand (hi part for 3xTF32)
-  uint32_t w_lo_off;     // 3xTF32 low part (unused otherwise)
+  uint32_t w_off[3];     // byte offsets of the K-major B operand parts (1, or 3 for split fp32)
   uint32_t idesc;        // UMMA instruction descriptor (A K-major)
   uint32_t idesc_mn;     // same with A MN-major (layer 0)
 };
 
 struct TcProgram {
   int32_t n_layers;
-  int32_t dtype;         // ponni_b200_dtype (0 f32 -> 3xTF32, 2 f16, 3 bf16)
+  int32_t dtype;         // ponni_b200_dtype (0 f32 -> bf16 3-way split, 2 f16, 3 bf16)
   int32_t nin, nout;
-  int32_t esz;           // operand element size (4 tf32, 2 f16/bf16)
+  int32_t nparts;        // operand parts: 3 (fp32 split into bf16 b0+b1+b2) or 1
   uint32_t image_bytes;  // staged parameter image (multiple of 16)
-  uint32_t a_bytes;      // one activation operand buffer
-  uint32_t stage_bytes;  // one input staging buffer (MN-major, k_pad0 rows)
+  uint32_t a_bytes;      // one activation operand buffer (one part)
+  uint32_t stage_bytes;  // one input staging buffer
   uint32_t tmem_cols;    // power of two >= 32 and >= every n_pad
   uint32_t smem_bytes;   // total dynamic shared memory requested (incl. 1 KB alignment slack)
   TcLayer layers[kTcMaxLayers];
