@@ -37,6 +37,8 @@ def parse():
     p.add_argument("--batch", type=int, default=0, help="override per-GPU batch (default: the config's)")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--arith", default="auto", choices=["auto", "reference", "tensor"],
+                   help="kernel selection (ponni_b200_model_set_arithmetic)")
     return p.parse_args()
 
 
@@ -164,7 +166,9 @@ def main():
     dev = torch.device(f"cuda:{local}")
     B = cfg.batch
     nin, nout = cfg.layers[0].num_inputs, cfg.layers[-1].num_outputs
-    model = pb.Inference(cfg.layers, dtype=cfg.dtype, device=local)
+    arith = {"auto": pb._abi.ARITH_AUTO, "reference": pb._abi.ARITH_REFERENCE, "tensor": pb._abi.ARITH_TENSOR}[args.arith]
+    model = pb.Inference(cfg.layers, dtype=cfg.dtype, device=local, arithmetic=arith)
+    kernel_name = {1: "tile_forward_kernel (SIMT)", 2: "tc_forward_kernel (tcgen05)"}[model.kernel()]
     tdt = model.torch_dtype()
     x = torch.empty((nin, B), dtype=tdt, device=dev)
     y = torch.empty((nout, B), dtype=tdt, device=dev)
@@ -255,7 +259,7 @@ def main():
             "config": {"workload": cfg.name, "batch_per_gpu": B, "global_batch": world * B, "nin": nin,
                        "nout": nout, "parallelism": f"column shards x{world}, no collective",
                        "l2": "inputs larger than L2 (no flush)"},
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,
+            "kernel": kernel_name, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,
         }), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -510,11 +510,7 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       e = cudaMemcpyAsync(m->tc_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
       if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
       if (e != cudaSuccess) return cuda_fail(m, e, "tensor-core parameter upload");
-      // Persistent CTAs; more than one per SM when shared memory and TMEM
-      // allow (co-resident CTAs overlap each other's MMA and epilogue phases).
-      int occ = std::max(1, tc_forward_occupancy(m->tcp));
-      occ = std::min<int>(occ, (int)(512 / m->tcp.tmem_cols));
-      m->tc_grid = m->num_sms * std::max(1, occ);
+      m->tc_grid = m->num_sms;  // one persistent CTA (two tile slots) per SM
       m->kernel = 2;
     } else if (m->arithmetic == PONNI_B200_ARITH_TENSOR) {
       return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED, "tensor-core kernel unavailable: " + m->tc_why);
@@ -714,7 +710,7 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
   cudaError_t e;
   if (m->kernel == 2) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
-    const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
+    const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + kTcSlots - 1) / kTcSlots);
     e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
   } else {
     const int64_t ntiles = (batch + m->prog.bt - 1) / m->prog.bt;

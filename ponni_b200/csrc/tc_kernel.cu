@@ -1,6 +1,8 @@
 // Tensor-core dense-chain kernel for sm_100a (tcgen05 UMMA + TMEM).
 //
-// One persistent CTA per SM, 4 warps.  Per batch tile of 128 columns:
+// One persistent CTA per SM with two warpgroups, each owning one tile slot so
+// that one slot's epilogue overlaps the other's MMAs.  Per batch tile of 128
+// columns:
 //   input  : cp.async (16 B, zero-filled tail) of the batch-contiguous input
 //            rows into a staging tile, prefetched one tile ahead into a
 //            second buffer; 16-bit models stage it as an MN-major SW128
@@ -50,7 +52,6 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int sr
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -160,13 +161,20 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Exact three-way split of fp32 values into bfloat16 parts.
-__device__ __forceinline__ void split3(float x, float& b0, float& b1, float& b2) {
-  b0 = __bfloat162float(__float2bfloat16_rn(x));
-  const float r = x - b0;
-  b1 = __bfloat162float(__float2bfloat16_rn(r));
-  b2 = r - b1;  // exactly representable in bf16 (at most 8 significant bits)
+// Exact three-way split of an fp32 value into bfloat16 parts by truncation:
+// b0 keeps the top 8 significant bits, b1 the next 8, b2 the rest (at most 8
+// bits, so exactly representable).  Integer masks and two FADDs, no
+// conversion instructions.  Returns the three parts as fp32 bit patterns
+// whose low 16 bits are zero.
+__device__ __forceinline__ void split3(float x, uint32_t& h0, uint32_t& h1, uint32_t& h2) {
+  h0 = __float_as_uint(x) & 0xFFFF0000u;
+  const float r1 = x - __uint_as_float(h0);
+  h1 = __float_as_uint(r1) & 0xFFFF0000u;
+  h2 = __float_as_uint(r1 - __uint_as_float(h1));
 }
+
+// Two bf16 parts (as fp32 bit patterns) -> one packed bf16x2 word (lo first).
+__device__ __forceinline__ uint32_t pack_hi16(uint32_t lo, uint32_t hi) { return __byte_perm(lo, hi, 0x7632); }
 
 // Byte offset of the 16-byte chunk holding byte `byte` of row m of a K-major
 // SW128 operand with 128 rows.
@@ -183,15 +191,15 @@ __device__ __forceinline__ void store_row8(const uint32_t* a, int m, int k0, con
   using Op = typename OperandOf<T>::type;
   const uint32_t off = kmajor_chunk(m, (uint32_t)k0 * 2);
   if constexpr (sizeof(T) == 4) {
-    float p0[8], p1[8], p2[8];
+    uint32_t p0[8], p1[8], p2[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) split3(v[e], p0[e], p1[e], p2[e]);
-    st_shared_v4(a[0] + off, pack2(p0[0], p0[1], (Op*)0), pack2(p0[2], p0[3], (Op*)0), pack2(p0[4], p0[5], (Op*)0),
-                 pack2(p0[6], p0[7], (Op*)0));
-    st_shared_v4(a[1] + off, pack2(p1[0], p1[1], (Op*)0), pack2(p1[2], p1[3], (Op*)0), pack2(p1[4], p1[5], (Op*)0),
-                 pack2(p1[6], p1[7], (Op*)0));
-    st_shared_v4(a[2] + off, pack2(p2[0], p2[1], (Op*)0), pack2(p2[2], p2[3], (Op*)0), pack2(p2[4], p2[5], (Op*)0),
-                 pack2(p2[6], p2[7], (Op*)0));
+    st_shared_v4(a[0] + off, pack_hi16(p0[0], p0[1]), pack_hi16(p0[2], p0[3]), pack_hi16(p0[4], p0[5]),
+                 pack_hi16(p0[6], p0[7]));
+    st_shared_v4(a[1] + off, pack_hi16(p1[0], p1[1]), pack_hi16(p1[2], p1[3]), pack_hi16(p1[4], p1[5]),
+                 pack_hi16(p1[6], p1[7]));
+    st_shared_v4(a[2] + off, pack_hi16(p2[0], p2[1]), pack_hi16(p2[2], p2[3]), pack_hi16(p2[4], p2[5]),
+                 pack_hi16(p2[6], p2[7]));
   } else {
     st_shared_v4(a[0] + off, pack2(v[0], v[1], (Op*)0), pack2(v[2], v[3], (Op*)0), pack2(v[4], v[5], (Op*)0),
                  pack2(v[6], v[7], (Op*)0));
@@ -202,12 +210,12 @@ __device__ __forceinline__ void store_row8(const uint32_t* a, int m, int k0, con
 // 16-bit: MN-major SW128 operand layout.
 template <class T>
 __device__ __forceinline__ void load_input(uint32_t stage, const T* __restrict__ in, int64_t in_ld, int nin,
-                                           int64_t col0, int64_t batch, bool vec) {
+                                           int64_t col0, int64_t batch, bool vec, int lt) {
   constexpr int esz = sizeof(T);
   constexpr int per16 = 16 / esz;
   constexpr int chunks_per_row = kTcM / per16;  // 32 (fp32) or 16 (16-bit)
   if (vec) {
-    for (int i = threadIdx.x; i < nin * chunks_per_row; i += kTcThreads) {
+    for (int i = lt; i < nin * chunks_per_row; i += kTcWgThreads) {
       const int f = i / chunks_per_row, j = i - f * chunks_per_row;
       const int64_t col = col0 + (int64_t)j * per16;
       const int64_t valid = batch - col;
@@ -221,7 +229,7 @@ __device__ __forceinline__ void load_input(uint32_t stage, const T* __restrict__
       cp_async16(dst, src, bytes);
     }
   } else {
-    for (int i = threadIdx.x; i < nin * kTcM; i += kTcThreads) {
+    for (int i = lt; i < nin * kTcM; i += kTcWgThreads) {
       const int f = i / kTcM, m = i - f * kTcM;
       const int64_t col = col0 + m;
       T v = col < batch ? in[(int64_t)f * in_ld + col] : Store<T>::from(0.0f);
@@ -245,7 +253,9 @@ __device__ __forceinline__ float epi_act(float v, const TcLayer& L) {
   else return activation<float>(ACT, L.act_flags, v, L.s0, L.s1);
 }
 
-// Epilogue of one layer for this thread's TMEM lane (= batch column m).
+// Epilogue of one layer for this thread's TMEM lane (= batch column m):
+// sum the layer's accumulators, add the bias, apply the activation (fp32),
+// then write the next layer's operand, or the caller's output.
 template <class T, int ACT>
 __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t tmem_lane, const float* bias,
                                          const uint32_t* a, T* __restrict__ out, int64_t out_ld, int64_t col,
@@ -253,11 +263,26 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
   for (int c0 = 0; c0 < L.n_pad; c0 += 32) {
     float v[32];
     tmem_ld32(tmem_lane + (uint32_t)c0, v);
+    for (int g = 1; g < L.groups; ++g) {
+      float w[32];
+      tmem_ld32(tmem_lane + (uint32_t)(g * L.n_pad + c0), w);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += w[j];
+    }
+    if (L.has_bias) {
+      const float4* b4 = reinterpret_cast<const float4*>(bias + c0);  // zero-padded to 32 columns
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 b = b4[q];
+        v[4 * q] += b.x;
+        v[4 * q + 1] += b.y;
+        v[4 * q + 2] += b.z;
+        v[4 * q + 3] += b.w;
+      }
+    }
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      float x = v[j];
-      if (L.has_bias) x += bias[c0 + j];  // bias is zero-padded to the 32-column boundary
-      x = epi_act<ACT>(x, L);
+      const float x = epi_act<ACT>(v[j], L);
       v[j] = c0 + j < L.nout ? x : 0.0f;
     }
     if (last) {
@@ -290,70 +315,130 @@ __device__ __forceinline__ void epilogue_dispatch(const TcLayer& L, bool last, u
 #undef PONNI_TC_EPI
 }
 
+// Named barrier over one warpgroup (ids 1..kTcSlots; 0 is __syncthreads).
+__device__ __forceinline__ void wg_sync(int wg) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(wg + 1), "r"(kTcWgThreads) : "memory");
+}
+__device__ __forceinline__ int wg_sync_or(int wg, int pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %2, 0;\n\t"
+      "bar.red.or.pred q, %1, %3, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(wg + 1), "r"(pred), "r"(kTcWgThreads)
+      : "memory");
+  return r;
+}
+
+// Issue the UMMA chain of layer L for one slot (one elected thread).
+template <bool SPLIT>
+__device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint32_t d_tmem, const uint32_t* s_a,
+                                            uint32_t s_image, uint32_t stage) {
+  const int nsteps = L.k_pad / 16;  // UMMA K = 16 for 16-bit operands (32 bytes)
+  const uint32_t b_block = (uint32_t)L.n_pad * 128;
+  for (int s = 0; s < nsteps; ++s) {
+    const uint32_t kb = (uint32_t)s >> 2, ks = (uint32_t)s & 3;
+    const uint32_t b_off = kb * b_block + ks * 32;
+    const uint32_t a_off = kb * (kTcM * 128) + ks * 32;
+    const int g = s / L.group_steps;
+    const uint32_t d = d_tmem + (uint32_t)(g * L.n_pad);
+    const uint32_t acc = (s - g * L.group_steps) > 0 ? 1u : 0u;
+    if constexpr (SPLIT) {
+      uint64_t ad[3], bd[3];
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        ad[q] = smem_desc(s_a[q] + a_off, 16, 1024);
+        bd[q] = smem_desc(s_image + L.w_off[q] + b_off, 16, 1024);
+      }
+      // smallest products first
+      umma_f16(d, ad[1], bd[1], L.idesc, acc);
+      umma_f16(d, ad[0], bd[2], L.idesc, 1u);
+      umma_f16(d, ad[2], bd[0], L.idesc, 1u);
+      umma_f16(d, ad[0], bd[1], L.idesc, 1u);
+      umma_f16(d, ad[1], bd[0], L.idesc, 1u);
+      umma_f16(d, ad[0], bd[0], L.idesc, 1u);
+    } else {
+      const uint64_t bd = smem_desc(s_image + L.w_off[0] + b_off, 16, 1024);
+      if (layer0) {
+        // The staged input tile is the MN-major layer-0 operand: one K step
+        // = 32 bytes of K for 128 rows = 4096 bytes.
+        umma_f16(d, smem_desc(stage + (uint32_t)s * 4096, 1024, 2048), bd, L.idesc_mn, acc);
+      } else {
+        umma_f16(d, smem_desc(s_a[0] + a_off, 16, 1024), bd, L.idesc, acc);
+      }
+    }
+  }
+}
+
 // --------------------------------------------------------------- kernel --
+// Two warpgroups per CTA, each owning one tile slot (operand buffers, input
+// stage, mbarrier, TMEM accumulators) and walking its own tiles; while one
+// warpgroup runs its epilogue the tensor core works on the other's chain.
 template <class T>
-__global__ void __launch_bounds__(kTcThreads)
+__global__ void __launch_bounds__(kTcThreads, 1)
     tc_forward_kernel(const __grid_constant__ TcProgram p, const unsigned char* __restrict__ image,
                       const T* __restrict__ in, int64_t in_ld, T* __restrict__ out, int64_t out_ld, int64_t batch,
                       int in_vec, int* __restrict__ err) {
   constexpr bool SPLIT = sizeof(T) == 4;
   constexpr int NP = SPLIT ? 3 : 1;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // Swizzled operands need 1024-byte aligned atoms.
   const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t base = (raw + 1023u) & ~1023u;  // swizzle atoms need 1024-byte alignment
   unsigned char* base_ptr = smem_raw + (base - raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wg = warp >> 2, lt = tid & (kTcWgThreads - 1);
   const uint32_t s_image = base;
+  const uint32_t s_slot = s_image + p.image_bytes + (uint32_t)wg * p.slot_bytes;
   uint32_t s_a[3];
 #pragma unroll
-  for (int q = 0; q < 3; ++q) s_a[q] = s_image + p.image_bytes + (uint32_t)(q < NP ? q : 0) * p.a_bytes;
-  const uint32_t s_stage0 = s_image + p.image_bytes + (uint32_t)NP * p.a_bytes;
-  const uint32_t s_stage1 = s_stage0 + p.stage_bytes;
-  const uint32_t s_bar = s_stage1 + p.stage_bytes;
-  const uint32_t s_tmem = s_bar + 8;
+  for (int q = 0; q < 3; ++q) s_a[q] = s_slot + (uint32_t)(q < NP ? q : 0) * p.a_bytes;
+  const uint32_t stage = s_slot + (uint32_t)NP * p.a_bytes;
+  const uint32_t s_bars = s_image + p.image_bytes + kTcSlots * p.slot_bytes;
+  const uint32_t s_bar = s_bars + 8u * (uint32_t)wg;
+  const uint32_t s_tmem = s_bars + 8u * kTcSlots;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(base_ptr + (s_tmem - base));
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t ntiles = (batch + kTcM - 1) / kTcM;
-  int64_t tile = blockIdx.x;
-  if (tile >= ntiles) return;
+  if ((int64_t)blockIdx.x * kTcSlots >= ntiles) return;
 
-  // ---- set-up: TMEM, mbarrier, zeroed staging, parameter image ----
+  // ---- set-up (whole CTA): TMEM, mbarriers, zeroed stages, parameter image ----
   if (warp == 0) tmem_alloc(s_tmem, p.tmem_cols);
   if (tid == 0) {
-    mbar_init(s_bar, 1);
+    for (int q = 0; q < kTcSlots; ++q) mbar_init(s_bars + 8u * q, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  {
-    uint4* z = reinterpret_cast<uint4*>(base_ptr + (s_stage0 - base));
-    const int n16 = (int)(2 * p.stage_bytes / 16);
-    for (int i = tid; i < n16; i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
+  for (int q = 0; q < kTcSlots; ++q) {
+    uint4* z = reinterpret_cast<uint4*>(base_ptr + (s_image + p.image_bytes + q * p.slot_bytes + NP * p.a_bytes - base));
+    for (int i = tid; i < (int)(p.stage_bytes / 16); i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
   }
   for (uint32_t i = tid; i < p.image_bytes / 16; i += kTcThreads) cp_async16(s_image + i * 16, image + i * 16, 16);
+  cp_async_commit();
+  cp_async_wait_0();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_lane = tmem_base + ((uint32_t)(warp * 32) << 16);
-  const int m = warp * 32 + lane;  // this thread's batch row in the tile
+  const uint32_t tmem_base = *tmem_slot + (uint32_t)wg * p.slot_cols;
+  const uint32_t tmem_lane = tmem_base + ((uint32_t)((warp & 3) * 32) << 16);
+  const int m = (warp & 3) * 32 + lane;  // this thread's batch row in its slot's tile
 
-  load_input<T>(s_stage0, in, in_ld, p.nin, tile * kTcM, batch, in_vec != 0);
-  cp_async_commit();
+  // ---- per-warpgroup tile loop ----
+  const int64_t stride = (int64_t)gridDim.x * kTcSlots;
+  int64_t tile = (int64_t)blockIdx.x * kTcSlots + wg;
   uint32_t phase = 0;
-  int cur = 0;
-  bool failed = false;
-
-  for (; tile < ntiles && !failed; tile += gridDim.x) {
-    const int64_t col0 = tile * kTcM;
-    const int64_t next = tile + gridDim.x;
-    const uint32_t stage = cur ? s_stage1 : s_stage0;
-    if (next < ntiles) load_input<T>(cur ? s_stage0 : s_stage1, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0);
+  if (tile < ntiles) {
+    load_input<T>(stage, in, in_ld, p.nin, tile * kTcM, batch, in_vec != 0, lt);
     cp_async_commit();
-    cp_async_wait_1();
-    __syncthreads();
+  }
+  for (; tile < ntiles; tile += stride) {
+    const int64_t col0 = tile * kTcM;
+    const int64_t next = tile + stride;
+    cp_async_wait_0();
+    wg_sync(wg);
     if constexpr (SPLIT) {
       // Thread m splits column m of the staged fp32 tile into the K-major
-      // bf16 operand parts of layer 0.
+      // bf16 operand parts of layer 0; then the stage is free for the next tile.
       const int k0 = p.layers[0].k_pad;
       const float* st = reinterpret_cast<const float*>(base_ptr + (stage - base));
       for (int f = 0; f < k0; f += 8) {
@@ -362,66 +447,46 @@ __global__ void __launch_bounds__(kTcThreads)
         for (int e = 0; e < 8; ++e) v[e] = st[(f + e) * kTcM + m];
         store_row8<T>(s_a, m, f, v);
       }
+      wg_sync(wg);
+      if (next < ntiles) load_input<T>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
+      cp_async_commit();
     }
+    bool failed = false;
     for (int l = 0; l < p.n_layers; ++l) {
       const TcLayer& L = p.layers[l];
       fence_proxy_async();
       tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
+      wg_sync(wg);
+      if (lt == 0) {
         tc_fence_after();
-        const int nsteps = L.k_pad / 16;  // UMMA K = 16 for 16-bit operands (32 bytes)
-        const uint32_t b_block = (uint32_t)L.n_pad * 128;
-        for (int s = 0; s < nsteps; ++s) {
-          const uint32_t kb = (uint32_t)s >> 2, ks = (uint32_t)s & 3;
-          const uint32_t b_off = kb * b_block + ks * 32;
-          const uint32_t a_off = kb * (kTcM * 128) + ks * 32;
-          const uint32_t acc = s > 0 ? 1u : 0u;
-          if constexpr (SPLIT) {
-            uint64_t ad[3], bd[3];
-#pragma unroll
-            for (int q = 0; q < 3; ++q) {
-              ad[q] = smem_desc(s_a[q] + a_off, 16, 1024);
-              bd[q] = smem_desc(s_image + L.w_off[q] + b_off, 16, 1024);
-            }
-            umma_f16(tmem_base, ad[1], bd[1], L.idesc, acc);
-            umma_f16(tmem_base, ad[0], bd[2], L.idesc, 1u);
-            umma_f16(tmem_base, ad[2], bd[0], L.idesc, 1u);
-            umma_f16(tmem_base, ad[0], bd[1], L.idesc, 1u);
-            umma_f16(tmem_base, ad[1], bd[0], L.idesc, 1u);
-            umma_f16(tmem_base, ad[0], bd[0], L.idesc, 1u);
-          } else {
-            const uint64_t bd = smem_desc(s_image + L.w_off[0] + b_off, 16, 1024);
-            if (l == 0) {
-              // The staged input tile is the MN-major layer-0 operand: one K
-              // step = 32 bytes of K for 128 rows = 4096 bytes.
-              umma_f16(tmem_base, smem_desc(stage + (uint32_t)s * 4096, 1024, 2048), bd, L.idesc_mn, acc);
-            } else {
-              umma_f16(tmem_base, smem_desc(s_a[0] + a_off, 16, 1024), bd, L.idesc, acc);
-            }
-          }
-        }
+        issue_layer<SPLIT>(L, l == 0, tmem_base, s_a, s_image, stage);
         umma_commit(s_bar);
       }
       const bool ok = mbar_wait_bounded(s_bar, phase);
       phase ^= 1u;
       tc_fence_after();
-      if (__syncthreads_or(!ok)) {
-        if (tid == 0) atomicExch(err, 1);
+      if (wg_sync_or(wg, !ok)) {
+        if (lt == 0) atomicExch(err, 1);
         failed = true;
         break;
+      }
+      if constexpr (!SPLIT) {
+        if (l == 0) {  // layer 0 has consumed the stage: prefetch the next tile
+          if (next < ntiles) load_input<T>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
+          cp_async_commit();
+        }
       }
       const float* bias = reinterpret_cast<const float*>(base_ptr + L.bias_off);
       epilogue_dispatch<T>(L, l == p.n_layers - 1, tmem_lane, bias, s_a, out, out_ld, col0 + m, batch, m);
     }
-    cur ^= 1;
+    if (failed) break;
   }
   cp_async_wait_0();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, p.tmem_cols);
+    tmem_dealloc(*tmem_slot, p.tmem_cols);
   }
 }
 
@@ -438,21 +503,6 @@ cudaError_t launch_impl(const TcProgram& p, const void* image, const void* in, i
   return cudaGetLastError();
 }
 
-template <class T>
-int occupancy_impl(size_t smem) {
-  auto kern = tc_forward_kernel<T>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, kTcThreads, smem) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  return blocks;
-}
-
 }  // namespace
 
 cudaError_t launch_tc_forward(const TcProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
@@ -463,15 +513,6 @@ cudaError_t launch_tc_forward(const TcProgram& p, const void* image, const void*
     case 3: return launch_impl<__nv_bfloat16>(p, image, in, in_ld, out, out_ld, batch, grid, err, stream);
   }
   return cudaErrorInvalidValue;
-}
-
-int tc_forward_occupancy(const TcProgram& p) {
-  switch (p.dtype) {
-    case 0: return occupancy_impl<float>(p.smem_bytes);
-    case 2: return occupancy_impl<__half>(p.smem_bytes);
-    case 3: return occupancy_impl<__nv_bfloat16>(p.smem_bytes);
-  }
-  return 0;
 }
 
 }  // namespace ponni_b200

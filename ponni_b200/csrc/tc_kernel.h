@@ -12,7 +12,4 @@ namespace ponni_b200 {
 cudaError_t launch_tc_forward(const TcProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
                               int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream);
 
-// Resident CTAs per SM for this program (0 = does not fit).
-int tc_forward_occupancy(const TcProgram& p);
-
 }  // namespace ponni_b200

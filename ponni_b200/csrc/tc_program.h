@@ -22,7 +22,9 @@
 namespace ponni_b200 {
 
 constexpr int kTcMaxLayers = 16;
-constexpr int kTcThreads = 128;  // 4 warps: one TMEM lane quarter each
+constexpr int kTcSlots = 2;      // tiles in flight per CTA, one per warpgroup
+constexpr int kTcWgThreads = 128;  // one warpgroup: 4 warps, one TMEM lane quarter each
+constexpr int kTcThreads = kTcSlots * kTcWgThreads;
 constexpr int kTcM = 128;        // batch rows per tile (UMMA M)
 
 struct TcLayer {
@@ -36,6 +38,8 @@ struct TcLayer {
   uint32_t w_off[3];     // byte offsets of the K-major B operand parts (1, or 3 for split fp32)
   uint32_t idesc;        // UMMA instruction descriptor (A K-major)
   uint32_t idesc_mn;     // same with A MN-major (layer 0)
+  int32_t groups;        // fp32 accumulators the K steps are spread over (summed in the epilogue)
+  int32_t group_steps;   // consecutive K steps per accumulator
 };
 
 struct TcProgram {
@@ -45,8 +49,10 @@ struct TcProgram {
   int32_t nparts;        // operand parts: 3 (fp32 split into bf16 b0+b1+b2) or 1
   uint32_t image_bytes;  // staged parameter image (multiple of 16)
   uint32_t a_bytes;      // one activation operand buffer (one part)
-  uint32_t stage_bytes;  // one input staging buffer
-  uint32_t tmem_cols;    // power of two >= 32 and >= every n_pad
+  uint32_t stage_bytes;  // one input staging buffer (one per slot)
+  uint32_t slot_bytes;   // shared memory of one slot: parts x a_bytes + stage_bytes
+  uint32_t slot_cols;    // TMEM columns of one tile slot (max over layers of groups * n_pad)
+  uint32_t tmem_cols;    // allocated TMEM columns: power of two >= kTcSlots * slot_cols
   uint32_t smem_bytes;   // total dynamic shared memory requested (incl. 1 KB alignment slack)
   TcLayer layers[kTcMaxLayers];
 };
