@@ -108,6 +108,34 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+// Two 32-column accumulator loads (addresses a0, a1) completed by one wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t a0, uint32_t a1, float (&v)[32], float (&w)[32]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(a0), "r"(a1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = __uint_as_float(r[i]);
+    w[i] = __uint_as_float(r[32 + i]);
+  }
+}
+
 // 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -262,8 +290,23 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
                                          int64_t batch, int m) {
   for (int c0 = 0; c0 < L.n_pad; c0 += 32) {
     float v[32];
-    tmem_ld32(tmem_lane + (uint32_t)c0, v);
-    for (int g = 1; g < L.groups; ++g) {
+    int g = 1;
+    if (L.groups == 1) {
+      tmem_ld32(tmem_lane + (uint32_t)c0, v);
+    } else {
+      float w[32];
+      tmem_ld32x2(tmem_lane + (uint32_t)c0, tmem_lane + (uint32_t)(L.n_pad + c0), v, w);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += w[j];
+      g = 2;
+    }
+    for (; g + 1 < L.groups; g += 2) {
+      float w0[32], w1[32];
+      tmem_ld32x2(tmem_lane + (uint32_t)(g * L.n_pad + c0), tmem_lane + (uint32_t)((g + 1) * L.n_pad + c0), w0, w1);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += w0[j] + w1[j];
+    }
+    for (; g < L.groups; ++g) {
       float w[32];
       tmem_ld32(tmem_lane + (uint32_t)(g * L.n_pad + c0), w);
 #pragma unroll
@@ -457,15 +500,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       fence_proxy_async();
       tc_fence_before();
       wg_sync(wg);
+      // One elected thread issues the chain and waits for its completion;
+      // the rest of the warpgroup parks on the named barrier (no issue slots
+      // spent spinning while the other slot's epilogue runs).
+      bool ok = true;
       if (lt == 0) {
         tc_fence_after();
         issue_layer<SPLIT>(L, l == 0, tmem_base, s_a, s_image, stage);
         umma_commit(s_bar);
+        ok = mbar_wait_bounded(s_bar, phase);
       }
-      const bool ok = mbar_wait_bounded(s_bar, phase);
       phase ^= 1u;
+      const int bad = wg_sync_or(wg, !ok);
       tc_fence_after();
-      if (wg_sync_or(wg, !ok)) {
+      if (bad) {
         if (lt == 0) atomicExch(err, 1);
         failed = true;
         break;
