@@ -163,6 +163,10 @@ ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* model, int a
  * 2 = tensor-core kernel; 0 on a planning error (see last_error). */
 int ponni_b200_model_kernel(ponni_b200_model* model);
 
+/* Diagnostic counters of the tensor-core kernel (up to 7 values; per-phase
+ * cycle sums in a build with -DPONNI_B200_TC_PROFILE, zeros otherwise). */
+ponni_b200_status ponni_b200_model_diagnostics(ponni_b200_model* model, uint64_t* out, int n);
+
 /* Device-resident forward: input [num_inputs, batch] with row stride in_ld
  * elements, output [num_outputs, batch] with row stride out_ld, both device
  * pointers in the model dtype.  Enqueued on `stream`; returns without a fence

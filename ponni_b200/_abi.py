@@ -9,7 +9,9 @@ from __future__ import annotations
 import ctypes
 import os
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libponni_b200.so")
+# PONNI_B200_LIB selects another build of the library (e.g. an instrumented one).
+LIB_PATH = os.environ.get("PONNI_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                             "libponni_b200.so")
 
 # ponni_b200_status
 OK = 0
@@ -69,6 +71,7 @@ SIGNATURES = {
     "ponni_b200_model_synchronize": (_STATUS, [_P]),
     "ponni_b200_model_set_arithmetic": (_STATUS, [_P, _I]),
     "ponni_b200_model_kernel": (_I, [_P]),
+    "ponni_b200_model_diagnostics": (_STATUS, [_P, ctypes.POINTER(ctypes.c_uint64), _I]),
     "ponni_b200_forward": (_STATUS, [_P, _P, _I64, _P, _I64, _I64, _P]),
     "ponni_b200_forward_host": (_STATUS, [_P, _P, _I64, _P, _I64, _I64]),
     "ponni_b200_reallocate_internal_state": (_STATUS, [_P, _I64]),

@@ -502,9 +502,11 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
         m->tc_image_bytes = image.size();
       }
       if (!m->err_dev) {
-        e = cudaMalloc(&m->err_dev, sizeof(int));
+        // error word + 7 diagnostic counters (filled only by a build with
+        // phase profiling enabled)
+        e = cudaMalloc(&m->err_dev, 64);
         if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(error word)");
-        e = cudaMemsetAsync(m->err_dev, 0, sizeof(int), m->stream);
+        e = cudaMemsetAsync(m->err_dev, 0, 64, m->stream);
         if (e != cudaSuccess) return cuda_fail(m, e, "cudaMemset(error word)");
       }
       e = cudaMemcpyAsync(m->tc_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
@@ -769,6 +771,19 @@ ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* m, int arith
 int ponni_b200_model_kernel(ponni_b200_model* m) {
   if (!m) return 0;
   return pb_plan(m) == PONNI_B200_OK ? m->kernel : 0;
+}
+
+ponni_b200_status ponni_b200_model_diagnostics(ponni_b200_model* m, uint64_t* out, int n) {
+  if (!m || !out || n < 0) return PONNI_B200_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < n; ++i) out[i] = 0;
+  if (!m->err_dev) return PONNI_B200_OK;
+  uint64_t buf[8];
+  cudaSetDevice(m->device);
+  cudaError_t e = cudaStreamSynchronize(m->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(buf, m->err_dev, 64, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(m, e, "diagnostics read");
+  for (int i = 0; i < n && i < 7; ++i) out[i] = buf[1 + i];
+  return PONNI_B200_OK;
 }
 
 int64_t ponni_b200_scratch_bytes(const ponni_b200_model* m) {

@@ -415,6 +415,17 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
   }
 }
 
+// Optional phase timing (compiled only with -DPONNI_B200_TC_PROFILE): thread
+// 0 of each warpgroup adds the cycles of each phase to `prof` (6 counters).
+#ifdef PONNI_B200_TC_PROFILE
+#define TC_PROF_T(var) const long long var = clock64()
+#define TC_PROF_ADD(idx, t0) \
+  if (lt == 0) atomicAdd(reinterpret_cast<unsigned long long*>(err) + 1 + (idx), (unsigned long long)(clock64() - (t0)))
+#else
+#define TC_PROF_T(var)
+#define TC_PROF_ADD(idx, t0)
+#endif
+
 // --------------------------------------------------------------- kernel --
 // Two warpgroups per CTA, each owning one tile slot (operand buffers, input
 // stage, mbarrier, TMEM accumulators) and walking its own tiles; while one
@@ -477,8 +488,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   for (; tile < ntiles; tile += stride) {
     const int64_t col0 = tile * kTcM;
     const int64_t next = tile + stride;
+    TC_PROF_T(t_in);
     cp_async_wait_0();
     wg_sync(wg);
+    TC_PROF_ADD(0, t_in);
+    TC_PROF_T(t_split);
     if constexpr (SPLIT) {
       // Thread m splits column m of the staged fp32 tile into the K-major
       // bf16 operand parts of layer 0; then the stage is free for the next tile.
@@ -494,21 +508,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (next < ntiles) load_input<T>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
       cp_async_commit();
     }
+    TC_PROF_ADD(1, t_split);
     bool failed = false;
     for (int l = 0; l < p.n_layers; ++l) {
       const TcLayer& L = p.layers[l];
+      TC_PROF_T(t_bar);
       fence_proxy_async();
       tc_fence_before();
       wg_sync(wg);
       // One elected thread issues the chain and waits for its completion;
       // the rest of the warpgroup parks on the named barrier (no issue slots
       // spent spinning while the other slot's epilogue runs).
+      TC_PROF_ADD(2, t_bar);
       bool ok = true;
       if (lt == 0) {
+        TC_PROF_T(t_issue);
         tc_fence_after();
         issue_layer<SPLIT>(L, l == 0, tmem_base, s_a, s_image, stage);
         umma_commit(s_bar);
+        TC_PROF_ADD(3, t_issue);
+        TC_PROF_T(t_mma);
         ok = mbar_wait_bounded(s_bar, phase);
+        TC_PROF_ADD(4, t_mma);
       }
       phase ^= 1u;
       const int bad = wg_sync_or(wg, !ok);
@@ -525,7 +546,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       const float* bias = reinterpret_cast<const float*>(base_ptr + L.bias_off);
+      TC_PROF_T(t_epi);
       epilogue_dispatch<T>(L, l == p.n_layers - 1, tmem_lane, bias, s_a, out, out_ld, col0 + m, batch, m);
+      TC_PROF_ADD(5, t_epi);
     }
     if (failed) break;
   }
