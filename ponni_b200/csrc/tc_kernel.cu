@@ -287,8 +287,8 @@ __device__ __forceinline__ float epi_act(float v, const TcLayer& L) {
 template <class T, int ACT>
 __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t tmem_lane, const float* bias,
                                          const uint32_t* a, T* __restrict__ out, int64_t out_ld, int64_t col,
-                                         int64_t batch, int m) {
-  for (int c0 = 0; c0 < L.n_pad; c0 += 32) {
+                                         int64_t batch, int m, int half) {
+  for (int c0 = 32 * half; c0 < L.n_pad; c0 += 64) {
     float v[32];
     int g = 1;
     if (L.groups == 1) {
@@ -344,8 +344,8 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
 template <class T>
 __device__ __forceinline__ void epilogue_dispatch(const TcLayer& L, bool last, uint32_t tmem_lane, const float* bias,
                                                   const uint32_t* a, T* __restrict__ out, int64_t out_ld,
-                                                  int64_t col, int64_t batch, int m) {
-#define PONNI_TC_EPI(A) epilogue<T, A>(L, last, tmem_lane, bias, a, out, out_ld, col, batch, m)
+                                                  int64_t col, int64_t batch, int m, int half) {
+#define PONNI_TC_EPI(A) epilogue<T, A>(L, last, tmem_lane, bias, a, out, out_ld, col, batch, m, half)
   switch (L.act) {
     case EPI_RELU: PONNI_TC_EPI(EPI_RELU); break;
     case EPI_LEAKY_RELU: PONNI_TC_EPI(EPI_LEAKY_RELU); break;
@@ -375,41 +375,57 @@ __device__ __forceinline__ int wg_sync_or(int wg, int pred) {
   return r;
 }
 
-// Issue the UMMA chain of layer L for one slot (one elected thread).
+// Issue the UMMA chain of layer L for one slot (one elected thread).  The
+// descriptors of each operand are built once per layer; the K steps then only
+// add the step offset to the 14-bit start-address field (>> 4), which never
+// carries out of the field for shared-memory addresses.
 template <bool SPLIT>
 __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint32_t d_tmem, const uint32_t* s_a,
                                             uint32_t s_image, uint32_t stage) {
   const int nsteps = L.k_pad / 16;  // UMMA K = 16 for 16-bit operands (32 bytes)
-  const uint32_t b_block = (uint32_t)L.n_pad * 128;
-  for (int s = 0; s < nsteps; ++s) {
-    const uint32_t kb = (uint32_t)s >> 2, ks = (uint32_t)s & 3;
-    const uint32_t b_off = kb * b_block + ks * 32;
-    const uint32_t a_off = kb * (kTcM * 128) + ks * 32;
-    const int g = s / L.group_steps;
-    const uint32_t d = d_tmem + (uint32_t)(g * L.n_pad);
-    const uint32_t acc = (s - g * L.group_steps) > 0 ? 1u : 0u;
-    if constexpr (SPLIT) {
-      uint64_t ad[3], bd[3];
+  const uint64_t b_step_kb = (uint64_t)L.n_pad * 8;  // (n_pad * 128) >> 4 per K block
+  const uint32_t gstep = (uint32_t)L.group_steps, n_pad = (uint32_t)L.n_pad;
+  const uint32_t idesc = L.idesc;
+  uint32_t d = d_tmem, in_group = 0;
+  if constexpr (SPLIT) {
+    uint64_t a0[3], b0[3];
 #pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        ad[q] = smem_desc(s_a[q] + a_off, 16, 1024);
-        bd[q] = smem_desc(s_image + L.w_off[q] + b_off, 16, 1024);
-      }
+    for (int q = 0; q < 3; ++q) {
+      a0[q] = smem_desc(s_a[q], 16, 1024);
+      b0[q] = smem_desc(s_image + L.w_off[q], 16, 1024);
+    }
+    for (int s = 0; s < nsteps; ++s) {
+      const uint64_t ao = (uint64_t)(s >> 2) * 1024 + (uint64_t)(s & 3) * 2;
+      const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
+      const uint32_t acc = in_group ? 1u : 0u;
       // smallest products first
-      umma_f16(d, ad[1], bd[1], L.idesc, acc);
-      umma_f16(d, ad[0], bd[2], L.idesc, 1u);
-      umma_f16(d, ad[2], bd[0], L.idesc, 1u);
-      umma_f16(d, ad[0], bd[1], L.idesc, 1u);
-      umma_f16(d, ad[1], bd[0], L.idesc, 1u);
-      umma_f16(d, ad[0], bd[0], L.idesc, 1u);
+      umma_f16(d, a0[1] + ao, b0[1] + bo, idesc, acc);
+      umma_f16(d, a0[0] + ao, b0[2] + bo, idesc, 1u);
+      umma_f16(d, a0[2] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16(d, a0[0] + ao, b0[1] + bo, idesc, 1u);
+      umma_f16(d, a0[1] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16(d, a0[0] + ao, b0[0] + bo, idesc, 1u);
+      if (++in_group == gstep) {
+        in_group = 0;
+        d += n_pad;
+      }
+    }
+  } else {
+    const uint64_t b0 = smem_desc(s_image + L.w_off[0], 16, 1024);
+    if (layer0) {
+      // The staged input tile is the MN-major layer-0 operand: one K step =
+      // 32 bytes of K for 128 rows = 4096 bytes.
+      const uint64_t a0 = smem_desc(stage, 1024, 2048);
+      for (int s = 0; s < nsteps; ++s) {
+        const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
+        umma_f16(d, a0 + (uint64_t)s * 256, b0 + bo, L.idesc_mn, s > 0 ? 1u : 0u);
+      }
     } else {
-      const uint64_t bd = smem_desc(s_image + L.w_off[0] + b_off, 16, 1024);
-      if (layer0) {
-        // The staged input tile is the MN-major layer-0 operand: one K step
-        // = 32 bytes of K for 128 rows = 4096 bytes.
-        umma_f16(d, smem_desc(stage + (uint32_t)s * 4096, 1024, 2048), bd, L.idesc_mn, acc);
-      } else {
-        umma_f16(d, smem_desc(s_a[0] + a_off, 16, 1024), bd, L.idesc, acc);
+      const uint64_t a0 = smem_desc(s_a[0], 16, 1024);
+      for (int s = 0; s < nsteps; ++s) {
+        const uint64_t ao = (uint64_t)(s >> 2) * 1024 + (uint64_t)(s & 3) * 2;
+        const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
+        umma_f16(d, a0 + ao, b0 + bo, idesc, s > 0 ? 1u : 0u);
       }
     }
   }
@@ -427,9 +443,10 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
 #endif
 
 // --------------------------------------------------------------- kernel --
-// Two warpgroups per CTA, each owning one tile slot (operand buffers, input
-// stage, mbarrier, TMEM accumulators) and walking its own tiles; while one
-// warpgroup runs its epilogue the tensor core works on the other's chain.
+// Two slots per CTA, each run by 8 warps (4 TMEM lane quarters x 2 column
+// halves) that own the slot's operand buffers, input stage, mbarrier and TMEM
+// accumulators and walk their own tiles; while one slot runs its epilogue the
+// tensor core works on the other's chain.
 template <class T>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_forward_kernel(const __grid_constant__ TcProgram p, const unsigned char* __restrict__ image,
@@ -442,7 +459,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzle atoms need 1024-byte alignment
   unsigned char* base_ptr = smem_raw + (base - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int wg = warp >> 2, lt = tid & (kTcWgThreads - 1);
+  const int wg = warp >> 3, lt = tid & (kTcWgThreads - 1);
+  const int half = (warp >> 2) & 1;  // column half of the epilogue this warp handles
   const uint32_t s_image = base;
   const uint32_t s_slot = s_image + p.image_bytes + (uint32_t)wg * p.slot_bytes;
   uint32_t s_a[3];
@@ -498,7 +516,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // bf16 operand parts of layer 0; then the stage is free for the next tile.
       const int k0 = p.layers[0].k_pad;
       const float* st = reinterpret_cast<const float*>(base_ptr + (stage - base));
-      for (int f = 0; f < k0; f += 8) {
+      for (int f = 8 * half; f < k0; f += 16) {
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = st[(f + e) * kTcM + m];
@@ -547,7 +565,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const float* bias = reinterpret_cast<const float*>(base_ptr + L.bias_off);
       TC_PROF_T(t_epi);
-      epilogue_dispatch<T>(L, l == p.n_layers - 1, tmem_lane, bias, s_a, out, out_ld, col0 + m, batch, m);
+      epilogue_dispatch<T>(L, l == p.n_layers - 1, tmem_lane, bias, s_a, out, out_ld, col0 + m, batch, m, half);
       TC_PROF_ADD(5, t_epi);
     }
     if (failed) break;

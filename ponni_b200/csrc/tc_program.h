@@ -22,8 +22,11 @@
 namespace ponni_b200 {
 
 constexpr int kTcMaxLayers = 16;
-constexpr int kTcSlots = 2;      // tiles in flight per CTA, one per warpgroup
-constexpr int kTcWgThreads = 128;  // one warpgroup: 4 warps, one TMEM lane quarter each
+#ifndef PONNI_B200_TC_SLOTS
+#define PONNI_B200_TC_SLOTS 2
+#endif
+constexpr int kTcSlots = PONNI_B200_TC_SLOTS;  // tiles in flight per CTA, one per warpgroup
+constexpr int kTcWgThreads = 256;  // threads of one slot: 8 warps = 4 TMEM lane quarters x 2 column halves
 constexpr int kTcThreads = kTcSlots * kTcWgThreads;
 constexpr int kTcM = 128;        // batch rows per tile (UMMA M)
 
