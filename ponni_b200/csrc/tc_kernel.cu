@@ -164,6 +164,10 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+#ifdef PONNI_B200_TC_PROFILE
+__device__ int* prof_ptr;
+#endif
+
 // ------------------------------------------------------------ helpers ----
 template <class T> struct Store;
 template <> struct Store<float> {
@@ -290,6 +294,9 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
                                          int64_t batch, int m, int half) {
   for (int c0 = 32 * half; c0 < L.n_pad; c0 += 64) {
     float v[32];
+#ifdef PONNI_B200_TC_PROFILE
+    const long long t_ld = clock64();
+#endif
     int g = 1;
     if (L.groups == 1) {
       tmem_ld32(tmem_lane + (uint32_t)c0, v);
@@ -312,6 +319,10 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] += w[j];
     }
+#ifdef PONNI_B200_TC_PROFILE
+    if ((threadIdx.x & (kTcWgThreads - 1)) == 0)
+      atomicAdd(reinterpret_cast<unsigned long long*>(prof_ptr) + 7, (unsigned long long)(clock64() - t_ld));
+#endif
     if (L.has_bias) {
       const float4* b4 = reinterpret_cast<const float4*>(bias + c0);  // zero-padded to 32 columns
 #pragma unroll
@@ -323,10 +334,15 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
         v[4 * q + 3] += b.w;
       }
     }
+    if (c0 + 32 <= L.nout) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float x = epi_act<ACT>(v[j], L);
-      v[j] = c0 + j < L.nout ? x : 0.0f;
+      for (int j = 0; j < 32; ++j) v[j] = epi_act<ACT>(v[j], L);
+    } else {  // the chunk holding the padding columns: force them to zero
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float x = epi_act<ACT>(v[j], L);
+        v[j] = c0 + j < L.nout ? x : 0.0f;
+      }
     }
     if (last) {
       if (col < batch) {
@@ -474,6 +490,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int64_t ntiles = (batch + kTcM - 1) / kTcM;
   if ((int64_t)blockIdx.x * kTcSlots >= ntiles) return;
+#ifdef PONNI_B200_TC_PROFILE
+  if (tid == 0) prof_ptr = err;
+#endif
 
   // ---- set-up (whole CTA): TMEM, mbarriers, zeroed stages, parameter image ----
   if (warp == 0) tmem_alloc(s_tmem, p.tmem_cols);
