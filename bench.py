@@ -37,8 +37,8 @@ def parse():
     p.add_argument("--batch", type=int, default=0, help="override per-GPU batch (default: the config's)")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--arith", default="auto", choices=["auto", "reference", "tensor"],
-                   help="kernel selection (ponni_b200_model_set_arithmetic)")
+    p.add_argument("--arith", default="", choices=["", "auto", "reference", "tensor"],
+                   help="kernel selection (ponni_b200_model_set_arithmetic); default: the config's")
     return p.parse_args()
 
 
@@ -166,7 +166,9 @@ def main():
     dev = torch.device(f"cuda:{local}")
     B = cfg.batch
     nin, nout = cfg.layers[0].num_inputs, cfg.layers[-1].num_outputs
-    arith = {"auto": pb._abi.ARITH_AUTO, "reference": pb._abi.ARITH_REFERENCE, "tensor": pb._abi.ARITH_TENSOR}[args.arith]
+    arith_name = args.arith or cfg.arith
+    arith = {"auto": pb._abi.ARITH_AUTO, "reference": pb._abi.ARITH_REFERENCE,
+             "tensor": pb._abi.ARITH_TENSOR}[arith_name]
     model = pb.Inference(cfg.layers, dtype=cfg.dtype, device=local, arithmetic=arith)
     kernel_name = {1: "tile_forward_kernel (SIMT)", 2: "tc_forward_kernel (tcgen05)"}[model.kernel()]
     tdt = model.torch_dtype()
@@ -201,18 +203,25 @@ def main():
     pk, pk_src = peaks()
     launch_s = (ms / args.steps) / 1e3
     sm_mhz = clk.get("sm_mhz") or pk.get("sm_max_mhz", 1965.0)
+    kernel = model.kernel()
     if cfg.bound == "hbm":
         roof = {"bound": "hbm", "achieved": cfg.bytes_per_sample * B / launch_s / 1e9, "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "peak_source": f"hbm_gbs ({pk_src})"}
-    elif cfg.dtype in (pb.F32, pb.F64):
+    elif kernel == pb._abi.KERNEL_TENSOR:
+        # fp32 models run six bf16 MMAs per multiply-add (exact 3-way operand
+        # split), so their tensor roofline is a sixth of the bf16 peak.
+        passes = 6 if cfg.dtype == pb.F32 else 1
+        roof = {"bound": "tensor", "achieved": cfg.flops_per_sample * B / launch_s / 1e12,
+                "peak": pk["bf16_tflops"] / passes, "unit": "TFLOP/s",
+                "peak_source": f"bf16_tflops ({pk_src})" + (" / 6 (six bf16 MMAs per fp32 multiply-add)"
+                                                             if passes == 6 else "")}
+    else:
         lanes = 128 if cfg.dtype == pb.F32 else 64
         roof = {"bound": "compute", "achieved": cfg.flops_per_sample * B / launch_s / 1e12,
                 "peak": 148 * lanes * 2 * sm_mhz * 1e6 / 1e12, "unit": "TFLOP/s",
                 "peak_source": f"SIMT FMA peak (148 SMs x {lanes} lanes x 2) at the sampled median SM clock "
                                f"{sm_mhz:.0f} MHz; no measured fp32 peak exists"}
-    else:
-        roof = {"bound": "tensor", "achieved": cfg.flops_per_sample * B / launch_s / 1e12,
-                "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "peak_source": f"bf16_tflops ({pk_src})"}
+    roof["hbm_gbs_achieved"] = cfg.bytes_per_sample * B / launch_s / 1e9
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["traffic"] = None
     tpath = os.path.join(ROOT, "profiles", f"traffic_{cfg.name}.json")
@@ -259,7 +268,7 @@ def main():
             "config": {"workload": cfg.name, "batch_per_gpu": B, "global_batch": world * B, "nin": nin,
                        "nout": nout, "parallelism": f"column shards x{world}, no collective",
                        "l2": "inputs larger than L2 (no flush)"},
-            "kernel": kernel_name, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,
+            "kernel": kernel_name, "arithmetic": arith_name, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,
         }), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -147,12 +147,14 @@ ponni_b200_status ponni_b200_model_synchronize(ponni_b200_model* model);
 
 /* Arithmetic / kernel selection (no counterpart in the reference, which has
  * one Kokkos kernel):
- *   AUTO      -- tensor cores (tcgen05) for dense chains of fp32 (3xTF32,
- *                fp32-level accuracy), fp16 and bf16 (fp32 accumulation)
- *                models that fit the kernel; the tile kernel otherwise;
+ *   AUTO      -- fp32 models: tensor cores (tcgen05) for dense chains that
+ *                fit the kernel, on an exact three-way bf16 split of every
+ *                operand (fp32-level accuracy); fp16/bf16 models: the tile
+ *                kernel with the reference's per-operation rounding;
  *   REFERENCE -- always the tile kernel: the reference's arithmetic order
  *                (fp16/bf16 accumulate in the model type, per operation);
- *   TENSOR    -- require the tensor-core kernel (forward fails otherwise). */
+ *   TENSOR    -- require the tensor-core kernel (forward fails otherwise);
+ *                fp16/bf16 models then accumulate in fp32. */
 typedef enum {
   PONNI_B200_ARITH_AUTO = 0,
   PONNI_B200_ARITH_REFERENCE = 1,

@@ -36,6 +36,7 @@ class Config:
     bytes_per_sample: int = 0
     bound: str = "hbm"
     description: str = ""
+    arith: str = "auto"  # cfg3/cfg5 are specified with fp32 accumulation: "tensor"
 
 
 def _dense_flops(layers) -> int:
@@ -75,14 +76,14 @@ def _emulator_layers(rng):
 def cfg2(batch: int = 1 << 24) -> Config:
     rng = np.random.default_rng(WEIGHT_SEED)
     return _finish(Config("cfg2_emulator_30_64x3_10_fp32", _emulator_layers(rng), _abi.F32, batch,
-                          bound="compute", description="Column-physics emulator MLP fp32"))
+                          bound="tensor", description="Column-physics emulator MLP fp32"))
 
 
 def cfg3(batch: int = 1 << 26) -> Config:
     rng = np.random.default_rng(WEIGHT_SEED)
     return _finish(Config("cfg3_emulator_30_64x3_10_fp16", _emulator_layers(rng), _abi.F16, batch,
-                          input_dist="uniform", lo=-2.0, hi=2.0, bound="compute",
-                          description="Column-physics emulator MLP fp16"))
+                          input_dist="uniform", lo=-2.0, hi=2.0, bound="tensor", arith="tensor",
+                          description="Column-physics emulator MLP fp16, fp32 accumulate"))
 
 
 def cfg4(batch: int = 1 << 25) -> Config:
@@ -97,7 +98,7 @@ def cfg4(batch: int = 1 << 25) -> Config:
         layers += [L.Save_State(128, 0), L.LayerNorm(128), L.Matvec(glorot_u(128, 128)), L.Bias(np.zeros(128)),
                    L.Gelu(128), L.Matvec(glorot_u(128, 128)), L.Bias(np.zeros(128)), L.Binop_Add(128, 0)]
     layers += [L.Matvec(glorot_u(128, 8)), L.Bias(np.zeros(8))]
-    return _finish(Config("cfg4_resmlp_16_128_ln_gelu_8_fp32", layers, _abi.F32, batch, bound="compute",
+    return _finish(Config("cfg4_resmlp_16_128_ln_gelu_8_fp32", layers, _abi.F32, batch, bound="tensor",
                           description="Residual MLP with LayerNorm/GELU fp32"))
 
 
@@ -111,8 +112,8 @@ def cfg5(batch: int = 1 << 27) -> Config:
         layers.append(L.Bias(rng.normal(0.0, 0.01, nout)))
         if i < 5:
             layers.append(L.Silu(nout))
-    return _finish(Config("cfg5_wide_64_256x5_32_bf16", layers, _abi.BF16, batch, bound="tensor",
-                          description="Wide dense chain bf16"))
+    return _finish(Config("cfg5_wide_64_256x5_32_bf16", layers, _abi.BF16, batch, bound="tensor", arith="tensor",
+                          description="Wide dense chain bf16, fp32 accumulate"))
 
 
 ALL = {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4, "cfg5": cfg5}

@@ -490,7 +490,12 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
   // Tensor-core dense-chain kernel, when allowed and eligible.
   m->kernel = 1;
   m->tc_why.clear();
-  if (m->arithmetic != PONNI_B200_ARITH_REFERENCE) {
+  // AUTO: tensor cores for fp32 models (fp32-accurate split arithmetic);
+  // fp16/bf16 models keep the reference's per-operation rounding unless the
+  // caller asks for fp32 accumulation (ARITH_TENSOR).
+  const bool want_tc = m->arithmetic == PONNI_B200_ARITH_TENSOR ||
+                       (m->arithmetic == PONNI_B200_ARITH_AUTO && m->dtype == PONNI_B200_F32);
+  if (want_tc) {
     std::vector<unsigned char> image;
     if (tc_plan(m, m->tcp, image, m->tc_why)) {
       if (image.size() > m->tc_image_bytes) {
@@ -712,7 +717,7 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
   cudaError_t e;
   if (m->kernel == 2) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
-    const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + kTcSlots - 1) / kTcSlots);
+    const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + m->tcp.slots - 1) / m->tcp.slots);
     e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
   } else {
     const int64_t ntiles = (batch + m->prog.bt - 1) / m->prog.bt;

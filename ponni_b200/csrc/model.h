@@ -52,7 +52,7 @@ struct ponni_b200_model {
   int num_sms = 0;
 
   // Tensor-core dense-chain kernel (planned when eligible and allowed).
-  int arithmetic = PONNI_B200_ARITH_REFERENCE;  // ponni_b200_arithmetic requested
+  int arithmetic = PONNI_B200_ARITH_AUTO;  // ponni_b200_arithmetic requested
   int kernel = 0;       // 1 tile (SIMT) kernel, 2 tensor-core kernel; 0 = not planned yet
   ponni_b200::TcProgram tcp;
   void* tc_image_dev = nullptr;

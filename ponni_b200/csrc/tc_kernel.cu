@@ -374,7 +374,7 @@ __device__ __forceinline__ void epilogue_dispatch(const TcLayer& L, bool last, u
 #undef PONNI_TC_EPI
 }
 
-// Named barrier over one warpgroup (ids 1..kTcSlots; 0 is __syncthreads).
+// Named barrier over one slot's threads (ids 1..slots; 0 is __syncthreads).
 __device__ __forceinline__ void wg_sync(int wg) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(wg + 1), "r"(kTcWgThreads) : "memory");
 }
@@ -464,7 +464,7 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
 // accumulators and walk their own tiles; while one slot runs its epilogue the
 // tensor core works on the other's chain.
 template <class T>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcMaxThreads, 1)
     tc_forward_kernel(const __grid_constant__ TcProgram p, const unsigned char* __restrict__ image,
                       const T* __restrict__ in, int64_t in_ld, T* __restrict__ out, int64_t out_ld, int64_t batch,
                       int in_vec, int* __restrict__ err) {
@@ -483,13 +483,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
   for (int q = 0; q < 3; ++q) s_a[q] = s_slot + (uint32_t)(q < NP ? q : 0) * p.a_bytes;
   const uint32_t stage = s_slot + (uint32_t)NP * p.a_bytes;
-  const uint32_t s_bars = s_image + p.image_bytes + kTcSlots * p.slot_bytes;
+  const int nslots = p.slots, nthreads = nslots * kTcWgThreads;
+  const uint32_t s_bars = s_image + p.image_bytes + (uint32_t)nslots * p.slot_bytes;
   const uint32_t s_bar = s_bars + 8u * (uint32_t)wg;
-  const uint32_t s_tmem = s_bars + 8u * kTcSlots;
+  const uint32_t s_tmem = s_bars + 8u * kTcMaxSlots;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(base_ptr + (s_tmem - base));
 
   const int64_t ntiles = (batch + kTcM - 1) / kTcM;
-  if ((int64_t)blockIdx.x * kTcSlots >= ntiles) return;
+  if ((int64_t)blockIdx.x * nslots >= ntiles) return;
 #ifdef PONNI_B200_TC_PROFILE
   if (tid == 0) prof_ptr = err;
 #endif
@@ -497,14 +498,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // ---- set-up (whole CTA): TMEM, mbarriers, zeroed stages, parameter image ----
   if (warp == 0) tmem_alloc(s_tmem, p.tmem_cols);
   if (tid == 0) {
-    for (int q = 0; q < kTcSlots; ++q) mbar_init(s_bars + 8u * q, 1);
+    for (int q = 0; q < nslots; ++q) mbar_init(s_bars + 8u * q, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  for (int q = 0; q < kTcSlots; ++q) {
+  for (int q = 0; q < nslots; ++q) {
     uint4* z = reinterpret_cast<uint4*>(base_ptr + (s_image + p.image_bytes + q * p.slot_bytes + NP * p.a_bytes - base));
-    for (int i = tid; i < (int)(p.stage_bytes / 16); i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < (int)(p.stage_bytes / 16); i += nthreads) z[i] = make_uint4(0, 0, 0, 0);
   }
-  for (uint32_t i = tid; i < p.image_bytes / 16; i += kTcThreads) cp_async16(s_image + i * 16, image + i * 16, 16);
+  for (uint32_t i = tid; i < p.image_bytes / 16; i += nthreads) cp_async16(s_image + i * 16, image + i * 16, 16);
   cp_async_commit();
   cp_async_wait_0();
   tc_fence_before();
@@ -515,8 +516,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int m = (warp & 3) * 32 + lane;  // this thread's batch row in its slot's tile
 
   // ---- per-warpgroup tile loop ----
-  const int64_t stride = (int64_t)gridDim.x * kTcSlots;
-  int64_t tile = (int64_t)blockIdx.x * kTcSlots + wg;
+  const int64_t stride = (int64_t)gridDim.x * nslots;
+  int64_t tile = (int64_t)blockIdx.x * nslots + wg;
   uint32_t phase = 0;
   if (tile < ntiles) {
     load_input<T>(stage, in, in_ld, p.nin, tile * kTcM, batch, in_vec != 0, lt);
@@ -605,7 +606,7 @@ cudaError_t launch_impl(const TcProgram& p, const void* image, const void* in, i
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
   if (e != cudaSuccess) return e;
   const bool vec = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && ((in_ld * (int64_t)sizeof(T)) % 16 == 0);
-  kern<<<grid, kTcThreads, p.smem_bytes, stream>>>(p, static_cast<const unsigned char*>(image),
+  kern<<<grid, p.slots * kTcWgThreads, p.smem_bytes, stream>>>(p, static_cast<const unsigned char*>(image),
                                                     static_cast<const T*>(in), in_ld, static_cast<T*>(out), out_ld,
                                                     batch, vec ? 1 : 0, err);
   return cudaGetLastError();

@@ -96,22 +96,6 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
     L.has_bias = blocks[l].bias ? 1 : 0;
     L.idesc = make_idesc(dt, L.n_pad, false);
     L.idesc_mn = make_idesc(dt, L.n_pad, true);
-    // fp32 (split) models spread the K steps over separate accumulators
-    // summed in the epilogue (PONNI_B200_TC_GROUP_STEPS steps each; default 1):
-    // the tensor core's fp32 accumulation truncates, so shorter accumulation
-    // chains keep the result fp32-accurate.
-    const int nsteps = L.k_pad / 16;
-    int gs = nsteps;
-    if (split) {
-      gs = 1;
-      if (const char* env = getenv("PONNI_B200_TC_GROUP_STEPS")) gs = std::max(1, atoi(env));
-    }
-    // Fewer, longer accumulation chains when the accumulators would not fit
-    // in tensor memory (512 columns for both slots).
-    while (gs < nsteps && kTcSlots * round_up((int64_t)((nsteps + gs - 1) / gs) * L.n_pad, 32) > 512) ++gs;
-    L.group_steps = std::min(gs, nsteps);
-    L.groups = (nsteps + L.group_steps - 1) / L.group_steps;
-    max_npad = std::max(max_npad, L.groups * L.n_pad);
     if (l + 1 < blocks.size()) max_w32 = std::max(max_w32, (int)round_up(L.n_pad, 32));
   }
   // Image: biases first (float, padded to 32 columns), then weights at
@@ -167,21 +151,41 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   p.stage_bytes = split ? (uint32_t)k0 * kTcM * 4 : (uint32_t)(k0 / 8) * 2048;
   const uint32_t a_kmajor = (uint32_t)((max_w32 * 2 + 127) / 128) * kTcM * 128;
   p.a_bytes = std::max(a_kmajor, 1024u);
-  p.slot_cols = (uint32_t)round_up(max_npad, 32);
-  uint32_t cols = 32;
-  while (cols < kTcSlots * p.slot_cols) cols <<= 1;
-  if (cols > 512) {
-    why = "accumulators exceed tensor memory";
-    return false;
-  }
-  p.tmem_cols = cols;
   p.slot_bytes = p.a_bytes * (uint32_t)nparts + p.stage_bytes;
-  p.smem_bytes = 1024 + p.image_bytes + kTcSlots * p.slot_bytes + 64;
-  if (p.smem_bytes > 227 * 1024) {
-    why = "weights and operand tiles exceed shared memory";
-    return false;
+  // Two tile slots when shared and tensor memory allow, else one.
+  for (int slots = kTcMaxSlots; slots >= 1; --slots) {
+    const int col_budget = 512 / slots;
+    max_npad = 0;
+    for (int l = 0; l < p.n_layers; ++l) {
+      TcLayer& L = p.layers[l];
+      // fp32 (split) models spread the K steps over separate accumulators
+      // summed in the epilogue (PONNI_B200_TC_GROUP_STEPS steps each; default
+      // 1): the tensor core's fp32 accumulation truncates, so shorter chains
+      // keep the result fp32-accurate.  Longer chains when the accumulators
+      // would not fit in tensor memory.
+      const int nsteps = L.k_pad / 16;
+      int gs = nsteps;
+      if (split) {
+        gs = 1;
+        if (const char* env = getenv("PONNI_B200_TC_GROUP_STEPS")) gs = std::max(1, atoi(env));
+      }
+      while (gs < nsteps && round_up((int64_t)((nsteps + gs - 1) / gs) * L.n_pad, 32) > col_budget) ++gs;
+      L.group_steps = std::min(gs, nsteps);
+      L.groups = (nsteps + L.group_steps - 1) / L.group_steps;
+      max_npad = std::max(max_npad, L.groups * L.n_pad);
+    }
+    p.slot_cols = (uint32_t)round_up(max_npad, 32);
+    uint32_t cols = 32;
+    while (cols < (uint32_t)slots * p.slot_cols) cols <<= 1;
+    p.smem_bytes = 1024 + p.image_bytes + (uint32_t)slots * p.slot_bytes + 64;
+    if (cols <= 512 && p.smem_bytes <= 227 * 1024) {
+      p.tmem_cols = cols;
+      p.slots = slots;
+      return true;
+    }
   }
-  return true;
+  why = "weights and operand tiles exceed shared memory";
+  return false;
 }
 
 }  // namespace ponni_b200

@@ -22,12 +22,9 @@
 namespace ponni_b200 {
 
 constexpr int kTcMaxLayers = 16;
-#ifndef PONNI_B200_TC_SLOTS
-#define PONNI_B200_TC_SLOTS 2
-#endif
-constexpr int kTcSlots = PONNI_B200_TC_SLOTS;  // tiles in flight per CTA, one per warpgroup
+constexpr int kTcMaxSlots = 2;   // tiles in flight per CTA (TcProgram::slots = 1 or 2)
 constexpr int kTcWgThreads = 256;  // threads of one slot: 8 warps = 4 TMEM lane quarters x 2 column halves
-constexpr int kTcThreads = kTcSlots * kTcWgThreads;
+constexpr int kTcMaxThreads = kTcMaxSlots * kTcWgThreads;
 constexpr int kTcM = 128;        // batch rows per tile (UMMA M)
 
 struct TcLayer {
@@ -55,7 +52,8 @@ struct TcProgram {
   uint32_t stage_bytes;  // one input staging buffer (one per slot)
   uint32_t slot_bytes;   // shared memory of one slot: parts x a_bytes + stage_bytes
   uint32_t slot_cols;    // TMEM columns of one tile slot (max over layers of groups * n_pad)
-  uint32_t tmem_cols;    // allocated TMEM columns: power of two >= kTcSlots * slot_cols
+  uint32_t tmem_cols;    // allocated TMEM columns: power of two >= slots * slot_cols
+  int32_t slots;         // tile slots per CTA (1 or 2); the CTA runs slots * kTcWgThreads threads
   uint32_t smem_bytes;   // total dynamic shared memory requested (incl. 1 KB alignment slack)
   TcLayer layers[kTcMaxLayers];
 };

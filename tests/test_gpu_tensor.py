@@ -70,8 +70,8 @@ def test_tc_cfg3_16bit(dtype, batch, oracle_lib):
 @pytest.mark.parametrize("dtype", [pb.F32, pb.F16, pb.BF16])
 def test_tc_odd_widths_all_activations(dtype, oracle_lib):
     rng = np.random.default_rng(11)
-    # fp32 operands take three bf16 parts: keep the widths within shared memory
-    dims = [3, 17, 40, 130, 9, 64, 5] if dtype == pb.F32 else [3, 17, 40, 130, 9, 256, 5]
+    # fp32 operands take three bf16 parts: these widths run with one tile slot
+    dims = [3, 17, 40, 96, 9, 64, 5] if dtype == pb.F32 else [3, 17, 40, 130, 9, 256, 5]
     acts = [pb.Relu, pb.Silu, pb.Gelu, pb.Tanh, pb.Sigmoid, lambda n: pb.LeakyRelu(n, 0.2)]
     layers = []
     for i in range(len(dims) - 1):
@@ -99,6 +99,14 @@ def test_tc_strided_misaligned(oracle_lib):
     m.synchronize()
     check(out_big[:, 1:1001].cpu().numpy(), oracle_lib.forward(cfg.layers, cfg.dtype, x), cfg.dtype, cfg.layers, x)
     assert torch.isnan(out_big[:, 0]).all() and torch.isnan(out_big[:, 1001:]).all()
+
+
+def test_auto_policy():
+    # fp32 dense chains run on tensor cores by default; 16-bit models keep the
+    # reference's per-operation rounding unless fp32 accumulation is requested.
+    assert pb.Inference(configs.cfg2(batch=10).layers, dtype=pb.F32).kernel() == pb._abi.KERNEL_TENSOR
+    assert pb.Inference(configs.cfg3(batch=10).layers, dtype=pb.F16).kernel() == pb._abi.KERNEL_TILE
+    assert pb.Inference(configs.cfg2(batch=10).layers, dtype=pb.F64).kernel() == pb._abi.KERNEL_TILE
 
 
 def test_tc_ineligible_falls_back_or_errors():
