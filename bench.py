@@ -170,6 +170,12 @@ def main():
     arith = {"auto": pb._abi.ARITH_AUTO, "reference": pb._abi.ARITH_REFERENCE,
              "tensor": pb._abi.ARITH_TENSOR}[arith_name]
     model = pb.Inference(cfg.layers, dtype=cfg.dtype, device=local, arithmetic=arith)
+    try:
+        model.kernel()
+    except pb.PonniError as e:  # the config's kernel is unavailable for this model: say so, use the default
+        print(f"note: {arith_name} arithmetic unavailable ({e.message}); using the default", file=sys.stderr)
+        arith_name = "auto"
+        model.set_arithmetic(pb._abi.ARITH_AUTO)
     kernel_name = {1: "tile_forward_kernel (SIMT)", 2: "tc_forward_kernel (tcgen05)"}[model.kernel()]
     tdt = model.torch_dtype()
     x = torch.empty((nin, B), dtype=tdt, device=dev)

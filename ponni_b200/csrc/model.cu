@@ -493,8 +493,12 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
   // AUTO: tensor cores for fp32 models (fp32-accurate split arithmetic);
   // fp16/bf16 models keep the reference's per-operation rounding unless the
   // caller asks for fp32 accumulation (ARITH_TENSOR).
+  // Narrow chains (every layer at most 16 wide) are bandwidth-bound and stay
+  // on the tile kernel under AUTO.
+  int widest = 0;
+  for (const auto& L : m->layers) widest = std::max(widest, std::max(L.d.num_inputs, L.d.num_outputs));
   const bool want_tc = m->arithmetic == PONNI_B200_ARITH_TENSOR ||
-                       (m->arithmetic == PONNI_B200_ARITH_AUTO && m->dtype == PONNI_B200_F32);
+                       (m->arithmetic == PONNI_B200_ARITH_AUTO && m->dtype == PONNI_B200_F32 && widest > 16);
   if (want_tc) {
     std::vector<unsigned char> image;
     if (tc_plan(m, m->tcp, image, m->tc_why)) {
