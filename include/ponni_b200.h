@@ -183,6 +183,29 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* model, const void* input,
 ponni_b200_status ponni_b200_forward_host(ponni_b200_model* model, const void* input, int64_t in_ld,
                                           void* output, int64_t out_ld, int64_t batch);
 
+/* Host-buffer forward that allocates nothing (no counterpart in the
+ * reference).  For callers that cannot allocate device memory while they
+ * run inference -- an application that gives all of its GPU memory to its
+ * own pool at start-up, a solver whose memory budget is fixed before its
+ * time loop, or code where a cudaMalloc would synchronise the device at the
+ * wrong moment.  Same arguments and result as ponni_b200_forward_host, but
+ * the input and output are staged in a static 64 MiB device array that the
+ * library holds on every GPU that loads it, until the process exits, and the
+ * copies and the kernel run on the model's own stream (no second stream).
+ *  - The model must already be prepared: call ponni_b200_model_kernel() once
+ *    (it uploads the parameters, which allocates) before the first call, and
+ *    again after changing parameters; otherwise this returns an error.
+ *  - batch * (num_inputs + num_outputs) * element size must fit in 64 MiB;
+ *    larger batches are rejected with an error naming the limit (split them).
+ *  - The first call on a device looks up the array's device address; make
+ *    that first call before any stream capture.
+ *  - Every call, from any model on the same device, shares the array: calls
+ *    that overlap on the GPU (other threads, other streams) race.  Each call
+ *    overwrites the staged input and output it uses, so nothing needs to be
+ *    cleared between calls. */
+ponni_b200_status ponni_b200_forward_host_static(ponni_b200_model* model, const void* input, int64_t in_ld,
+                                                 void* output, int64_t out_ld, int64_t batch);
+
 /* Scratch capacity, reference semantics: grows on demand to the largest batch
  * seen, shrinks exactly on an explicit call, 0 releases. */
 ponni_b200_status ponni_b200_reallocate_internal_state(ponni_b200_model* model, int64_t batch);

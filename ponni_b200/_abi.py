@@ -74,6 +74,7 @@ SIGNATURES = {
     "ponni_b200_model_diagnostics": (_STATUS, [_P, ctypes.POINTER(ctypes.c_uint64), _I]),
     "ponni_b200_forward": (_STATUS, [_P, _P, _I64, _P, _I64, _I64, _P]),
     "ponni_b200_forward_host": (_STATUS, [_P, _P, _I64, _P, _I64, _I64]),
+    "ponni_b200_forward_host_static": (_STATUS, [_P, _P, _I64, _P, _I64, _I64]),
     "ponni_b200_reallocate_internal_state": (_STATUS, [_P, _I64]),
     "ponni_b200_internal_state_capacity": (_I64, [_P]),
     "ponni_b200_planned_temporary_size": (_I, [_P, _I]),

@@ -5,6 +5,8 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
+#include <string>
 
 #include "model.h"
 
@@ -154,3 +156,87 @@ ponni_b200_status ponni_b200_forward_host(ponni_b200_model* m, const void* input
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Host-buffer forward without any device allocation.
+//
+// Some callers cannot allocate device memory while they run inference: an
+// application that hands all of its GPU memory to its own pool or allocator
+// at start-up, a process whose allocation budget is fixed before a
+// time-stepping loop begins, or code where a cudaMalloc would synchronise
+// the device at the wrong moment.  For them this entry point stages the
+// host input and output in a static device array that the library holds for
+// the life of the process (on every GPU that loads it), instead of the
+// cudaMalloc'd staging of ponni_b200_forward_host.
+namespace {
+
+constexpr size_t kStaticStageBytes = (size_t)64 << 20;  // 64 MiB per GPU
+static __device__ __align__(256) unsigned char g_static_stage[kStaticStageBytes];
+
+// Device address of g_static_stage, looked up once per device.
+constexpr int kMaxDevices = 64;
+void* g_static_stage_ptr[kMaxDevices] = {nullptr};
+std::mutex g_static_stage_mutex;
+
+cudaError_t static_stage_address(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_static_stage_mutex);
+  if (!g_static_stage_ptr[device]) {
+    // In host code g_static_stage is only a stand-in symbol; the device
+    // address comes from the runtime, with the device current.
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_stage);
+    if (e != cudaSuccess) return e;
+    g_static_stage_ptr[device] = p;
+  }
+  *out = g_static_stage_ptr[device];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" ponni_b200_status ponni_b200_forward_host_static(ponni_b200_model* m, const void* input, int64_t in_ld,
+                                                            void* output, int64_t out_ld, int64_t batch) {
+  if (!m) return PONNI_B200_ERR_INVALID_ARGUMENT;
+  if (batch <= 0) return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "Inference requires a nonzero batch size");
+  if (!input || !output) return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "input/output pointer is NULL");
+  if (in_ld < batch || out_ld < batch)
+    return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "row stride smaller than the batch size");
+  // Planning uploads the parameters (an allocation): it must have happened
+  // already, through ponni_b200_model_kernel() or an earlier forward.
+  if (!m->planned || m->params_dirty)
+    return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT,
+                   "model not prepared: call ponni_b200_model_kernel() once before the first "
+                   "ponni_b200_forward_host_static() (and again after changing parameters)");
+  const size_t esz = dtype_bytes(m->dtype);
+  const int nin = ponni_b200_num_inputs(m), nout = ponni_b200_num_outputs(m);
+  const size_t need = (size_t)batch * (size_t)(nin + nout) * esz;
+  if (need > kStaticStageBytes) {
+    return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT,
+                   "batch of " + std::to_string(batch) + " columns needs " + std::to_string(need) +
+                       " bytes of device staging; the static staging buffer holds " +
+                       std::to_string(kStaticStageBytes) + " bytes (at most " +
+                       std::to_string(kStaticStageBytes / ((size_t)(nin + nout) * esz)) +
+                       " columns for this model)");
+  }
+  cudaError_t e = cudaSetDevice(m->device);
+  if (e != cudaSuccess) return cuda_status(m, e, "cudaSetDevice");
+  void* stage = nullptr;
+  e = static_stage_address(m->device, &stage);
+  if (e != cudaSuccess) return cuda_status(m, e, "cudaGetSymbolAddress(static staging)");
+  unsigned char* din = static_cast<unsigned char*>(stage);
+  unsigned char* dout = din + (((size_t)nin * batch * esz + 255) & ~(size_t)255);
+  if ((size_t)(dout - din) + (size_t)nout * batch * esz > kStaticStageBytes) dout = din + (size_t)nin * batch * esz;
+  cudaStream_t s = m->stream;
+  e = cudaMemcpy2DAsync(din, (size_t)batch * esz, input, (size_t)in_ld * esz, (size_t)batch * esz, nin,
+                        cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_status(m, e, "input copy");
+  ponni_b200_status st = ponni_b200_forward(m, din, batch, dout, batch, batch, s);
+  if (st) return st;
+  e = cudaMemcpy2DAsync(output, (size_t)out_ld * esz, dout, (size_t)batch * esz, (size_t)batch * esz, nout,
+                        cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_status(m, e, "output copy");
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(m, e, "forward_host_static");
+  return PONNI_B200_OK;
+}
