@@ -162,7 +162,8 @@ typedef enum {
 } ponni_b200_arithmetic;
 ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* model, int arithmetic);
 /* Kernel the next forward uses (plans the model): 1 = tile kernel (SIMT),
- * 2 = tensor-core kernel; 0 on a planning error (see last_error). */
+ * 2 = tensor-core kernel, 3 = narrow streaming kernel (chains at most 32
+ * wide); 0 on a planning error (see last_error). */
 int ponni_b200_model_kernel(ponni_b200_model* model);
 
 /* Diagnostic counters of the tensor-core kernel (up to 7 values; per-phase

@@ -17,6 +17,7 @@
 #include <sstream>
 
 #include "model.h"
+#include "narrow_kernel.h"
 #include "tc_kernel.h"
 #include "tc_plan.h"
 #include "tile_kernel.h"
@@ -527,6 +528,10 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED, "tensor-core kernel unavailable: " + m->tc_why);
     }
   }
+  // Narrow chains (every width <= 32) stream through registers, unless the
+  // tile kernel is forced (PONNI_B200_FORCE_TILE=1, a test aid).
+  const char* force_tile = getenv("PONNI_B200_FORCE_TILE");
+  if (m->kernel == 1 && !(force_tile && force_tile[0] == '1') && narrow_eligible(p, &m->narrow_maxw)) m->kernel = 3;
   m->planned = true;
   m->params_dirty = false;
   return PONNI_B200_OK;
@@ -723,6 +728,9 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + m->tcp.slots - 1) / m->tcp.slots);
     e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
+  } else if (m->kernel == 3) {
+    e = launch_narrow_forward((int)m->dtype, m->prog, m->narrow_maxw, m->packed_dev, input, in_ld, output, out_ld,
+                              batch, m->num_sms, s);
   } else {
     const int64_t ntiles = (batch + m->prog.bt - 1) / m->prog.bt;
     const int grid = (int)std::min<int64_t>(m->grid, ntiles);

@@ -53,7 +53,8 @@ struct ponni_b200_model {
 
   // Tensor-core dense-chain kernel (planned when eligible and allowed).
   int arithmetic = PONNI_B200_ARITH_AUTO;  // ponni_b200_arithmetic requested
-  int kernel = 0;       // 1 tile (SIMT) kernel, 2 tensor-core kernel; 0 = not planned yet
+  int kernel = 0;       // 1 tile (SIMT), 2 tensor-core, 3 narrow streaming kernel; 0 = not planned yet
+  int narrow_maxw = 0;
   ponni_b200::TcProgram tcp;
   void* tc_image_dev = nullptr;
   size_t tc_image_bytes = 0;

@@ -198,3 +198,30 @@ def test_full_size_shard_consistency():
     xs = x[:, cols].contiguous().cpu().numpy()
     ys = y[:, cols].cpu().numpy()
     check(ys, oracle.forward(cfg.layers, cfg.dtype, xs), cfg.dtype, cfg.layers, xs)
+
+
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F64, pb.F16, pb.BF16])
+@pytest.mark.parametrize("maxw", [3, 8, 13, 32])
+def test_narrow_kernel(dtype, maxw, oracle_lib):
+    rng = np.random.default_rng(maxw)
+    dims = [min(maxw, 5), maxw, max(2, maxw // 2), 3]
+    layers = []
+    for i in range(3):
+        layers += [pb.Matvec(rng.normal(0, 1 / np.sqrt(dims[i]), (dims[i], dims[i + 1]))),
+                   pb.Bias(rng.normal(0, 0.1, dims[i + 1]))]
+        if i < 2:
+            layers.append([pb.Relu, pb.Silu, pb.Tanh][i % 3](dims[i + 1]))
+    m = pb.Inference(layers, dtype=dtype)
+    assert m.kernel() == pb._abi.KERNEL_NARROW
+    for batch in (1, 7, 1001):
+        x = pb.to_dtype_bytes(rng.normal(0, 1, (dims[0], batch)), dtype)
+        check(run_device(layers, dtype, x), oracle_lib.forward(layers, dtype, x), dtype, layers, x)
+
+
+def test_tile_kernel_on_narrow_models(monkeypatch):
+    # the tile kernel still serves narrow chains when forced (and every
+    # program with barriers); rerun the known answers on it
+    monkeypatch.setenv("PONNI_B200_FORCE_TILE", "1")
+    m = pb.Inference(K.readme_mlp())
+    assert m.kernel() == pb._abi.KERNEL_TILE
+    test_kats_on_gpu()
