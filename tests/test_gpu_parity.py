@@ -30,8 +30,8 @@ def from_torch(y, dtype):
     return y.cpu().numpy()
 
 
-def run_device(layers, dtype, x_raw):
-    m = pb.Inference(layers, dtype=dtype)
+def run_device(layers, dtype, x_raw, arithmetic=None):
+    m = pb.Inference(layers, dtype=dtype, arithmetic=arithmetic)
     y = m.forward_batch_parallel(to_torch(x_raw, dtype).cuda())
     torch.cuda.synchronize()
     return from_torch(y, dtype)
@@ -211,11 +211,12 @@ def test_narrow_kernel(dtype, maxw, oracle_lib):
                    pb.Bias(rng.normal(0, 0.1, dims[i + 1]))]
         if i < 2:
             layers.append([pb.Relu, pb.Silu, pb.Tanh][i % 3](dims[i + 1]))
-    m = pb.Inference(layers, dtype=dtype)
+    ref_arith = pb._abi.ARITH_REFERENCE  # (fp32 chains wider than 16 go to tensor cores under AUTO)
+    m = pb.Inference(layers, dtype=dtype, arithmetic=ref_arith)
     assert m.kernel() == pb._abi.KERNEL_NARROW
     for batch in (1, 7, 1001):
         x = pb.to_dtype_bytes(rng.normal(0, 1, (dims[0], batch)), dtype)
-        check(run_device(layers, dtype, x), oracle_lib.forward(layers, dtype, x), dtype, layers, x)
+        check(run_device(layers, dtype, x, ref_arith), oracle_lib.forward(layers, dtype, x), dtype, layers, x)
 
 
 def test_tile_kernel_on_narrow_models(monkeypatch):
