@@ -531,7 +531,17 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
   // Narrow chains (every width <= 32) stream through registers, unless the
   // tile kernel is forced (PONNI_B200_FORCE_TILE=1, a test aid).
   const char* force_tile = getenv("PONNI_B200_FORCE_TILE");
-  if (m->kernel == 1 && !(force_tile && force_tile[0] == '1') && narrow_eligible(p, &m->narrow_maxw)) m->kernel = 3;
+  if (m->kernel == 1 && !(force_tile && force_tile[0] == '1') && narrow_eligible((int)m->dtype, p, &m->narrow_maxw)) {
+    if (!m->prog_dev) {
+      e = cudaMalloc(&m->prog_dev, sizeof(Program));
+      if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(program)");
+    }
+    e = cudaMemcpyAsync(m->prog_dev, &p, sizeof(Program), cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e == cudaSuccess) e = narrow_prepare((int)m->dtype, p, m->narrow_maxw, m->num_sms, &m->narrow);
+    if (e != cudaSuccess) return cuda_fail(m, e, "narrow kernel preparation");
+    m->kernel = 3;
+  }
   m->planned = true;
   m->params_dirty = false;
   return PONNI_B200_OK;
@@ -650,11 +660,12 @@ ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, i
 
 void ponni_b200_model_destroy(ponni_b200_model* m) {
   if (!m) return;
-  if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev) {
+  if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev || m->prog_dev) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
     if (m->packed_dev) cudaFree(m->packed_dev);
+    if (m->prog_dev) cudaFree(m->prog_dev);
     if (m->stage_dev) cudaFree(m->stage_dev);
     if (m->tc_image_dev) cudaFree(m->tc_image_dev);
     if (m->err_dev) cudaFree(m->err_dev);
@@ -729,8 +740,8 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
     const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + m->tcp.slots - 1) / m->tcp.slots);
     e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
   } else if (m->kernel == 3) {
-    e = launch_narrow_forward((int)m->dtype, m->prog, m->narrow_maxw, m->packed_dev, input, in_ld, output, out_ld,
-                              batch, m->num_sms, s);
+    e = launch_narrow_forward(m->narrow, static_cast<const Program*>(m->prog_dev), m->packed_dev, input, in_ld,
+                              output, out_ld, batch, s);
   } else {
     const int64_t ntiles = (batch + m->prog.bt - 1) / m->prog.bt;
     const int grid = (int)std::min<int64_t>(m->grid, ntiles);

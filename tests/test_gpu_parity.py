@@ -212,11 +212,18 @@ def test_narrow_kernel(dtype, maxw, oracle_lib):
         if i < 2:
             layers.append([pb.Relu, pb.Silu, pb.Tanh][i % 3](dims[i + 1]))
     ref_arith = pb._abi.ARITH_REFERENCE  # (fp32 chains wider than 16 go to tensor cores under AUTO)
-    m = pb.Inference(layers, dtype=dtype, arithmetic=ref_arith)
-    assert m.kernel() == pb._abi.KERNEL_NARROW
-    for batch in (1, 7, 1001):
-        x = pb.to_dtype_bytes(rng.normal(0, 1, (dims[0], batch)), dtype)
-        check(run_device(layers, dtype, x, ref_arith), oracle_lib.forward(layers, dtype, x), dtype, layers, x)
+    # second network: a leading pointwise run (its own step), LeakyReLU on the
+    # register path, a Bias-free dense layer, GELU + Sigmoid on the staged path
+    layers2 = [pb.Tanh(dims[0]), pb.LeakyRelu(dims[0], 0.05),
+               pb.Matvec(rng.normal(0, 1 / np.sqrt(dims[0]), (dims[0], dims[1]))), pb.LeakyRelu(dims[1], 0.2),
+               pb.Matvec(rng.normal(0, 1 / np.sqrt(dims[1]), (dims[1], dims[3]))),
+               pb.Bias(rng.normal(0, 0.1, dims[3])), pb.Gelu(dims[3]), pb.Sigmoid(dims[3])]
+    for net in (layers, layers2):
+        m = pb.Inference(net, dtype=dtype, arithmetic=ref_arith)
+        assert m.kernel() == pb._abi.KERNEL_NARROW
+        for batch in (1, 7, 1001, 4099):
+            x = pb.to_dtype_bytes(rng.normal(0, 1, (dims[0], batch)), dtype)
+            check(run_device(net, dtype, x, ref_arith), oracle_lib.forward(net, dtype, x), dtype, net, x)
 
 
 def test_tile_kernel_on_narrow_models(monkeypatch):
