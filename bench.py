@@ -177,7 +177,8 @@ def main():
         arith_name = "auto"
         model.set_arithmetic(pb._abi.ARITH_AUTO)
     kernel_name = {1: "tile_forward_kernel (SIMT)", 2: "tc_forward_kernel (tcgen05)",
-                   3: "narrow_forward_kernel (streaming)"}[model.kernel()]
+                   3: "narrow_forward_kernel (streaming)",
+                   4: "ponni_narrow_jit (streaming, model-specialised)"}[model.kernel()]
     tdt = model.torch_dtype()
     x = torch.empty((nin, B), dtype=tdt, device=dev)
     y = torch.empty((nout, B), dtype=tdt, device=dev)

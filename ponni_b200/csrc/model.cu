@@ -541,6 +541,13 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
     if (e == cudaSuccess) e = narrow_prepare((int)m->dtype, p, m->narrow_maxw, m->num_sms, &m->narrow);
     if (e != cudaSuccess) return cuda_fail(m, e, "narrow kernel preparation");
     m->kernel = 3;
+    // Model-specialised form, unless disabled (PONNI_B200_NARROW_JIT=0) or
+    // unavailable (then the generic narrow kernel runs).
+    const char* jit = getenv("PONNI_B200_NARROW_JIT");
+    m->jit_why.clear();
+    if (jit && jit[0] == '0') m->jit_why = "disabled by PONNI_B200_NARROW_JIT=0";
+    else if (narrow_jit_build((int)m->dtype, p, m->narrow_maxw, m->packed_host, m->num_sms, &m->jit, &m->jit_why))
+      m->kernel = 4;
   }
   m->planned = true;
   m->params_dirty = false;
@@ -739,6 +746,8 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + m->tcp.slots - 1) / m->tcp.slots);
     e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
+  } else if (m->kernel == 4) {
+    e = narrow_jit_launch(m->jit, input, in_ld, output, out_ld, batch, s);
   } else if (m->kernel == 3) {
     e = launch_narrow_forward(m->narrow, static_cast<const Program*>(m->prog_dev), m->packed_dev, input, in_ld,
                               output, out_ld, batch, s);

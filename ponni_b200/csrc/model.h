@@ -7,6 +7,7 @@
 
 #include "../../include/ponni_b200.h"
 #include "program.h"
+#include "narrow_jit.h"
 #include "narrow_kernel.h"
 #include "tc_program.h"
 
@@ -54,10 +55,13 @@ struct ponni_b200_model {
 
   // Tensor-core dense-chain kernel (planned when eligible and allowed).
   int arithmetic = PONNI_B200_ARITH_AUTO;  // ponni_b200_arithmetic requested
-  int kernel = 0;       // 1 tile (SIMT), 2 tensor-core, 3 narrow streaming kernel; 0 = not planned yet
+  int kernel = 0;       // 1 tile (SIMT), 2 tensor-core, 3 narrow streaming kernel, 4 its model-specialised
+                        // (NVRTC-compiled) form; 0 = not planned yet
   int narrow_maxw = 0;
   ponni_b200::NarrowLaunch narrow;     // narrow kernel launch configuration
   void* prog_dev = nullptr;            // the Program in device memory (narrow kernel)
+  ponni_b200::NarrowJit jit;           // model-specialised narrow kernel (kernel 4)
+  std::string jit_why;                 // why the specialised kernel is not used
   ponni_b200::TcProgram tcp;
   void* tc_image_dev = nullptr;
   size_t tc_image_bytes = 0;

@@ -12,6 +12,8 @@
 #pragma once
 #include <stdint.h>
 
+#include "epi_kinds.h"
+
 namespace ponni_b200 {
 
 constexpr int kMaxSteps = 64;
@@ -31,14 +33,6 @@ enum StepKind : int32_t {
   STEP_COPY = 6,       // Save_State: dst[f][c] = src[f][c]
   STEP_ADD = 7,        // Binop_Add: src[f][c] += aux[f][c]
   STEP_CONCAT = 8,     // Binop_Concatenate: dst = [src ; aux] or [aux ; src]
-};
-
-// Pointwise operation kinds (values match ponni_b200_layer_kind).
-enum EpiKind : int32_t {
-  EPI_NONE = 0,
-  EPI_BIAS = 1, EPI_RELU = 2, EPI_LEAKY_RELU = 3, EPI_ELU = 4, EPI_SELU = 5, EPI_GELU = 6,
-  EPI_SILU = 7, EPI_SIGMOID = 8, EPI_TANH = 9, EPI_SOFTPLUS = 10, EPI_HARD_SIGMOID = 11,
-  EPI_HARD_SWISH = 12, EPI_MISH = 13,
 };
 
 // Dense flags.

@@ -200,9 +200,15 @@ def test_full_size_shard_consistency():
     check(ys, oracle.forward(cfg.layers, cfg.dtype, xs), cfg.dtype, cfg.layers, xs)
 
 
+@pytest.mark.parametrize("jit", [True, False])
 @pytest.mark.parametrize("dtype", [pb.F32, pb.F64, pb.F16, pb.BF16])
 @pytest.mark.parametrize("maxw", [3, 8, 13, 32])
-def test_narrow_kernel(dtype, maxw, oracle_lib):
+def test_narrow_kernel(dtype, maxw, jit, oracle_lib, monkeypatch):
+    """Narrow chains on the model-specialised (NVRTC) kernel and on the
+    generic narrow kernel (PONNI_B200_NARROW_JIT=0)."""
+    if not jit:
+        monkeypatch.setenv("PONNI_B200_NARROW_JIT", "0")
+    want = pb._abi.KERNEL_NARROW_JIT if jit else pb._abi.KERNEL_NARROW
     rng = np.random.default_rng(maxw)
     dims = [min(maxw, 5), maxw, max(2, maxw // 2), 3]
     layers = []
@@ -220,7 +226,7 @@ def test_narrow_kernel(dtype, maxw, oracle_lib):
                pb.Bias(rng.normal(0, 0.1, dims[3])), pb.Gelu(dims[3]), pb.Sigmoid(dims[3])]
     for net in (layers, layers2):
         m = pb.Inference(net, dtype=dtype, arithmetic=ref_arith)
-        assert m.kernel() == pb._abi.KERNEL_NARROW
+        assert m.kernel() == want
         for batch in (1, 7, 1001, 4099):
             x = pb.to_dtype_bytes(rng.normal(0, 1, (dims[0], batch)), dtype)
             check(run_device(net, dtype, x, ref_arith), oracle_lib.forward(net, dtype, x), dtype, net, x)
@@ -233,3 +239,34 @@ def test_tile_kernel_on_narrow_models(monkeypatch):
     m = pb.Inference(K.readme_mlp())
     assert m.kernel() == pb._abi.KERNEL_TILE
     test_kats_on_gpu()
+
+
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F64, pb.F16, pb.BF16])
+def test_narrow_jit_matches_generic(dtype, monkeypatch):
+    """The model-specialised narrow kernel performs the same operations in the
+    same order as the generic narrow kernel: results agree bit for bit."""
+    rng = np.random.default_rng(7)
+    net = [pb.Matvec(rng.normal(0, 0.5, (6, 8))), pb.Bias(rng.normal(0, 0.1, 8)), pb.Silu(8),
+           pb.Matvec(rng.normal(0, 0.5, (8, 5))), pb.Bias(rng.normal(0, 0.1, 5)), pb.LeakyRelu(5, 0.1),
+           pb.Matvec(rng.normal(0, 0.5, (5, 2))), pb.Bias(rng.normal(0, 0.1, 2)), pb.Tanh(2)]
+    x = pb.to_dtype_bytes(rng.normal(0, 1, (6, 70001)), dtype)
+    ref = pb._abi.ARITH_REFERENCE
+    y_jit = run_device(net, dtype, x, ref)
+    assert pb.Inference(net, dtype=dtype, arithmetic=ref).kernel() == pb._abi.KERNEL_NARROW_JIT
+    monkeypatch.setenv("PONNI_B200_NARROW_JIT", "0")
+    assert pb.Inference(net, dtype=dtype, arithmetic=ref).kernel() == pb._abi.KERNEL_NARROW
+    y_gen = run_device(net, dtype, x, ref)
+    assert np.array_equal(np.asarray(y_jit).view(np.uint8), np.asarray(y_gen).view(np.uint8))
+
+
+def test_narrow_jit_weights_change_reuses_kernel(oracle_lib):
+    """Two models of one structure share the compiled kernel; each runs with
+    its own weights (they travel as a kernel parameter)."""
+    rng = np.random.default_rng(11)
+    for seed in (1, 2):
+        r = np.random.default_rng(seed)
+        net = [pb.Matvec(r.normal(0, 1, (2, 3))), pb.Bias(r.normal(0, 1, 3)), pb.Relu(3),
+               pb.Matvec(r.normal(0, 1, (3, 1))), pb.Bias(r.normal(0, 1, 1))]
+        assert pb.Inference(net).kernel() == pb._abi.KERNEL_NARROW_JIT
+        x = pb.to_dtype_bytes(rng.normal(0, 1, (2, 5000)), pb.F32)
+        check(run_device(net, pb.F32, x), oracle_lib.forward(net, pb.F32, x), pb.F32, net, x)
