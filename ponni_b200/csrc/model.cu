@@ -522,7 +522,7 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       e = cudaMemcpyAsync(m->tc_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
       if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
       if (e != cudaSuccess) return cuda_fail(m, e, "tensor-core parameter upload");
-      m->tc_grid = m->num_sms;  // one persistent CTA (two tile slots) per SM
+      m->tc_grid = m->num_sms;  // one persistent CTA (up to four tile slots) per SM
       m->kernel = 2;
     } else if (m->arithmetic == PONNI_B200_ARITH_TENSOR) {
       return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED, "tensor-core kernel unavailable: " + m->tc_why);
@@ -741,6 +741,10 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
   // Reference ensure_internal_state_capacity (src/ponni_Inference.h:197-199).
   if (batch > m->capacity) m->capacity = batch;
   cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
+  // Launch on the model's device; the caller's current device is restored.
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != m->device) cudaSetDevice(m->device);
   cudaError_t e;
   if (m->kernel == 2) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
@@ -757,7 +761,8 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
     e = launch_tile_forward((int)m->dtype, m->prog, m->packed_dev, input, in_ld, output, out_ld, batch, grid,
                             m->smem_bytes, s);
   }
-  if (e != cudaSuccess) return cuda_fail(m, e, "tile kernel launch");
+  if (cur >= 0 && cur != m->device) cudaSetDevice(cur);
+  if (e != cudaSuccess) return cuda_fail(m, e, "kernel launch");
   return PONNI_B200_OK;
 }
 

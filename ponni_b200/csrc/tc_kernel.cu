@@ -1,7 +1,7 @@
 // Tensor-core dense-chain kernel for sm_100a (tcgen05 UMMA + TMEM).
 //
-// One persistent CTA per SM with two warpgroups, each owning one tile slot so
-// that one slot's epilogue overlaps the other's MMAs.  Per batch tile of 128
+// One persistent CTA per SM with up to four thread groups, each owning one
+// tile slot, so that the slots' epilogues overlap the others' MMAs.  Per batch tile of 128
 // columns:
 //   input  : cp.async (16 B, zero-filled tail) of the batch-contiguous input
 //            rows into a staging tile, prefetched one tile ahead into a
@@ -161,7 +161,9 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+  // No "memory" clobber: ordering against the MMAs that read these operands
+  // comes from the proxy fence and barrier asm statements (all volatile).
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d));
 }
 
 #ifdef PONNI_B200_TC_PROFILE
@@ -240,14 +242,14 @@ __device__ __forceinline__ void store_row8(const uint32_t* a, int m, int k0, con
 
 // Stage input columns [col0, col0+128).  fp32: row-major [k][128] fp32;
 // 16-bit: MN-major SW128 operand layout.
-template <class T>
+template <class T, int TPS>
 __device__ __forceinline__ void load_input(uint32_t stage, const T* __restrict__ in, int64_t in_ld, int nin,
                                            int64_t col0, int64_t batch, bool vec, int lt) {
   constexpr int esz = sizeof(T);
   constexpr int per16 = 16 / esz;
   constexpr int chunks_per_row = kTcM / per16;  // 32 (fp32) or 16 (16-bit)
   if (vec) {
-    for (int i = lt; i < nin * chunks_per_row; i += kTcWgThreads) {
+    for (int i = lt; i < nin * chunks_per_row; i += TPS) {
       const int f = i / chunks_per_row, j = i - f * chunks_per_row;
       const int64_t col = col0 + (int64_t)j * per16;
       const int64_t valid = batch - col;
@@ -261,7 +263,7 @@ __device__ __forceinline__ void load_input(uint32_t stage, const T* __restrict__
       cp_async16(dst, src, bytes);
     }
   } else {
-    for (int i = lt; i < nin * kTcM; i += kTcWgThreads) {
+    for (int i = lt; i < nin * kTcM; i += TPS) {
       const int f = i / kTcM, m = i - f * kTcM;
       const int64_t col = col0 + m;
       T v = col < batch ? in[(int64_t)f * in_ld + col] : Store<T>::from(0.0f);
@@ -279,51 +281,75 @@ __device__ __forceinline__ void load_input(uint32_t stage, const T* __restrict__
   }
 }
 
+// The fields of a layer the epilogue needs, held in registers (a reference
+// into shared memory would be re-read after every shared-memory store).
+struct EpiArgs {
+  int n_pad, nout, groups, has_bias, act_flags;
+  float s0, s1;
+};
+
 template <int ACT>
-__device__ __forceinline__ float epi_act(float v, const TcLayer& L) {
+__device__ __forceinline__ float epi_act(float v, const EpiArgs& E) {
   if constexpr (ACT == EPI_NONE) return v;
-  else return activation<float>(ACT, L.act_flags, v, L.s0, L.s1);
+  else return activation<float>(ACT, E.act_flags, v, E.s0, E.s1);
+}
+
+// ReLU on two packed 16-bit values: max(x, 0) after rounding equals the
+// rounding of max(x, 0) (rounding is monotonic and keeps the sign).
+__device__ __forceinline__ uint32_t relu2(uint32_t w, __half*) {
+  uint32_t r;
+  asm("max.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(w), "r"(0u));
+  return r;
+}
+__device__ __forceinline__ uint32_t relu2(uint32_t w, __nv_bfloat16*) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(w), "r"(0u));
+  return r;
 }
 
 // Epilogue of one layer for this thread's TMEM lane (= batch column m):
 // sum the layer's accumulators, add the bias, apply the activation (fp32),
-// then write the next layer's operand, or the caller's output.
-template <class T, int ACT>
-__device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t tmem_lane, const float* bias,
+// then write the next layer's operand, or the caller's output.  Padding
+// columns (nout..n_pad) need no masking: their weights and biases are zero
+// and the next layer's padded K rows of B are zero.
+template <class T, int TPS, int ACT>
+__device__ __forceinline__ void epilogue(const EpiArgs E, bool last, uint32_t tmem_lane, const float* bias,
                                          const uint32_t* a, T* __restrict__ out, int64_t out_ld, int64_t col,
                                          int64_t batch, int m, int half) {
-  for (int c0 = 32 * half; c0 < L.n_pad; c0 += 64) {
+  using Op = typename OperandOf<T>::type;
+  constexpr int kStep = 32 * (TPS / 128);  // 256-thread slots split the columns in two halves
+  for (int c0 = 32 * half; c0 < E.n_pad; c0 += kStep) {
     float v[32];
 #ifdef PONNI_B200_TC_PROFILE
     const long long t_ld = clock64();
 #endif
     int g = 1;
-    if (L.groups == 1) {
+    if (E.groups == 1) {
       tmem_ld32(tmem_lane + (uint32_t)c0, v);
     } else {
       float w[32];
-      tmem_ld32x2(tmem_lane + (uint32_t)c0, tmem_lane + (uint32_t)(L.n_pad + c0), v, w);
+      tmem_ld32x2(tmem_lane + (uint32_t)c0, tmem_lane + (uint32_t)(E.n_pad + c0), v, w);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] += w[j];
       g = 2;
     }
-    for (; g + 1 < L.groups; g += 2) {
+    for (; g + 1 < E.groups; g += 2) {
       float w0[32], w1[32];
-      tmem_ld32x2(tmem_lane + (uint32_t)(g * L.n_pad + c0), tmem_lane + (uint32_t)((g + 1) * L.n_pad + c0), w0, w1);
+      tmem_ld32x2(tmem_lane + (uint32_t)(g * E.n_pad + c0), tmem_lane + (uint32_t)((g + 1) * E.n_pad + c0), w0, w1);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] += w0[j] + w1[j];
     }
-    for (; g < L.groups; ++g) {
+    for (; g < E.groups; ++g) {
       float w[32];
-      tmem_ld32(tmem_lane + (uint32_t)(g * L.n_pad + c0), w);
+      tmem_ld32(tmem_lane + (uint32_t)(g * E.n_pad + c0), w);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] += w[j];
     }
 #ifdef PONNI_B200_TC_PROFILE
-    if ((threadIdx.x & (kTcWgThreads - 1)) == 0)
+    if ((threadIdx.x & (TPS - 1)) == 0)
       atomicAdd(reinterpret_cast<unsigned long long*>(prof_ptr) + 7, (unsigned long long)(clock64() - t_ld));
 #endif
-    if (L.has_bias) {
+    if (E.has_bias) {
       const float4* b4 = reinterpret_cast<const float4*>(bias + c0);  // zero-padded to 32 columns
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
@@ -334,35 +360,43 @@ __device__ __forceinline__ void epilogue(const TcLayer& L, bool last, uint32_t t
         v[4 * q + 3] += b.w;
       }
     }
-    if (c0 + 32 <= L.nout) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = epi_act<ACT>(v[j], L);
-    } else {  // the chunk holding the padding columns: force them to zero
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float x = epi_act<ACT>(v[j], L);
-        v[j] = c0 + j < L.nout ? x : 0.0f;
-      }
-    }
     if (last) {
-      if (col < batch) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < L.nout) out[(int64_t)(c0 + j) * out_ld + col] = Store<T>::from(v[j]);
+      for (int j = 0; j < 32; ++j) v[j] = epi_act<ACT>(v[j], E);
+      if (col < batch) {
+        // Rows c0 .. c0 + nv of the output (a warp stores 32 consecutive
+        // columns of each row).
+        const int nv = min(32, E.nout - c0);
+        T* o = out + (int64_t)c0 * out_ld + col;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (j >= nv) break;
+          o[(int64_t)j * out_ld] = Store<T>::from(v[j]);
+        }
+      }
+    } else if constexpr (sizeof(T) == 2 && ACT == EPI_RELU) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = relu2(pack2(v[8 * q + 2 * e], v[8 * q + 2 * e + 1], (Op*)0), (Op*)0);
+        st_shared_v4(a[0] + kmajor_chunk(m, (uint32_t)(c0 + 8 * q) * 2), w[0], w[1], w[2], w[3]);
       }
     } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = epi_act<ACT>(v[j], E);
 #pragma unroll
       for (int q = 0; q < 4; ++q) store_row8<T>(a, m, c0 + 8 * q, v + 8 * q);
     }
   }
 }
 
-template <class T>
-__device__ __forceinline__ void epilogue_dispatch(const TcLayer& L, bool last, uint32_t tmem_lane, const float* bias,
-                                                  const uint32_t* a, T* __restrict__ out, int64_t out_ld,
-                                                  int64_t col, int64_t batch, int m, int half) {
-#define PONNI_TC_EPI(A) epilogue<T, A>(L, last, tmem_lane, bias, a, out, out_ld, col, batch, m, half)
-  switch (L.act) {
+template <class T, int TPS>
+__device__ __forceinline__ void epilogue_dispatch(int act, const EpiArgs E, bool last, uint32_t tmem_lane,
+                                                  const float* bias, const uint32_t* a, T* __restrict__ out,
+                                                  int64_t out_ld, int64_t col, int64_t batch, int m, int half) {
+#define PONNI_TC_EPI(A) epilogue<T, TPS, A>(E, last, tmem_lane, bias, a, out, out_ld, col, batch, m, half)
+  switch (act) {
     case EPI_RELU: PONNI_TC_EPI(EPI_RELU); break;
     case EPI_LEAKY_RELU: PONNI_TC_EPI(EPI_LEAKY_RELU); break;
     case EPI_SILU: PONNI_TC_EPI(EPI_SILU); break;
@@ -375,9 +409,11 @@ __device__ __forceinline__ void epilogue_dispatch(const TcLayer& L, bool last, u
 }
 
 // Named barrier over one slot's threads (ids 1..slots; 0 is __syncthreads).
+template <int TPS>
 __device__ __forceinline__ void wg_sync(int wg) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(wg + 1), "r"(kTcWgThreads) : "memory");
+  asm volatile("bar.sync %0, %1;\n" ::"r"(wg + 1), "r"(TPS) : "memory");
 }
+template <int TPS>
 __device__ __forceinline__ int wg_sync_or(int wg, int pred) {
   int r;
   asm volatile(
@@ -386,7 +422,7 @@ __device__ __forceinline__ int wg_sync_or(int wg, int pred) {
       "bar.red.or.pred q, %1, %3, p;\n\t"
       "selp.b32 %0, 1, 0, q;\n\t}\n"
       : "=r"(r)
-      : "r"(wg + 1), "r"(pred), "r"(kTcWgThreads)
+      : "r"(wg + 1), "r"(pred), "r"(TPS)
       : "memory");
   return r;
 }
@@ -459,11 +495,11 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
 #endif
 
 // --------------------------------------------------------------- kernel --
-// Two slots per CTA, each run by 8 warps (4 TMEM lane quarters x 2 column
-// halves) that own the slot's operand buffers, input stage, mbarrier and TMEM
+// Up to four slots per CTA, each run by 4 or 8 warps (4 TMEM lane quarters,
+// x 2 column halves with 8) that own the slot's operand buffers, input stage, mbarrier and TMEM
 // accumulators and walk their own tiles; while one slot runs its epilogue the
 // tensor core works on the other's chain.
-template <class T>
+template <class T, int TPS>
 __global__ void __launch_bounds__(kTcMaxThreads, 1)
     tc_forward_kernel(const __grid_constant__ TcProgram p, const unsigned char* __restrict__ image,
                       const T* __restrict__ in, int64_t in_ld, T* __restrict__ out, int64_t out_ld, int64_t batch,
@@ -475,19 +511,24 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzle atoms need 1024-byte alignment
   unsigned char* base_ptr = smem_raw + (base - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int wg = warp >> 3, lt = tid & (kTcWgThreads - 1);
-  const int half = (warp >> 2) & 1;  // column half of the epilogue this warp handles
+  constexpr int kWarps = TPS / 32;
+  const int wg = warp / kWarps, lt = tid & (TPS - 1);
+  const int half = TPS == 256 ? (warp >> 2) & 1 : 0;  // column half of the epilogue this warp handles
   const uint32_t s_image = base;
   const uint32_t s_slot = s_image + p.image_bytes + (uint32_t)wg * p.slot_bytes;
   uint32_t s_a[3];
 #pragma unroll
   for (int q = 0; q < 3; ++q) s_a[q] = s_slot + (uint32_t)(q < NP ? q : 0) * p.a_bytes;
   const uint32_t stage = s_slot + (uint32_t)NP * p.a_bytes;
-  const int nslots = p.slots, nthreads = nslots * kTcWgThreads;
+  const int nslots = p.slots, nthreads = nslots * TPS;
   const uint32_t s_bars = s_image + p.image_bytes + (uint32_t)nslots * p.slot_bytes;
   const uint32_t s_bar = s_bars + 8u * (uint32_t)wg;
   const uint32_t s_tmem = s_bars + 8u * kTcMaxSlots;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(base_ptr + (s_tmem - base));
+  // Layer table copied to shared memory: the layer loop indexes it with a
+  // run-time index, which on the kernel-parameter copy would go through the
+  // constant cache's slow address-divergence path.
+  TcLayer* layers = reinterpret_cast<TcLayer*>(base_ptr + (s_bars + 64u - base));
 
   const int64_t ntiles = (batch + kTcM - 1) / kTcM;
   if ((int64_t)blockIdx.x * nslots >= ntiles) return;
@@ -506,6 +547,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
     for (int i = tid; i < (int)(p.stage_bytes / 16); i += nthreads) z[i] = make_uint4(0, 0, 0, 0);
   }
   for (uint32_t i = tid; i < p.image_bytes / 16; i += nthreads) cp_async16(s_image + i * 16, image + i * 16, 16);
+  for (int i = tid; i < p.n_layers; i += nthreads) layers[i] = p.layers[i];
   cp_async_commit();
   cp_async_wait_0();
   tc_fence_before();
@@ -520,7 +562,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   int64_t tile = (int64_t)blockIdx.x * nslots + wg;
   uint32_t phase = 0;
   if (tile < ntiles) {
-    load_input<T>(stage, in, in_ld, p.nin, tile * kTcM, batch, in_vec != 0, lt);
+    load_input<T, TPS>(stage, in, in_ld, p.nin, tile * kTcM, batch, in_vec != 0, lt);
     cp_async_commit();
   }
   for (; tile < ntiles; tile += stride) {
@@ -528,7 +570,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
     const int64_t next = tile + stride;
     TC_PROF_T(t_in);
     cp_async_wait_0();
-    wg_sync(wg);
+    wg_sync<TPS>(wg);
     TC_PROF_ADD(0, t_in);
     TC_PROF_T(t_split);
     if constexpr (SPLIT) {
@@ -536,24 +578,27 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
       // bf16 operand parts of layer 0; then the stage is free for the next tile.
       const int k0 = p.layers[0].k_pad;
       const float* st = reinterpret_cast<const float*>(base_ptr + (stage - base));
-      for (int f = 8 * half; f < k0; f += 16) {
+      for (int f = 8 * half; f < k0; f += 8 * (TPS / 128)) {
         float v[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[e] = st[(f + e) * kTcM + m];
         store_row8<T>(s_a, m, f, v);
       }
-      wg_sync(wg);
-      if (next < ntiles) load_input<T>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
+      wg_sync<TPS>(wg);
+      if (next < ntiles) load_input<T, TPS>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
       cp_async_commit();
     }
     TC_PROF_ADD(1, t_split);
     bool failed = false;
     for (int l = 0; l < p.n_layers; ++l) {
-      const TcLayer& L = p.layers[l];
+      const TcLayer& L = layers[l];
+      const EpiArgs E{L.n_pad, L.nout, L.groups, L.has_bias, L.act_flags, L.s0, L.s1};
+      const int act = L.act;
+      const uint32_t bias_off = L.bias_off;
       TC_PROF_T(t_bar);
       fence_proxy_async();
       tc_fence_before();
-      wg_sync(wg);
+      wg_sync<TPS>(wg);
       // One elected thread issues the chain and waits for its completion;
       // the rest of the warpgroup parks on the named barrier (no issue slots
       // spent spinning while the other slot's epilogue runs).
@@ -570,7 +615,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
         TC_PROF_ADD(4, t_mma);
       }
       phase ^= 1u;
-      const int bad = wg_sync_or(wg, !ok);
+      const int bad = wg_sync_or<TPS>(wg, !ok);
       tc_fence_after();
       if (bad) {
         if (lt == 0) atomicExch(err, 1);
@@ -579,13 +624,13 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
       }
       if constexpr (!SPLIT) {
         if (l == 0) {  // layer 0 has consumed the stage: prefetch the next tile
-          if (next < ntiles) load_input<T>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
+          if (next < ntiles) load_input<T, TPS>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
           cp_async_commit();
         }
       }
-      const float* bias = reinterpret_cast<const float*>(base_ptr + L.bias_off);
+      const float* bias = reinterpret_cast<const float*>(base_ptr + bias_off);
       TC_PROF_T(t_epi);
-      epilogue_dispatch<T>(L, l == p.n_layers - 1, tmem_lane, bias, s_a, out, out_ld, col0 + m, batch, m, half);
+      epilogue_dispatch<T, TPS>(act, E, l == p.n_layers - 1, tmem_lane, bias, s_a, out, out_ld, col0 + m, batch, m, half);
       TC_PROF_ADD(5, t_epi);
     }
     if (failed) break;
@@ -599,17 +644,24 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   }
 }
 
-template <class T>
-cudaError_t launch_impl(const TcProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
-                        int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream) {
-  auto kern = tc_forward_kernel<T>;
+template <class T, int TPS>
+cudaError_t launch_tps(const TcProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
+                       int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream) {
+  auto kern = tc_forward_kernel<T, TPS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
   if (e != cudaSuccess) return e;
   const bool vec = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && ((in_ld * (int64_t)sizeof(T)) % 16 == 0);
-  kern<<<grid, p.slots * kTcWgThreads, p.smem_bytes, stream>>>(p, static_cast<const unsigned char*>(image),
-                                                    static_cast<const T*>(in), in_ld, static_cast<T*>(out), out_ld,
-                                                    batch, vec ? 1 : 0, err);
+  kern<<<grid, p.slots * TPS, p.smem_bytes, stream>>>(p, static_cast<const unsigned char*>(image),
+                                                     static_cast<const T*>(in), in_ld, static_cast<T*>(out), out_ld,
+                                                     batch, vec ? 1 : 0, err);
   return cudaGetLastError();
+}
+
+template <class T>
+cudaError_t launch_impl(const TcProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
+                        int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream) {
+  if (p.slot_threads == 128) return launch_tps<T, 128>(p, image, in, in_ld, out, out_ld, batch, grid, err, stream);
+  return launch_tps<T, 256>(p, image, in, in_ld, out, out_ld, batch, grid, err, stream);
 }
 
 }  // namespace

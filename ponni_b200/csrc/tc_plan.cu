@@ -152,36 +152,41 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   const uint32_t a_kmajor = (uint32_t)((max_w32 * 2 + 127) / 128) * kTcM * 128;
   p.a_bytes = std::max(a_kmajor, 1024u);
   p.slot_bytes = p.a_bytes * (uint32_t)nparts + p.stage_bytes;
-  // Two tile slots when shared and tensor memory allow, else one.
-  for (int slots = kTcMaxSlots; slots >= 1; --slots) {
-    const int col_budget = 512 / slots;
-    max_npad = 0;
-    for (int l = 0; l < p.n_layers; ++l) {
-      TcLayer& L = p.layers[l];
-      // fp32 (split) models spread the K steps over separate accumulators
-      // summed in the epilogue (PONNI_B200_TC_GROUP_STEPS steps each; default
-      // 1): the tensor core's fp32 accumulation truncates, so shorter chains
-      // keep the result fp32-accurate.  Longer chains when the accumulators
-      // would not fit in tensor memory.
-      const int nsteps = L.k_pad / 16;
-      int gs = nsteps;
-      if (split) {
-        gs = 1;
-        if (const char* env = getenv("PONNI_B200_TC_GROUP_STEPS")) gs = std::max(1, atoi(env));
+  // As many tile slots (tiles in flight per SM) as shared and tensor memory
+  // allow, up to four.  fp32 (split) models spread the K steps over separate
+  // accumulators summed in the epilogue (PONNI_B200_TC_GROUP_STEPS steps
+  // each; default 1): the tensor core's fp32 accumulation truncates, so short
+  // chains keep the result fp32-accurate; a slot count that would force
+  // longer chains is skipped unless nothing else fits.
+  int gs_req = 1;
+  if (const char* env = getenv("PONNI_B200_TC_GROUP_STEPS")) gs_req = std::max(1, atoi(env));
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int slots = kTcMaxSlots; slots >= 1; --slots) {
+      const int col_budget = 512 / slots;
+      max_npad = 0;
+      bool longer = false;
+      for (int l = 0; l < p.n_layers; ++l) {
+        TcLayer& L = p.layers[l];
+        const int nsteps = L.k_pad / 16;
+        int gs = split ? gs_req : nsteps;
+        while (gs < nsteps && round_up((int64_t)((nsteps + gs - 1) / gs) * L.n_pad, 32) > col_budget) ++gs;
+        if (split && gs > gs_req && gs < nsteps) longer = true;
+        L.group_steps = std::min(gs, nsteps);
+        L.groups = (nsteps + L.group_steps - 1) / L.group_steps;
+        max_npad = std::max(max_npad, L.groups * L.n_pad);
       }
-      while (gs < nsteps && round_up((int64_t)((nsteps + gs - 1) / gs) * L.n_pad, 32) > col_budget) ++gs;
-      L.group_steps = std::min(gs, nsteps);
-      L.groups = (nsteps + L.group_steps - 1) / L.group_steps;
-      max_npad = std::max(max_npad, L.groups * L.n_pad);
-    }
-    p.slot_cols = (uint32_t)round_up(max_npad, 32);
-    uint32_t cols = 32;
-    while (cols < (uint32_t)slots * p.slot_cols) cols <<= 1;
-    p.smem_bytes = 1024 + p.image_bytes + (uint32_t)slots * p.slot_bytes + 64;
-    if (cols <= 512 && p.smem_bytes <= 227 * 1024) {
-      p.tmem_cols = cols;
-      p.slots = slots;
-      return true;
+      if (longer && pass == 0) continue;
+      p.slot_cols = (uint32_t)round_up(max_npad, 32);
+      uint32_t cols = 32;
+      while (cols < (uint32_t)slots * p.slot_cols) cols <<= 1;
+      p.smem_bytes = 1024 + p.image_bytes + (uint32_t)slots * p.slot_bytes + 64 +
+                     (uint32_t)(kTcMaxLayers * sizeof(TcLayer));
+      if (cols <= 512 && p.smem_bytes <= 227 * 1024) {
+        p.tmem_cols = cols;
+        p.slots = slots;
+        p.slot_threads = slots >= 3 ? 128 : 256;
+        return true;
+      }
     }
   }
   why = "weights and operand tiles exceed shared memory";

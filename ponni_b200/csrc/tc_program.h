@@ -22,9 +22,11 @@
 namespace ponni_b200 {
 
 constexpr int kTcMaxLayers = 16;
-constexpr int kTcMaxSlots = 2;   // tiles in flight per CTA (TcProgram::slots = 1 or 2)
-constexpr int kTcWgThreads = 256;  // threads of one slot: 8 warps = 4 TMEM lane quarters x 2 column halves
-constexpr int kTcMaxThreads = kTcMaxSlots * kTcWgThreads;
+constexpr int kTcMaxSlots = 4;     // tiles in flight per CTA (TcProgram::slots = 1..4)
+constexpr int kTcMaxThreads = 512;  // slots x slot_threads
+// Threads of one slot (TcProgram::slot_threads): 128 = 4 warps, one per TMEM
+// lane quarter, each thread walking all accumulator columns of its lane; or
+// 256 = 8 warps, 4 lane quarters x 2 column halves (used with <= 2 slots).
 constexpr int kTcM = 128;        // batch rows per tile (UMMA M)
 
 struct TcLayer {
@@ -53,8 +55,10 @@ struct TcProgram {
   uint32_t slot_bytes;   // shared memory of one slot: parts x a_bytes + stage_bytes
   uint32_t slot_cols;    // TMEM columns of one tile slot (max over layers of groups * n_pad)
   uint32_t tmem_cols;    // allocated TMEM columns: power of two >= slots * slot_cols
-  int32_t slots;         // tile slots per CTA (1 or 2); the CTA runs slots * kTcWgThreads threads
-  uint32_t smem_bytes;   // total dynamic shared memory requested (incl. 1 KB alignment slack)
+  int32_t slots;         // tile slots per CTA (1..4); the CTA runs slots * slot_threads threads
+  int32_t slot_threads;  // 128 or 256
+  uint32_t smem_bytes;   // total dynamic shared memory requested (incl. 1 KB alignment slack,
+                         // mbarriers, the TMEM address and a copy of the layer table)
   TcLayer layers[kTcMaxLayers];
 };
 

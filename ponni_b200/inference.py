@@ -74,7 +74,11 @@ def torch_stream_handle(device) -> int:
     default stream is the legacy NULL stream; the C ABI reads NULL as "the
     model's own stream", so the legacy stream is passed as cudaStreamLegacy."""
     import torch
-    h = torch.cuda.current_stream(device).cuda_stream
+    index = device.index if isinstance(device, torch.device) else int(device)
+    try:  # the raw handle without building a Stream object (per-call cost)
+        h = torch._C._cuda_getCurrentRawStream(index)
+    except AttributeError:
+        h = torch.cuda.current_stream(index).cuda_stream
     return h if h else 0x1
 
 
@@ -114,6 +118,8 @@ class Inference:
         self.layers = list(layers)
         self.dtype = dtype_code(dtype)
         self.device = int(device)
+        self._tdtype = None
+        self._fwd = _abi.lib().ponni_b200_forward
         descs, keep = build_descriptors(self.layers, self.dtype)
         ptr = ctypes.c_void_p()
         _check(_abi.lib().ponni_b200_model_create(descs, len(self.layers), self.dtype, self.device,
@@ -180,26 +186,34 @@ class Inference:
 
     def torch_dtype(self):
         import torch
-        return {_abi.F32: torch.float32, _abi.F64: torch.float64, _abi.F16: torch.float16,
-                _abi.BF16: torch.bfloat16}[self.dtype]
+        if self._tdtype is None:
+            self._tdtype = {_abi.F32: torch.float32, _abi.F64: torch.float64, _abi.F16: torch.float16,
+                            _abi.BF16: torch.bfloat16}[self.dtype]
+        return self._tdtype
 
     def _forward_device(self, input, output):
         import torch
 
-        self._layout(input, self.get_num_inputs(), "input")
+        nin, nout = self.get_num_inputs(), self.get_num_outputs()
+        self._layout(input, nin, "input")
         if input.dtype != self.torch_dtype():
             raise _abi.PonniError(1, f"input dtype {input.dtype} does not match the model dtype")
+        dev = input.device
+        if dev.index != self.device:
+            raise _abi.PonniError(1, f"input is on {dev}, the model on cuda:{self.device}")
         batch = input.shape[1]
         if batch == 0:
             raise _abi.PonniError(1, "Inference requires a nonzero batch size")
         if output is None:
-            output = torch.empty((self.get_num_outputs(), batch), dtype=input.dtype, device=input.device)
-        self._layout(output, self.get_num_outputs(), "output")
-        if output.shape[1] != batch or output.dtype != input.dtype:
-            raise _abi.PonniError(2, "Error: Provided output dimensions do not match the model and input batch")
-        _check(_abi.lib().ponni_b200_forward(self._m, input.data_ptr(), input.stride(0), output.data_ptr(),
-                                             output.stride(0), batch, torch_stream_handle(input.device)),
-               self._m)
+            output = torch.empty((nout, batch), dtype=input.dtype, device=dev)
+        else:
+            self._layout(output, nout, "output")
+            if output.shape[1] != batch or output.dtype != input.dtype:
+                raise _abi.PonniError(2, "Error: Provided output dimensions do not match the model and input batch")
+            if output.device != dev:
+                raise _abi.PonniError(1, f"output is on {output.device}, the input on {dev}")
+        _check(self._fwd(self._m, input.data_ptr(), input.stride(0), output.data_ptr(), output.stride(0), batch,
+                         torch_stream_handle(self.device)), self._m)
         return output
 
     def _forward_host(self, input, output):
