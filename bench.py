@@ -163,6 +163,7 @@ def main():
     import torch
     import torch.distributed as dist
     import ponni_b200 as pb
+    from ponni_b200.sharding import job_time, shard_range
 
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
@@ -186,7 +187,8 @@ def main():
     tdt = model.torch_dtype()
     x = torch.empty((nin, B), dtype=tdt, device=dev)
     y = torch.empty((nout, B), dtype=tdt, device=dev)
-    pb.fill_synthetic(x, configs.INPUT_SEED, col0=rank * B, dist=cfg.input_dist, lo=cfg.lo, hi=cfg.hi)
+    col0, _ = shard_range(rank, world, B)
+    pb.fill_synthetic(x, configs.INPUT_SEED, col0=col0, dist=cfg.input_dist, lo=cfg.lo, hi=cfg.hi)
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         model.forward_batch_parallel(x, y)
@@ -222,10 +224,7 @@ def main():
         torch.cuda.synchronize(dev)
         ms = start.elapsed_time(end)
     clk = clocks.stop()
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = float(t.item()) / args.steps
+    ms_step = job_time(ms, world, dev) / args.steps
     value = world * B / (ms_step / 1e3)
 
     # Roofline of the fused kernel (one launch per step), algorithmic FLOPs or bytes.
@@ -273,11 +272,9 @@ def main():
         for _ in range(args.e2e_steps):
             model.forward_batch_parallel(xh, yh)
         e2e_s = (time.perf_counter() - t0) / args.e2e_steps
-        te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_s = job_time(e2e_s, world, dev)
         esz = x.element_size()
-        e2e = {"value": world * B / float(te.item()), "unit": unit, "h2d_bytes_per_step": world * nin * B * esz,
+        e2e = {"value": world * B / e2e_s, "unit": unit, "h2d_bytes_per_step": world * nin * B * esz,
                "d2h_bytes_per_step": world * nout * B * esz,
                "path": "ponni_b200_forward_host (C ABI), pinned host buffers, chunked copy/compute overlap"}
         del xh, yh

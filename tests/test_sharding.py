@@ -1,0 +1,82 @@
+"""The multi-GPU path's host logic on CPU: two gloo ranks shard the batch by
+columns (no data exchange), compute their shards, and reduce their timings to
+the slowest rank's; the gathered shards equal the one-process result."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from ponni_b200 import sharding
+
+NIN, PER_RANK = 5, 777
+
+
+def keyed_inputs(col0: int, n: int) -> np.ndarray:
+    """Inputs keyed by global column (like the device generator): any column
+    range gives the same values whichever rank produces it."""
+    cols = np.arange(col0, col0 + n, dtype=np.uint64)[None, :]
+    feats = np.arange(NIN, dtype=np.uint64)[:, None]
+    h = (cols * np.uint64(0x9E3779B97F4A7C15) + feats * np.uint64(0xBF58476D1CE4E5B9)) & np.uint64((1 << 53) - 1)
+    return (h.astype(np.float64) / float(1 << 53) * 4.0 - 2.0).astype(np.float32)
+
+
+def layers():
+    import ponni_b200 as pb
+    rng = np.random.default_rng(3)
+    return [pb.Matvec(rng.normal(0, 0.5, (NIN, 6))), pb.Bias(rng.normal(0, 0.1, 6)), pb.Relu(6),
+            pb.Matvec(rng.normal(0, 0.5, (6, 2))), pb.Bias(rng.normal(0, 0.1, 2))]
+
+
+def _rank(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    col0, n = sharding.shard_range(rank, world, PER_RANK)
+    y = oracle.forward(layers(), 0, keyed_inputs(col0, n), 1)
+    shards = [torch.empty((2, PER_RANK), dtype=torch.float32) for _ in range(world)]
+    dist.all_gather(shards, torch.from_numpy(np.ascontiguousarray(y)))
+    t = sharding.job_time(0.5 + rank, world)  # rank r "took" 0.5 + r seconds
+    if rank == 0:
+        out.put((torch.cat(shards, dim=1).numpy(), t))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shard_range():
+    assert sharding.shard_range(0, 1, 10) == (0, 10)
+    assert sharding.shard_range(3, 4, 10) == (30, 10)
+    with pytest.raises(ValueError):
+        sharding.shard_range(4, 4, 10)
+    with pytest.raises(ValueError):
+        sharding.shard_range(0, 2, 0)
+    assert sharding.job_time(1.25, 1) == 1.25
+
+
+def test_two_gloo_ranks_match_one_process(oracle_lib):
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    y_sharded, t = out.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    from oracle import oracle
+    y_full = oracle.forward(layers(), 0, keyed_inputs(0, world * PER_RANK), 1)
+    assert np.array_equal(y_sharded, y_full)
+    assert t == 1.5  # the slowest rank's time
