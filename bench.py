@@ -183,7 +183,8 @@ def main():
         model.set_arithmetic(pb._abi.ARITH_AUTO)
     kernel_name = {1: "tile_forward_kernel (SIMT)", 2: "tc_forward_kernel (tcgen05)",
                    3: "narrow_forward_kernel (streaming)",
-                   4: "ponni_narrow_jit (streaming, model-specialised)"}[model.kernel()]
+                   4: "ponni_narrow_jit (streaming, model-specialised)",
+                   5: "ts_forward_kernel (tcgen05, streamed weights)"}[model.kernel()]
     tdt = model.torch_dtype()
     x = torch.empty((nin, B), dtype=tdt, device=dev)
     y = torch.empty((nout, B), dtype=tdt, device=dev)
@@ -235,7 +236,7 @@ def main():
     if cfg.bound == "hbm":
         roof = {"bound": "hbm", "achieved": cfg.bytes_per_sample * B / launch_s / 1e9, "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "peak_source": f"hbm_gbs ({pk_src})"}
-    elif kernel == pb._abi.KERNEL_TENSOR:
+    elif kernel in (pb._abi.KERNEL_TENSOR, pb._abi.KERNEL_TENSOR_STREAM):
         # fp32 models run six bf16 MMAs per multiply-add (exact 3-way operand
         # split), so their tensor roofline is a sixth of the bf16 peak.
         passes = 6 if cfg.dtype == pb.F32 else 1

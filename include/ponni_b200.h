@@ -165,8 +165,10 @@ ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* model, int a
  * 2 = tensor-core kernel, 3 = narrow streaming kernel (chains at most 32
  * wide), 4 = the narrow kernel specialised to this model's structure and
  * compiled at plan time with NVRTC (the counterpart of the reference's
- * per-model code generator; PONNI_B200_NARROW_JIT=0 disables it); 0 on a
- * planning error (see last_error). */
+ * per-model code generator; PONNI_B200_NARROW_JIT=0 disables it), 5 = the
+ * tensor-core kernel with the weights streamed through shared memory layer by
+ * layer (16-bit chains whose weights exceed shared memory, ARITH_TENSOR);
+ * 0 on a planning error (see last_error). */
 int ponni_b200_model_kernel(ponni_b200_model* model);
 
 /* Diagnostic counters of the tensor-core kernel (up to 7 values; per-phase

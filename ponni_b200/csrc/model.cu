@@ -502,7 +502,11 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
                        (m->arithmetic == PONNI_B200_ARITH_AUTO && m->dtype == PONNI_B200_F32 && widest > 16);
   if (want_tc) {
     std::vector<unsigned char> image;
-    if (tc_plan(m, m->tcp, image, m->tc_why)) {
+    // PONNI_B200_TC_STREAM=1 (a test aid) sends eligible 16-bit chains to the
+    // streamed-weights kernel even when their weights fit shared memory.
+    const char* force_stream = getenv("PONNI_B200_TC_STREAM");
+    const bool stream_first = force_stream && force_stream[0] == '1' && m->dtype != PONNI_B200_F32;
+    if (!stream_first && tc_plan(m, m->tcp, image, m->tc_why)) {
       if (image.size() > m->tc_image_bytes) {
         if (m->tc_image_dev) cudaFree(m->tc_image_dev);
         m->tc_image_dev = nullptr;
@@ -525,7 +529,30 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       m->tc_grid = m->num_sms;  // one persistent CTA (up to four tile slots) per SM
       m->kernel = 2;
     } else if (m->arithmetic == PONNI_B200_ARITH_TENSOR) {
-      return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED, "tensor-core kernel unavailable: " + m->tc_why);
+      // Weights beyond shared memory: stream them per layer (16-bit models).
+      std::string why2;
+      if (!ts_plan(m, m->tsp, image, why2))
+        return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED,
+                       "tensor-core kernel unavailable: " + (m->tc_why.empty() ? why2 : m->tc_why + "; " + why2));
+      if (image.size() > m->ts_image_bytes) {
+        if (m->ts_image_dev) cudaFree(m->ts_image_dev);
+        m->ts_image_dev = nullptr;
+        m->ts_image_bytes = 0;
+        e = cudaMalloc(&m->ts_image_dev, image.size());
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(streamed tensor-core parameters)");
+        m->ts_image_bytes = image.size();
+      }
+      if (!m->err_dev) {
+        e = cudaMalloc(&m->err_dev, 64);
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(error word)");
+        e = cudaMemsetAsync(m->err_dev, 0, 64, m->stream);
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMemset(error word)");
+      }
+      e = cudaMemcpyAsync(m->ts_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+      if (e != cudaSuccess) return cuda_fail(m, e, "streamed tensor-core parameter upload");
+      m->tc_grid = m->num_sms;
+      m->kernel = 5;
     }
   }
   // Narrow chains (every width <= 32) stream through registers, unless the
@@ -667,12 +694,14 @@ ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, i
 
 void ponni_b200_model_destroy(ponni_b200_model* m) {
   if (!m) return;
-  if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev || m->prog_dev) {
+  if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev || m->prog_dev ||
+      m->ts_image_dev) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
     if (m->packed_dev) cudaFree(m->packed_dev);
     if (m->prog_dev) cudaFree(m->prog_dev);
+    if (m->ts_image_dev) cudaFree(m->ts_image_dev);
     if (m->stage_dev) cudaFree(m->stage_dev);
     if (m->tc_image_dev) cudaFree(m->tc_image_dev);
     if (m->err_dev) cudaFree(m->err_dev);
@@ -750,6 +779,10 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + m->tcp.slots - 1) / m->tcp.slots);
     e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
+  } else if (m->kernel == 5) {
+    const int64_t ntiles = (batch + kTcM - 1) / kTcM;
+    const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
+    e = launch_ts_forward(m->tsp, m->ts_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
   } else if (m->kernel == 4) {
     e = narrow_jit_launch(m->jit, input, in_ld, output, out_ld, batch, s);
   } else if (m->kernel == 3) {

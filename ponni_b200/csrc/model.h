@@ -10,6 +10,7 @@
 #include "narrow_jit.h"
 #include "narrow_kernel.h"
 #include "tc_program.h"
+#include "tc_stream.h"
 
 namespace ponni_b200 {
 
@@ -56,7 +57,8 @@ struct ponni_b200_model {
   // Tensor-core dense-chain kernel (planned when eligible and allowed).
   int arithmetic = PONNI_B200_ARITH_AUTO;  // ponni_b200_arithmetic requested
   int kernel = 0;       // 1 tile (SIMT), 2 tensor-core, 3 narrow streaming kernel, 4 its model-specialised
-                        // (NVRTC-compiled) form; 0 = not planned yet
+                        // (NVRTC-compiled) form, 5 tensor-core kernel with streamed weights;
+                        // 0 = not planned yet
   int narrow_maxw = 0;
   ponni_b200::NarrowLaunch narrow;     // narrow kernel launch configuration
   void* prog_dev = nullptr;            // the Program in device memory (narrow kernel)
@@ -66,6 +68,9 @@ struct ponni_b200_model {
   void* tc_image_dev = nullptr;
   size_t tc_image_bytes = 0;
   int tc_grid = 0;
+  ponni_b200::TsProgram tsp;            // streamed-weights tensor-core kernel (kernel 5)
+  void* ts_image_dev = nullptr;
+  size_t ts_image_bytes = 0;
   int* err_dev = nullptr;  // device error word (bounded waits that gave up)
   std::string tc_why;      // why the tensor-core kernel is not used
 

@@ -11,6 +11,7 @@
 
 #include "model.h"
 #include "tc_plan.h"
+#include "tc_stream.h"
 
 namespace ponni_b200 {
 namespace {
@@ -191,6 +192,98 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   }
   why = "weights and operand tiles exceed shared memory";
   return false;
+}
+
+bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>& image, std::string& why) {
+  memset(&p, 0, sizeof(p));
+  image.clear();
+  const ponni_b200_dtype dt = m->dtype;
+  if (dt != PONNI_B200_F16 && dt != PONNI_B200_BF16) {
+    why = "the streamed tensor-core path supports fp16 and bf16 models";
+    return false;
+  }
+  const size_t msz = dtype_bytes(dt);
+  struct Blk { const Layer* mv; const Layer* bias; const Layer* act; };
+  std::vector<Blk> blocks;
+  const auto& Ls = m->layers;
+  for (size_t i = 0; i < Ls.size();) {
+    if (Ls[i].d.kind != PONNI_B200_MATVEC) {
+      why = std::string("layer ") + layer_label(Ls[i].d.kind) + " is outside a dense chain";
+      return false;
+    }
+    Blk b{&Ls[i], nullptr, nullptr};
+    ++i;
+    if (i < Ls.size() && Ls[i].d.kind == PONNI_B200_BIAS) b.bias = &Ls[i++];
+    if (i < Ls.size() && tc_activation(Ls[i].d.kind)) b.act = &Ls[i++];
+    blocks.push_back(b);
+  }
+  if (blocks.empty() || blocks.size() > (size_t)kTsMaxLayers) {
+    why = "dense chain length out of range";
+    return false;
+  }
+  p.n_layers = (int)blocks.size();
+  p.dtype = (int)dt;
+  p.fast_act = 1;
+  p.nin = blocks.front().mv->d.num_inputs;
+  p.nout = blocks.back().mv->d.num_outputs;
+  uint64_t off = 0;
+  uint32_t a_blocks = 1;
+  for (int l = 0; l < p.n_layers; ++l) {
+    const auto& d = blocks[l].mv->d;
+    if (d.num_inputs > 256 || d.num_outputs > 256) {
+      why = "layer wider than 256";
+      return false;
+    }
+    TsLayer& L = p.layers[l];
+    L.nin = d.num_inputs;
+    L.nout = d.num_outputs;
+    L.k_pad = (int)round_up(d.num_inputs, 16);
+    L.n_pad = (int)round_up(d.num_outputs, 16);
+    L.nblk = (L.n_pad + kTsBlockN - 1) / kTsBlockN;
+    L.kblk = (L.k_pad + kTsBlockK - 1) / kTsBlockK;
+    L.act = blocks[l].act ? blocks[l].act->d.kind : EPI_NONE;
+    L.act_flags = blocks[l].act ? blocks[l].act->d.flags : 0;
+    L.s0 = blocks[l].act ? (float)blocks[l].act->d.scalar[0] : 0.f;
+    L.s1 = blocks[l].act ? (float)blocks[l].act->d.scalar[1] : 0.f;
+    L.has_bias = blocks[l].bias ? 1 : 0;
+    L.w_off = off;
+    off += (uint64_t)L.nblk * L.kblk * kTsChunkBytes;
+    if (l + 1 < p.n_layers) a_blocks = std::max(a_blocks, (uint32_t)((L.n_pad + 63) / 64));
+  }
+  for (int l = 0; l < p.n_layers; ++l) {
+    p.layers[l].bias_off = (uint32_t)off;
+    off += (uint64_t)round_up(round_up(p.layers[l].n_pad, 32) * 4, 16);
+  }
+  p.image_bytes = round_up((int64_t)off, 1024);
+  image.assign(p.image_bytes, 0);
+  for (int l = 0; l < p.n_layers; ++l) {
+    const TsLayer& L = p.layers[l];
+    const Layer& mv = *blocks[l].mv;
+    if (blocks[l].bias) {
+      float* b = reinterpret_cast<float*>(image.data() + L.bias_off);
+      for (int f = 0; f < L.nout; ++f) b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
+    }
+    for (int n = 0; n < L.nout; ++n) {
+      const int nb = n / kTsBlockN, r = n % kTsBlockN;
+      const int rows = std::min(kTsBlockN, L.n_pad - nb * kTsBlockN);
+      for (int k = 0; k < L.nin; ++k) {
+        const int kb = k / kTsBlockK;
+        const size_t chunk = L.w_off + ((size_t)nb * L.kblk + kb) * kTsChunkBytes;
+        put_kmajor(image, chunk, rows, r, k % kTsBlockK, 2, mv.params.data() + ((size_t)k * L.nout + n) * msz);
+      }
+    }
+  }
+  p.a_bytes = a_blocks * (uint32_t)(kTcM * 128);
+  p.stage_bytes = (uint32_t)(p.layers[0].k_pad / 8) * 2048;
+  const uint32_t fixed = 1024 + 2 * p.a_bytes + p.stage_bytes + 256 + (uint32_t)(kTsMaxLayers * sizeof(TsLayer));
+  const uint32_t budget = 227 * 1024;
+  if (fixed + 2 * kTsChunkBytes > budget) {
+    why = "operand tiles exceed shared memory";
+    return false;
+  }
+  p.ring_stages = std::min<uint32_t>(kTsMaxStages, (budget - fixed) / kTsChunkBytes);
+  p.smem_bytes = fixed + p.ring_stages * kTsChunkBytes;
+  return true;
 }
 
 }  // namespace ponni_b200

@@ -1,0 +1,60 @@
+// Tensor-core dense-chain kernel with the weights streamed from HBM/L2
+// (tc_stream.cu), for 16-bit chains whose weights exceed shared memory
+// (the 64->256x5->32 bf16 network: 573 KB of weights).
+//
+// Work unit ("job"): one layer's 128-column block of the accumulator for one
+// tile of 128 batch columns, D[128 x N<=128] = A[128 x K] * B[N x K]^T, with
+// B streamed in chunks of K = 64 (one 128-byte swizzle block: N rows x
+// 128 B <= 16 KB) through a ring of shared-memory stages.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+struct ponni_b200_model;
+
+namespace ponni_b200 {
+
+constexpr int kTsMaxLayers = 16;
+constexpr int kTsBlockN = 128;                  // accumulator columns of one job
+constexpr int kTsBlockK = 64;                   // K elements of one streamed chunk
+constexpr int kTsChunkBytes = kTsBlockN * 128;  // chunk stride (rows x 128 B)
+constexpr int kTsEpiWarps = 8;                  // 4 TMEM lane quarters x 2 column halves
+constexpr int kTsThreads = (kTsEpiWarps + 2) * 32;  // + producer warp + MMA warp
+constexpr int kTsMaxStages = 8;
+
+struct TsLayer {
+  int32_t nin, nout;
+  int32_t k_pad, n_pad;  // K rounded to 16, N rounded to 16
+  int32_t nblk, kblk;    // column blocks of 128, K chunks of 64
+  int32_t act, act_flags;
+  float s0, s1;
+  int32_t has_bias;
+  uint32_t bias_off;     // byte offset of float bias[round_up(n_pad, 32)] in the image
+  uint64_t w_off;        // byte offset of chunk (nb = 0, kb = 0); chunk (nb, kb) at + (nb*kblk + kb) * 16 KB
+};
+
+struct TsProgram {
+  int32_t n_layers;
+  int32_t dtype;          // ponni_b200_dtype: 2 f16, 3 bf16
+  int32_t nin, nout;
+  int32_t fast_act;       // SiLU / sigmoid / tanh through tanh.approx (fp32 accumulation mode)
+  uint32_t a_bytes;       // one K-major activation operand buffer (two, ping-pong)
+  uint32_t stage_bytes;   // MN-major layer-0 input stage
+  uint32_t ring_stages;   // weight ring stages of kTsChunkBytes
+  uint32_t smem_bytes;    // dynamic shared memory requested
+  uint64_t image_bytes;   // weight chunks + biases
+  TsLayer layers[kTsMaxLayers];
+};
+
+// Plan the streamed kernel for a Matvec[Bias][activation] chain of a 16-bit
+// model; builds the chunked, pre-swizzled weight image.  False with `why`
+// when not eligible.
+bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>& image, std::string& why);
+
+cudaError_t launch_ts_forward(const TsProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
+                              int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream);
+
+}  // namespace ponni_b200

@@ -116,3 +116,65 @@ def test_tc_ineligible_falls_back_or_errors():
     m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=pb._abi.ARITH_TENSOR)
     with pytest.raises(pb.PonniError):
         m.kernel()
+
+
+# ---- streamed-weights kernel (weights beyond shared memory) ----
+
+def run_ts(layers, dtype, x_raw, monkeypatch=None):
+    if monkeypatch is not None:
+        monkeypatch.setenv("PONNI_B200_TC_STREAM", "1")
+    m = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_STREAM
+    y = m.forward_batch_parallel(to_torch(x_raw, dtype).cuda())
+    m.synchronize()
+    torch.cuda.synchronize()
+    return from_torch(y, dtype)
+
+
+@pytest.mark.parametrize("batch", [1, 129, 3000])
+def test_ts_cfg5(batch, oracle_lib):
+    """The wide bf16 chain (573 KB of weights) streams its weights."""
+    cfg = configs.cfg5(batch=batch)
+    x = configs.host_inputs(cfg, batch)
+    y = run_ts(cfg.layers, cfg.dtype, x)
+    check_acc32(y, cfg.layers, cfg.dtype, x, oracle_lib)
+
+
+@pytest.mark.parametrize("dtype", [pb.F16, pb.BF16])
+@pytest.mark.parametrize("batch", [3, 1000, 5000])
+def test_ts_forced_cfg3(dtype, batch, oracle_lib, monkeypatch):
+    cfg = configs.cfg3(batch=batch)
+    x = pb.to_dtype_bytes(K.as_float(configs.host_inputs(cfg, batch), cfg.dtype), dtype)
+    y = run_ts(cfg.layers, dtype, x, monkeypatch)
+    check_acc32(y, cfg.layers, dtype, x, oracle_lib)
+
+
+@pytest.mark.parametrize("dtype", [pb.F16, pb.BF16])
+def test_ts_odd_widths_all_activations(dtype, oracle_lib, monkeypatch):
+    rng = np.random.default_rng(12)
+    dims = [3, 17, 40, 130, 9, 256, 5]
+    acts = [pb.Relu, pb.Silu, pb.Gelu, pb.Tanh, pb.Sigmoid, lambda n: pb.LeakyRelu(n, 0.2)]
+    layers = []
+    for i in range(len(dims) - 1):
+        layers.append(pb.Matvec(rng.normal(0, 1.0 / np.sqrt(dims[i]), (dims[i], dims[i + 1]))))
+        if i % 2 == 0:
+            layers.append(pb.Bias(rng.normal(0, 0.1, dims[i + 1])))
+        if i < len(dims) - 2:
+            layers.append(acts[i % len(acts)](dims[i + 1]))
+    x = pb.to_dtype_bytes(rng.normal(0, 1, (3, 777)), dtype)
+    y = run_ts(layers, dtype, x, monkeypatch)
+    check_acc32(y, layers, dtype, x, oracle_lib)
+
+
+def test_ts_strided_misaligned(oracle_lib):
+    cfg = configs.cfg5(batch=1000)
+    x = configs.host_inputs(cfg, 1000)
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_STREAM
+    big = torch.zeros((64, 1000 + 17), dtype=torch.bfloat16, device="cuda")
+    big[:, 3:1003] = to_torch(x, cfg.dtype).cuda()
+    out_big = torch.full((32, 1009), float("nan"), dtype=torch.bfloat16, device="cuda")
+    m.forward_batch_parallel(big[:, 3:1003], out_big[:, 1:1001])
+    m.synchronize()
+    check_acc32(from_torch(out_big[:, 1:1001].contiguous(), cfg.dtype), cfg.layers, cfg.dtype, x, oracle_lib)
+    assert torch.isnan(out_big[:, 0].float()).all() and torch.isnan(out_big[:, 1001:].float()).all()
