@@ -3,17 +3,17 @@
 // For 16-bit Matvec[Bias][activation] chains whose weights do not fit in
 // shared memory next to the operand tiles (e.g. 64->256x5->32 bf16: 573 KB).
 // One persistent CTA per SM, warp-specialised:
-//   producer (warp 8, one thread): streams the pre-swizzled weight chunks of
+//   producer (warp 16, one thread): streams the pre-swizzled weight chunks of
 //     every job, in job order, from global memory (L2-resident: every CTA
 //     reads the same image) into a ring of shared-memory stages with 1-D bulk
 //     copies (cp.async.bulk, completion counted in bytes on the stage's
 //     "full" mbarrier; no multicast);
-//   MMA issuer (warp 9, one thread): per job (layer l, column block nb of
+//   MMA issuer (warp 17, one thread): per job (layer l, column block nb of
 //     128) issues D[128 x N] += A[128 x K] * B[N x K]^T chunk by chunk
 //     (tcgen05.mma kind::f16, fp32 accumulator in TMEM columns nb*128...),
 //     frees each ring stage with tcgen05.commit and signals the finished job
 //     on the block's "acc full" mbarrier;
-//   epilogue (warps 0-7: 4 TMEM lane quarters x 2 column halves): per job,
+//   epilogue (warps 0-15: 4 TMEM lane quarters x 4 column quarters): per job,
 //     tcgen05.ld of the accumulator, bias, activation (reference fused
 //     epilogue, src/ponni_Inference.h:416-444), and the next layer's K-major
 //     operand (ping-pong buffers A0/A1) or the caller's output; then signals
@@ -23,10 +23,10 @@
 // A job's epilogue overlaps the MMAs of the next column block; a layer's
 // MMAs start when every block of the previous layer has been written.
 //
-// In this fp32-accumulation mode SiLU, sigmoid and tanh use the hardware
-// tanh approximation (sigmoid(x) = (1 + tanh(x/2)) / 2), whose error is far
-// below one fp16/bf16 unit; the epilogue then needs one MUFU operation per
-// value, which keeps it under the MMA time.
+// In this fp32-accumulation mode SiLU and sigmoid use the hardware base-2
+// exponential and reciprocal approximations (two full-rate MUFU operations
+// per value) and tanh the hardware tanh approximation; their errors are far
+// below one unit of the 16-bit model type.
 //
 // Every wait is bounded; a role that gives up raises a shared abort flag
 // (the others see it and leave), records an error code, and the CTA drains
@@ -44,6 +44,19 @@ namespace {
 using namespace tc;
 
 constexpr long long kWaitCycles = 1ll << 31;
+
+// Optional phase timing (compiled only with -DPONNI_B200_TC_PROFILE): each
+// role sums the cycles of its waits locally and adds them once per CTA to
+// the diagnostic counters after the error word.
+#ifdef PONNI_B200_TC_PROFILE
+#define TS_T(var) const long long var = clock64()
+#define TS_ACC(acc, t0) acc += clock64() - (t0)
+#define TS_FLUSH(idx, acc) atomicAdd(reinterpret_cast<unsigned long long*>(err) + (idx), (unsigned long long)(acc))
+#else
+#define TS_T(var)
+#define TS_ACC(acc, t0)
+#define TS_FLUSH(idx, acc)
+#endif
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
@@ -92,10 +105,7 @@ __device__ __forceinline__ float ts_act(float x, int fast, int flags, float s0, 
   } else if constexpr (ACT == EPI_SILU || ACT == EPI_SIGMOID || ACT == EPI_TANH) {
     if (fast) {
       if constexpr (ACT == EPI_TANH) return tanh_fast(x);
-      const float h = 0.5f * x;
-      const float sg = fmaf(0.5f, tanh_fast(h), 0.5f);
-      if constexpr (ACT == EPI_SIGMOID) return sg;
-      else return x * sg;
+      else return x * 0.f;  // SiLU / sigmoid take ts_act32's fast path
     }
     return activation<float>(ACT, flags, x, s0, s1);
   } else {
@@ -103,23 +113,55 @@ __device__ __forceinline__ float ts_act(float x, int fast, int flags, float s0, 
   }
 }
 
+// sigmoid(x) = 1 / (1 + 2^(-x log2 e)) with the hardware base-2 exponential
+// and reciprocal approximations (relative error near 2^-22 each): two
+// full-rate MUFU operations per value.
+__device__ __forceinline__ float sigmoid_fast(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(e) : "f"(x * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(1.0f + e));
+  return r;
+}
+
+// Activation of 32 values; in the fast mode SiLU and sigmoid use
+// sigmoid_fast, tanh the fp32 tanh approximation.
+template <int ACT>
+__device__ __forceinline__ void ts_act32(float (&v)[32], int fast, int flags, float s0, float s1) {
+  if constexpr (ACT == EPI_SILU || ACT == EPI_SIGMOID) {
+    if (fast) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float g = sigmoid_fast(v[j]);
+        v[j] = ACT == EPI_SILU ? v[j] * g : g;
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = ts_act<ACT>(v[j], fast, flags, s0, s1);
+}
+
 struct TsShared {
   uint32_t a[2], stage, ring, full, empty, accf, epi_done, stage_full, drain;
 };
 
-// Epilogue of the 64 columns [c_begin, c_begin + 64) of job (l, nb) for
-// this thread's row m.
+// Epilogue of the columns [c_begin, c_begin + kTsColsPerWarp) of job
+// (l, nb) for this thread's row m.
 template <class T, int ACT>
 __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool last, uint32_t tmem_row, int c_begin,
                                             const float* __restrict__ bias, uint32_t a_out, T* __restrict__ out,
-                                            int64_t out_ld, int64_t col, int64_t batch, int m) {
+                                            int64_t out_ld, int64_t col, int64_t batch, int m, long long (&t_ph)[3]) {
+  (void)t_ph;
   using Op = typename OperandOf<T>::type;
   const int n_pad = L.n_pad, nout = L.nout, has_bias = L.has_bias, flags = L.act_flags;
   const float s0 = L.s0, s1 = L.s1;
 #pragma unroll 1
-  for (int c0 = c_begin; c0 < c_begin + 64 && c0 < n_pad; c0 += 32) {
+  for (int c0 = c_begin; c0 < c_begin + kTsColsPerWarp && c0 < n_pad; c0 += 32) {
     float v[32];
+    TS_T(tl);
     tmem_ld32(tmem_row + (uint32_t)c0, v);
+    TS_ACC(t_ph[0], tl);
+    TS_T(ta);
     if (has_bias) {
       const float4* b4 = reinterpret_cast<const float4*>(bias + c0);
 #pragma unroll
@@ -132,8 +174,7 @@ __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool las
       }
     }
     if (last) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = ts_act<ACT>(v[j], fast, flags, s0, s1);
+      ts_act32<ACT>(v, fast, flags, s0, s1);
       if (col < batch) {
         const int nv = min(32, nout - c0);
         T* o = out + (int64_t)c0 * out_ld + col;
@@ -144,11 +185,20 @@ __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool las
         }
       }
     } else {
+      ts_act32<ACT>(v, fast, flags, s0, s1);
+#ifdef PONNI_B200_TC_PROFILE
+      // make the timing see the activation results before the stores
+      float sink = 0.f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = ts_act<ACT>(v[j], fast, flags, s0, s1);
+      for (int j = 0; j < 32; ++j) sink += v[j];
+      if (sink == 12345.678f) v[0] += 1e-30f;
+#endif
+      TS_ACC(t_ph[1], ta);
+      TS_T(ts);
       const uint32_t a[1] = {a_out};
 #pragma unroll
       for (int q = 0; q < 4; ++q) store_row8<T>(a, m, c0 + 8 * q, v + 8 * q);
+      TS_ACC(t_ph[2], ts);
     }
   }
   (void)sizeof(Op);
@@ -158,8 +208,9 @@ template <class T>
 __device__ __forceinline__ void ts_epilogue_dispatch(const TsLayer& L, int fast, bool last, uint32_t tmem_row,
                                                      int c_begin, const float* bias, uint32_t a_out,
                                                      T* __restrict__ out, int64_t out_ld, int64_t col, int64_t batch,
-                                                     int m) {
-#define PONNI_TS_EPI(A) ts_epilogue<T, A>(L, fast, last, tmem_row, c_begin, bias, a_out, out, out_ld, col, batch, m)
+                                                     int m, long long (&t_ph)[3]) {
+#define PONNI_TS_EPI(A) \
+  ts_epilogue<T, A>(L, fast, last, tmem_row, c_begin, bias, a_out, out, out_ld, col, batch, m, t_ph)
   switch (L.act) {
     case EPI_RELU: PONNI_TS_EPI(EPI_RELU); break;
     case EPI_LEAKY_RELU: PONNI_TS_EPI(EPI_LEAKY_RELU); break;
@@ -205,7 +256,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   if ((int64_t)blockIdx.x >= ntiles) return;
 
   // ---- set-up ----
-  if (warp == 9) tmem_alloc(s_tmem, 256);
+  if (warp == kTsMmaWarp) tmem_alloc(s_tmem, 256);
   if (tid == 0) {
     for (int r = 0; r < R; ++r) {
       mbar_init(S.full + 8u * r, 1);
@@ -233,11 +284,13 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   const int nl = p.n_layers;
   const int64_t stride = gridDim.x;
 
-  if (warp == 8) {
+  if (warp == kTsProducerWarp) {
     // ------------------------------------------------ producer ----
     if (lane == 0) {
       uint32_t use = 0;
       bool ok = true;
+      long long w_empty = 0;
+      (void)w_empty;
       for (int64_t t = blockIdx.x; t < ntiles && ok; t += stride) {
         for (int l = 0; l < nl && ok; ++l) {
           const TsLayer& L = layers[l];
@@ -245,10 +298,12 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             const uint32_t bytes = (uint32_t)min(kTsBlockN, L.n_pad - nb * kTsBlockN) * 128u;
             for (int kb = 0; kb < L.kblk; ++kb) {
               const uint32_t r = use % (uint32_t)R;
+              TS_T(t0);
               if (use >= (uint32_t)R && !wait_phase(S.empty + 8u * r, ((use / R) - 1) & 1u, abort_flag)) {
                 ok = false;
                 break;
               }
+              TS_ACC(w_empty, t0);
               mbar_expect_tx(S.full + 8u * r, bytes);
               bulk_load(S.ring + r * kTsChunkBytes,
                         image + L.w_off + ((uint64_t)nb * L.kblk + kb) * kTsChunkBytes, bytes, S.full + 8u * r);
@@ -267,20 +322,26 @@ __global__ void __launch_bounds__(kTsThreads, 1)
       if (!ok) atomicExch(err, 2);
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == kTsMmaWarp) {
     // --------------------------------------------- MMA issuer ----
     if (lane == 0) {
       uint32_t use = 0, st_ph = 0, epi_ph[2] = {0, 0};
       int prev_nblk = 0;
       bool ok = true;
+      long long w_stage = 0, w_epi = 0, w_full = 0;
+      (void)w_stage; (void)w_epi; (void)w_full;
+      TS_T(t_all);
       const uint64_t a_stage = smem_desc(S.stage, 1024, 2048);
       for (int64_t t = blockIdx.x; t < ntiles && ok; t += stride) {
         for (int l = 0; l < nl && ok; ++l) {
           const TsLayer& L = layers[l];
           if (l == 0) {
+            TS_T(t0);
             if (!(ok = wait_phase(S.stage_full, st_ph, abort_flag))) break;
+            TS_ACC(w_stage, t0);
             st_ph ^= 1u;
           }
+          TS_T(t1);
           // Every block of the previous job layer written (operand A ready,
           // accumulator columns free).
           for (int b = 0; b < prev_nblk && ok; ++b) {
@@ -288,6 +349,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             epi_ph[b] ^= 1u;
           }
           if (!ok) break;
+          TS_ACC(w_epi, t1);
           tc_fence_after();
           const int nsteps = L.k_pad / 16;
           const uint64_t a_in = smem_desc(S.a[(l + 1) & 1], 16, 1024);  // written by the epilogue of layer l-1
@@ -297,7 +359,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             const uint32_t d = tmem_base + (uint32_t)(nb * kTsBlockN);
             for (int kb = 0; kb < L.kblk; ++kb) {
               const uint32_t r = use % (uint32_t)R;
+              TS_T(t2);
               if (!(ok = wait_phase(S.full + 8u * r, (use / R) & 1u, abort_flag))) break;
+              TS_ACC(w_full, t2);
               tc_fence_after();
               const uint64_t b0 = smem_desc(S.ring + r * kTsChunkBytes, 16, 1024);
               const int s_end = min(nsteps, kb * 4 + 4);
@@ -320,6 +384,10 @@ __global__ void __launch_bounds__(kTsThreads, 1)
       while (!mbar_try_wait(S.drain, 0))
         if (clock64() - t0 > kWaitCycles) break;
       if (!ok) atomicExch(err, 3);
+      TS_FLUSH(1, w_epi);
+#ifdef PONNI_B200_TC_PROFILE
+      TS_FLUSH(7, clock64() - t_all);
+#endif
     }
     __syncwarp();
   } else {
@@ -330,6 +398,8 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     const bool vec = in_vec != 0;
     uint32_t acc_ph[2] = {0, 0};
     bool ok = true;
+    long long w_acc = 0, c_epi = 0, c_sig = 0, t_ph[3] = {0, 0, 0};
+    (void)w_acc; (void)c_epi; (void)c_sig;
     int64_t t = blockIdx.x;
     load_input<T, kTsEpiWarps * 32>(S.stage, in, in_ld, p.nin, t * kTcM, batch, vec, tid);
     cp_async_commit();
@@ -348,9 +418,12 @@ __global__ void __launch_bounds__(kTsThreads, 1)
         for (int nb = 0; nb < L.nblk; ++nb) {
           // One lane waits, the warp follows (the TMEM loads are warp-collective).
           int got = 0;
+          TS_T(t0);
           if (lane == 0) got = wait_phase(S.accf + 8u * nb, acc_ph[nb], abort_flag) ? 1 : 0;
           got = __shfl_sync(0xffffffffu, got, 0);
           if (!(ok = got != 0)) break;
+          TS_ACC(w_acc, t0);
+          TS_T(t1);
           acc_ph[nb] ^= 1u;
           tc_fence_after();
           if (l == 0 && nb == L.nblk - 1 && next < ntiles) {
@@ -358,12 +431,15 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             load_input<T, kTsEpiWarps * 32>(S.stage, in, in_ld, p.nin, next * kTcM, batch, vec, tid);
             cp_async_commit();
           }
-          ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, nb * kTsBlockN + ch * 64, bias, a_out, out, out_ld,
-                                  col, batch, m);
+          ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, nb * kTsBlockN + ch * kTsColsPerWarp, bias, a_out, out, out_ld,
+                                  col, batch, m, t_ph);
+          TS_T(t2);
           fence_proxy_async();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(S.epi_done + 8u * nb);
+          TS_ACC(c_sig, t2);
+          TS_ACC(c_epi, t1);
         }
       }
       if (ok && next < ntiles) {
@@ -375,11 +451,18 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     }
     cp_async_wait_0();
     if (!ok && lane == 0) atomicExch(err, 4);
+    if (tid == 0) {
+      TS_FLUSH(3, t_ph[0]);
+      TS_FLUSH(2, t_ph[1]);
+      TS_FLUSH(6, t_ph[2]);
+      TS_FLUSH(4, w_acc);
+      TS_FLUSH(5, c_epi);
+    }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kTsMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 256);
   }

@@ -21,7 +21,10 @@ constexpr int kTsMaxLayers = 16;
 constexpr int kTsBlockN = 128;                  // accumulator columns of one job
 constexpr int kTsBlockK = 64;                   // K elements of one streamed chunk
 constexpr int kTsChunkBytes = kTsBlockN * 128;  // chunk stride (rows x 128 B)
-constexpr int kTsEpiWarps = 8;                  // 4 TMEM lane quarters x 2 column halves
+constexpr int kTsEpiWarps = 16;                 // 4 TMEM lane quarters x 4 column quarters
+constexpr int kTsColsPerWarp = kTsBlockN / (kTsEpiWarps / 4);  // accumulator columns per warp and job
+constexpr int kTsProducerWarp = kTsEpiWarps;
+constexpr int kTsMmaWarp = kTsEpiWarps + 1;
 constexpr int kTsThreads = (kTsEpiWarps + 2) * 32;  // + producer warp + MMA warp
 constexpr int kTsMaxStages = 8;
 
@@ -40,7 +43,7 @@ struct TsProgram {
   int32_t n_layers;
   int32_t dtype;          // ponni_b200_dtype: 2 f16, 3 bf16
   int32_t nin, nout;
-  int32_t fast_act;       // SiLU / sigmoid / tanh through tanh.approx (fp32 accumulation mode)
+  int32_t fast_act;       // SiLU / sigmoid / tanh through the hardware approximations (fp32 accumulation mode)
   uint32_t a_bytes;       // one K-major activation operand buffer (two, ping-pong)
   uint32_t stage_bytes;   // MN-major layer-0 input stage
   uint32_t ring_stages;   // weight ring stages of kTsChunkBytes
