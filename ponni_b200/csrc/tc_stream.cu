@@ -341,23 +341,33 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             TS_ACC(w_stage, t0);
             st_ph ^= 1u;
           }
-          TS_T(t1);
-          // Every block of the previous job layer written (operand A ready,
-          // accumulator columns free).
-          for (int b = 0; b < prev_nblk && ok; ++b) {
-            ok = wait_phase(S.epi_done + 8u * b, epi_ph[b], abort_flag);
-            epi_ph[b] ^= 1u;
-          }
-          if (!ok) break;
-          TS_ACC(w_epi, t1);
-          tc_fence_after();
+          // Dependencies on the previous job layer (l - 1, or the last layer
+          // of the previous tile), per chunk: the accumulator block nb must
+          // have been read out, and for l >= 1 the operand K block kb must
+          // have been written (by the epilogue of block kb*64/128).  So a
+          // layer's first chunks start while the previous layer's last block
+          // is still in its epilogue.
+          bool waited[2] = {false, false};
+          auto need = [&](int b) {
+            if (ok && b < prev_nblk && !waited[b]) {
+              TS_T(tw);
+              ok = wait_phase(S.epi_done + 8u * b, epi_ph[b], abort_flag);
+              TS_ACC(w_epi, tw);
+              epi_ph[b] ^= 1u;
+              waited[b] = true;
+              tc_fence_after();
+            }
+          };
           const int nsteps = L.k_pad / 16;
           const uint64_t a_in = smem_desc(S.a[(l + 1) & 1], 16, 1024);  // written by the epilogue of layer l-1
           for (int nb = 0; nb < L.nblk && ok; ++nb) {
             const int rows = min(kTsBlockN, L.n_pad - nb * kTsBlockN);
             const uint32_t idesc = idesc_of(p.dtype, rows, l == 0);
             const uint32_t d = tmem_base + (uint32_t)(nb * kTsBlockN);
-            for (int kb = 0; kb < L.kblk; ++kb) {
+            need(nb);
+            for (int kb = 0; kb < L.kblk && ok; ++kb) {
+              if (l > 0) need(kb * kTsBlockK / kTsBlockN);
+              if (!ok) break;
               const uint32_t r = use % (uint32_t)R;
               TS_T(t2);
               if (!(ok = wait_phase(S.full + 8u * r, (use / R) & 1u, abort_flag))) break;
@@ -375,6 +385,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             }
             if (ok) umma_commit(S.accf + 8u * nb);
           }
+          // Consume the remaining completions of the previous layer's blocks
+          // (keeps every barrier's phase accounting one-to-one).
+          for (int b = 0; b < prev_nblk; ++b) need(b);
           prev_nblk = L.nblk;
         }
       }
@@ -385,6 +398,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
         if (clock64() - t0 > kWaitCycles) break;
       if (!ok) atomicExch(err, 3);
       TS_FLUSH(1, w_epi);
+      TS_FLUSH(6, w_full);
 #ifdef PONNI_B200_TC_PROFILE
       TS_FLUSH(7, clock64() - t_all);
 #endif
@@ -454,7 +468,6 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     if (tid == 0) {
       TS_FLUSH(3, t_ph[0]);
       TS_FLUSH(2, t_ph[1]);
-      TS_FLUSH(6, t_ph[2]);
       TS_FLUSH(4, w_acc);
       TS_FLUSH(5, c_epi);
     }
