@@ -230,7 +230,7 @@ bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>
   uint32_t a_blocks = 1;
   for (int l = 0; l < p.n_layers; ++l) {
     const auto& d = blocks[l].mv->d;
-    if (d.num_inputs > 256 || d.num_outputs > 256) {
+    if (d.num_inputs > kTsMaxN || d.num_outputs > kTsMaxN) {
       why = "layer wider than 256";
       return false;
     }
@@ -239,7 +239,6 @@ bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>
     L.nout = d.num_outputs;
     L.k_pad = (int)round_up(d.num_inputs, 16);
     L.n_pad = (int)round_up(d.num_outputs, 16);
-    L.nblk = (L.n_pad + kTsBlockN - 1) / kTsBlockN;
     L.kblk = (L.k_pad + kTsBlockK - 1) / kTsBlockK;
     L.act = blocks[l].act ? blocks[l].act->d.kind : EPI_NONE;
     L.act_flags = blocks[l].act ? blocks[l].act->d.flags : 0;
@@ -247,7 +246,7 @@ bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>
     L.s1 = blocks[l].act ? (float)blocks[l].act->d.scalar[1] : 0.f;
     L.has_bias = blocks[l].bias ? 1 : 0;
     L.w_off = off;
-    off += (uint64_t)L.nblk * L.kblk * kTsChunkBytes;
+    off += (uint64_t)L.kblk * kTsChunkBytes;
     if (l + 1 < p.n_layers) a_blocks = std::max(a_blocks, (uint32_t)((L.n_pad + 63) / 64));
   }
   for (int l = 0; l < p.n_layers; ++l) {
@@ -263,19 +262,15 @@ bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>
       float* b = reinterpret_cast<float*>(image.data() + L.bias_off);
       for (int f = 0; f < L.nout; ++f) b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
     }
-    for (int n = 0; n < L.nout; ++n) {
-      const int nb = n / kTsBlockN, r = n % kTsBlockN;
-      const int rows = std::min(kTsBlockN, L.n_pad - nb * kTsBlockN);
+    for (int n = 0; n < L.nout; ++n)
       for (int k = 0; k < L.nin; ++k) {
-        const int kb = k / kTsBlockK;
-        const size_t chunk = L.w_off + ((size_t)nb * L.kblk + kb) * kTsChunkBytes;
-        put_kmajor(image, chunk, rows, r, k % kTsBlockK, 2, mv.params.data() + ((size_t)k * L.nout + n) * msz);
+        const size_t chunk = L.w_off + (size_t)(k / kTsBlockK) * kTsChunkBytes;
+        put_kmajor(image, chunk, L.n_pad, n, k % kTsBlockK, 2, mv.params.data() + ((size_t)k * L.nout + n) * msz);
       }
-    }
   }
-  p.a_bytes = a_blocks * (uint32_t)(kTcM * 128);
   p.stage_bytes = (uint32_t)(p.layers[0].k_pad / 8) * 2048;
-  const uint32_t fixed = 1024 + 2 * p.a_bytes + p.stage_bytes + 256 + (uint32_t)(kTsMaxLayers * sizeof(TsLayer));
+  p.a_bytes = std::max(a_blocks * (uint32_t)(kTcM * 128), (p.stage_bytes + 1023u) & ~1023u);
+  const uint32_t fixed = 1024 + kTsSlots * p.a_bytes + 256 + (uint32_t)(kTsMaxLayers * sizeof(TsLayer));
   const uint32_t budget = 227 * 1024;
   if (fixed + 2 * kTsChunkBytes > budget) {
     why = "operand tiles exceed shared memory";

@@ -8,20 +8,21 @@
 //     reads the same image) into a ring of shared-memory stages with 1-D bulk
 //     copies (cp.async.bulk, completion counted in bytes on the stage's
 //     "full" mbarrier; no multicast);
-//   MMA issuer (warp 17, one thread): per job (layer l, column block nb of
-//     128) issues D[128 x N] += A[128 x K] * B[N x K]^T chunk by chunk
-//     (tcgen05.mma kind::f16, fp32 accumulator in TMEM columns nb*128...),
-//     frees each ring stage with tcgen05.commit and signals the finished job
-//     on the block's "acc full" mbarrier;
+//   MMA issuer (warp 17, one thread): per job (one layer of one tile)
+//     issues D[128 x N<=256] += A[128 x K] * B[N x K]^T chunk by chunk
+//     (tcgen05.mma kind::f16, fp32 accumulator in the slot's 256 TMEM
+//     columns), frees each ring stage with tcgen05.commit and signals the
+//     finished job on the slot's "acc full" mbarrier;
 //   epilogue (warps 0-15: 4 TMEM lane quarters x 4 column quarters): per job,
 //     tcgen05.ld of the accumulator, bias, activation (reference fused
 //     epilogue, src/ponni_Inference.h:416-444), and the next layer's K-major
-//     operand (ping-pong buffers A0/A1) or the caller's output; then signals
-//     "epi done" for the block.  They also stage each tile's input (cp.async
-//     into the MN-major layer-0 operand) as soon as layer 0 has consumed the
-//     previous one.
-// A job's epilogue overlaps the MMAs of the next column block; a layer's
-// MMAs start when every block of the previous layer has been written.
+//     operand, written in place into the slot's operand buffer (the job's
+//     MMAs have completed), or the caller's output; each column quarter then
+//     signals its own mbarrier.  They also stage each tile's input (cp.async,
+//     the MN-major layer-0 operand, in the same buffer) once the slot's last
+//     layer has consumed the buffer.
+// Two tiles (slots) are in flight and their jobs alternate layer by layer,
+// so one slot's epilogue runs while the tensor core works on the other's.
 //
 // In this fp32-accumulation mode SiLU and sigmoid use the hardware base-2
 // exponential and reciprocal approximations (two full-rate MUFU operations
@@ -141,18 +142,14 @@ __device__ __forceinline__ void ts_act32(float (&v)[32], int fast, int flags, fl
   for (int j = 0; j < 32; ++j) v[j] = ts_act<ACT>(v[j], fast, flags, s0, s1);
 }
 
-struct TsShared {
-  uint32_t a[2], stage, ring, full, empty, accf, epi_done, stage_full, drain;
-};
-
-// Epilogue of the columns [c_begin, c_begin + kTsColsPerWarp) of job
-// (l, nb) for this thread's row m.
+// Epilogue of the columns [c_begin, c_begin + kTsColsPerWarp) of one job
+// for this thread's row m: accumulator -> bias -> activation -> the tile's
+// K-major operand (in place: the job's MMAs have completed) or the output.
 template <class T, int ACT>
 __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool last, uint32_t tmem_row, int c_begin,
                                             const float* __restrict__ bias, uint32_t a_out, T* __restrict__ out,
                                             int64_t out_ld, int64_t col, int64_t batch, int m, long long (&t_ph)[3]) {
   (void)t_ph;
-  using Op = typename OperandOf<T>::type;
   const int n_pad = L.n_pad, nout = L.nout, has_bias = L.has_bias, flags = L.act_flags;
   const float s0 = L.s0, s1 = L.s1;
 #pragma unroll 1
@@ -173,8 +170,9 @@ __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool las
         v[4 * q + 3] += b.w;
       }
     }
+    ts_act32<ACT>(v, fast, flags, s0, s1);
+    TS_ACC(t_ph[1], ta);
     if (last) {
-      ts_act32<ACT>(v, fast, flags, s0, s1);
       if (col < batch) {
         const int nv = min(32, nout - c0);
         T* o = out + (int64_t)c0 * out_ld + col;
@@ -185,23 +183,11 @@ __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool las
         }
       }
     } else {
-      ts_act32<ACT>(v, fast, flags, s0, s1);
-#ifdef PONNI_B200_TC_PROFILE
-      // make the timing see the activation results before the stores
-      float sink = 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) sink += v[j];
-      if (sink == 12345.678f) v[0] += 1e-30f;
-#endif
-      TS_ACC(t_ph[1], ta);
-      TS_T(ts);
       const uint32_t a[1] = {a_out};
 #pragma unroll
       for (int q = 0; q < 4; ++q) store_row8<T>(a, m, c0 + 8 * q, v + 8 * q);
-      TS_ACC(t_ph[2], ts);
     }
   }
-  (void)sizeof(Op);
 }
 
 template <class T>
@@ -223,6 +209,37 @@ __device__ __forceinline__ void ts_epilogue_dispatch(const TsLayer& L, int fast,
 #undef PONNI_TS_EPI
 }
 
+// Stage tile `t`'s input into a slot's operand buffer as the MN-major
+// layer-0 operand (cp.async), and zero its padding K rows nin..k_pad (the
+// buffer holds the previous tile's activations).  Epilogue threads only.
+template <class T>
+__device__ __forceinline__ void ts_load_tile(uint32_t buf, unsigned char* buf_ptr, const T* in, int64_t in_ld,
+                                             int nin, int k0, int64_t t, int64_t batch, bool vec, int tid) {
+  load_input<T, kTsEpiWarps * 32>(buf, in, in_ld, nin, t * kTcM, batch, vec, tid);
+  cp_async_commit();
+  for (int i = tid; i < (k0 - nin) * 16; i += kTsEpiWarps * 32) {
+    const int f = nin + i / 16, j = i % 16;
+    const uint32_t off = (uint32_t)(f >> 3) * 2048 + (uint32_t)(j >> 3) * 1024 + (uint32_t)(f & 7) * 128 +
+                         ((((uint32_t)j & 7) ^ ((uint32_t)f & 7)) << 4);
+    *reinterpret_cast<uint4*>(buf_ptr + off) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Job order shared by the three roles: rounds of two tiles (one per slot);
+// within a round, layer by layer, slot 0's job then slot 1's.  Slot s's
+// j-th tile is this CTA's tile 2j + s of the grid-strided sequence.
+struct TsJobs {
+  int64_t first, stride, ntiles;
+  int64_t count[kTsSlots];
+  __device__ TsJobs(int64_t ntiles_, int64_t first_, int64_t stride_) : first(first_), stride(stride_), ntiles(ntiles_) {
+    const int64_t mine = first_ < ntiles_ ? (ntiles_ - first_ + stride_ - 1) / stride_ : 0;
+    count[0] = (mine + 1) / 2;
+    count[1] = mine / 2;
+  }
+  __device__ int64_t rounds() const { return count[0]; }
+  __device__ int64_t tile(int s, int64_t r) const { return first + (2 * r + s) * stride; }
+};
+
 template <class T>
 __global__ void __launch_bounds__(kTsThreads, 1)
     ts_forward_kernel(const __grid_constant__ TsProgram p, const unsigned char* __restrict__ image,
@@ -235,88 +252,75 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int R = (int)p.ring_stages;
 
-  TsShared S;
-  S.a[0] = base;
-  S.a[1] = base + p.a_bytes;
-  S.stage = base + 2 * p.a_bytes;
-  S.ring = S.stage + p.stage_bytes;
-  const uint32_t s_bars = S.ring + (uint32_t)R * kTsChunkBytes;
-  S.full = s_bars;                 // [R]
-  S.empty = s_bars + 64;           // [R]
-  S.accf = s_bars + 128;           // [2]
-  S.epi_done = s_bars + 144;       // [2]
-  S.stage_full = s_bars + 160;
-  S.drain = s_bars + 168;
-  const uint32_t s_tmem = s_bars + 176;
+  const uint32_t s_a[kTsSlots] = {base, base + p.a_bytes};  // per-slot operand buffer (input stage inside)
+  const uint32_t s_ring = base + kTsSlots * p.a_bytes;
+  const uint32_t s_bars = s_ring + (uint32_t)R * kTsChunkBytes;
+  const uint32_t b_full = s_bars;          // [R]
+  const uint32_t b_empty = s_bars + 64;    // [R]
+  const uint32_t b_accf = s_bars + 128;    // [slot]
+  const uint32_t b_kbar = s_bars + 144;    // [slot][4 column quarters]
+  const uint32_t b_stage = s_bars + 208;   // [slot]
+  const uint32_t b_drain = s_bars + 224;
+  const uint32_t s_tmem = s_bars + 232;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(base_ptr + (s_tmem - base));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + (s_tmem + 4 - base));
   TsLayer* layers = reinterpret_cast<TsLayer*>(base_ptr + (s_bars + 256 - base));
 
   const int64_t ntiles = (batch + kTcM - 1) / kTcM;
   if ((int64_t)blockIdx.x >= ntiles) return;
+  const TsJobs jobs(ntiles, blockIdx.x, gridDim.x);
 
   // ---- set-up ----
-  if (warp == kTsMmaWarp) tmem_alloc(s_tmem, 256);
+  if (warp == kTsMmaWarp) tmem_alloc(s_tmem, 512);
   if (tid == 0) {
     for (int r = 0; r < R; ++r) {
-      mbar_init(S.full + 8u * r, 1);
-      mbar_init(S.empty + 8u * r, 1);
+      mbar_init(b_full + 8u * r, 1);
+      mbar_init(b_empty + 8u * r, 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(S.accf + 8u * b, 1);
-      mbar_init(S.epi_done + 8u * b, kTsEpiWarps);
+    for (int s = 0; s < kTsSlots; ++s) {
+      mbar_init(b_accf + 8u * s, 1);
+      for (int q = 0; q < 4; ++q) mbar_init(b_kbar + 8u * (4 * s + q), 4);
+      mbar_init(b_stage + 8u * s, kTsEpiWarps);
     }
-    mbar_init(S.stage_full, kTsEpiWarps);
-    mbar_init(S.drain, 1);
+    mbar_init(b_drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   for (int i = tid; i < p.n_layers; i += kTsThreads) layers[i] = p.layers[i];
-  {
-    uint4* z = reinterpret_cast<uint4*>(base_ptr + (S.stage - base));
-    for (int i = tid; i < (int)(p.stage_bytes / 16); i += kTsThreads) z[i] = make_uint4(0, 0, 0, 0);
-  }
-  fence_proxy_async();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nl = p.n_layers;
-  const int64_t stride = gridDim.x;
 
   if (warp == kTsProducerWarp) {
     // ------------------------------------------------ producer ----
     if (lane == 0) {
       uint32_t use = 0;
       bool ok = true;
-      long long w_empty = 0;
-      (void)w_empty;
-      for (int64_t t = blockIdx.x; t < ntiles && ok; t += stride) {
-        for (int l = 0; l < nl && ok; ++l) {
-          const TsLayer& L = layers[l];
-          for (int nb = 0; nb < L.nblk && ok; ++nb) {
-            const uint32_t bytes = (uint32_t)min(kTsBlockN, L.n_pad - nb * kTsBlockN) * 128u;
+      for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
+        for (int l = 0; l < nl && ok; ++l)
+          for (int s = 0; s < kTsSlots && ok; ++s) {
+            if (r >= jobs.count[s]) continue;
+            const TsLayer& L = layers[l];
+            const uint32_t bytes = (uint32_t)L.n_pad * 128u;
             for (int kb = 0; kb < L.kblk; ++kb) {
-              const uint32_t r = use % (uint32_t)R;
-              TS_T(t0);
-              if (use >= (uint32_t)R && !wait_phase(S.empty + 8u * r, ((use / R) - 1) & 1u, abort_flag)) {
+              const uint32_t st = use % (uint32_t)R;
+              if (use >= (uint32_t)R && !wait_phase(b_empty + 8u * st, ((use / R) - 1) & 1u, abort_flag)) {
                 ok = false;
                 break;
               }
-              TS_ACC(w_empty, t0);
-              mbar_expect_tx(S.full + 8u * r, bytes);
-              bulk_load(S.ring + r * kTsChunkBytes,
-                        image + L.w_off + ((uint64_t)nb * L.kblk + kb) * kTsChunkBytes, bytes, S.full + 8u * r);
+              mbar_expect_tx(b_full + 8u * st, bytes);
+              bulk_load(s_ring + st * kTsChunkBytes, image + L.w_off + (uint64_t)kb * kTsChunkBytes, bytes,
+                        b_full + 8u * st);
               ++use;
             }
           }
-        }
-      }
       // Drain: the last copies issued must have landed before the CTA exits.
       const uint32_t n = use < (uint32_t)R ? use : (uint32_t)R;
       for (uint32_t u = use - n; u < use; ++u) {
         const long long t0 = clock64();
-        while (!mbar_try_wait(S.full + 8u * (u % R), (u / R) & 1u))
+        while (!mbar_try_wait(b_full + 8u * (u % R), (u / R) & 1u))
           if (clock64() - t0 > kWaitCycles) break;
       }
       if (!ok) atomicExch(err, 2);
@@ -325,76 +329,57 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   } else if (warp == kTsMmaWarp) {
     // --------------------------------------------- MMA issuer ----
     if (lane == 0) {
-      uint32_t use = 0, st_ph = 0, epi_ph[2] = {0, 0};
-      int prev_nblk = 0;
+      uint32_t use = 0, st_ph[kTsSlots] = {0, 0}, k_ph[kTsSlots] = {0, 0};
+      bool has_prev[kTsSlots] = {false, false};
       bool ok = true;
-      long long w_stage = 0, w_epi = 0, w_full = 0;
-      (void)w_stage; (void)w_epi; (void)w_full;
+      long long w_epi = 0, w_full = 0;
+      (void)w_epi; (void)w_full;
       TS_T(t_all);
-      const uint64_t a_stage = smem_desc(S.stage, 1024, 2048);
-      for (int64_t t = blockIdx.x; t < ntiles && ok; t += stride) {
-        for (int l = 0; l < nl && ok; ++l) {
-          const TsLayer& L = layers[l];
-          if (l == 0) {
-            TS_T(t0);
-            if (!(ok = wait_phase(S.stage_full, st_ph, abort_flag))) break;
-            TS_ACC(w_stage, t0);
-            st_ph ^= 1u;
-          }
-          // Dependencies on the previous job layer (l - 1, or the last layer
-          // of the previous tile), per chunk: the accumulator block nb must
-          // have been read out, and for l >= 1 the operand K block kb must
-          // have been written (by the epilogue of block kb*64/128).  So a
-          // layer's first chunks start while the previous layer's last block
-          // is still in its epilogue.
-          bool waited[2] = {false, false};
-          auto need = [&](int b) {
-            if (ok && b < prev_nblk && !waited[b]) {
-              TS_T(tw);
-              ok = wait_phase(S.epi_done + 8u * b, epi_ph[b], abort_flag);
-              TS_ACC(w_epi, tw);
-              epi_ph[b] ^= 1u;
-              waited[b] = true;
-              tc_fence_after();
+      for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
+        for (int l = 0; l < nl && ok; ++l)
+          for (int s = 0; s < kTsSlots && ok; ++s) {
+            if (r >= jobs.count[s]) continue;
+            const TsLayer& L = layers[l];
+            TS_T(tw);
+            if (l == 0) {
+              if (!(ok = wait_phase(b_stage + 8u * s, st_ph[s], abort_flag))) break;
+              st_ph[s] ^= 1u;
             }
-          };
-          const int nsteps = L.k_pad / 16;
-          const uint64_t a_in = smem_desc(S.a[(l + 1) & 1], 16, 1024);  // written by the epilogue of layer l-1
-          for (int nb = 0; nb < L.nblk && ok; ++nb) {
-            const int rows = min(kTsBlockN, L.n_pad - nb * kTsBlockN);
-            const uint32_t idesc = idesc_of(p.dtype, rows, l == 0);
-            const uint32_t d = tmem_base + (uint32_t)(nb * kTsBlockN);
-            need(nb);
-            for (int kb = 0; kb < L.kblk && ok; ++kb) {
-              if (l > 0) need(kb * kTsBlockK / kTsBlockN);
-              if (!ok) break;
-              const uint32_t r = use % (uint32_t)R;
+            // The slot's previous epilogue has read its accumulator and
+            // written the operand (all four column quarters).
+            if (has_prev[s]) {
+              for (int q = 0; q < 4 && ok; ++q) ok = wait_phase(b_kbar + 8u * (4 * s + q), k_ph[s], abort_flag);
+              k_ph[s] ^= 1u;
+            }
+            if (!ok) break;
+            TS_ACC(w_epi, tw);
+            has_prev[s] = true;
+            tc_fence_after();
+            const int nsteps = L.k_pad / 16;
+            const uint32_t idesc = idesc_of(p.dtype, L.n_pad, l == 0);
+            const uint32_t d = tmem_base + (uint32_t)(s * kTsMaxN);
+            const uint64_t a0 = l == 0 ? smem_desc(s_a[s], 1024, 2048) : smem_desc(s_a[s], 16, 1024);
+            for (int kb = 0; kb < L.kblk; ++kb) {
+              const uint32_t st = use % (uint32_t)R;
               TS_T(t2);
-              if (!(ok = wait_phase(S.full + 8u * r, (use / R) & 1u, abort_flag))) break;
+              if (!(ok = wait_phase(b_full + 8u * st, (use / R) & 1u, abort_flag))) break;
               TS_ACC(w_full, t2);
               tc_fence_after();
-              const uint64_t b0 = smem_desc(S.ring + r * kTsChunkBytes, 16, 1024);
+              const uint64_t b0 = smem_desc(s_ring + st * kTsChunkBytes, 16, 1024);
               const int s_end = min(nsteps, kb * 4 + 4);
-              for (int s = kb * 4; s < s_end; ++s) {
-                const uint64_t a = l == 0 ? a_stage + (uint64_t)s * 256
-                                          : a_in + (uint64_t)(s >> 2) * 1024 + (uint64_t)(s & 3) * 2;
-                umma_f16(d, a, b0 + (uint64_t)(s & 3) * 2, idesc, s > 0 ? 1u : 0u);
+              for (int k = kb * 4; k < s_end; ++k) {
+                const uint64_t a = l == 0 ? a0 + (uint64_t)k * 256 : a0 + (uint64_t)(k >> 2) * 1024 + (uint64_t)(k & 3) * 2;
+                umma_f16(d, a, b0 + (uint64_t)(k & 3) * 2, idesc, k > 0 ? 1u : 0u);
               }
-              umma_commit(S.empty + 8u * r);
+              umma_commit(b_empty + 8u * st);
               ++use;
             }
-            if (ok) umma_commit(S.accf + 8u * nb);
+            if (ok) umma_commit(b_accf + 8u * s);
           }
-          // Consume the remaining completions of the previous layer's blocks
-          // (keeps every barrier's phase accounting one-to-one).
-          for (int b = 0; b < prev_nblk; ++b) need(b);
-          prev_nblk = L.nblk;
-        }
-      }
       // Drain: every MMA issued has completed before TMEM is freed.
-      umma_commit(S.drain);
+      umma_commit(b_drain);
       const long long t0 = clock64();
-      while (!mbar_try_wait(S.drain, 0))
+      while (!mbar_try_wait(b_drain, 0))
         if (clock64() - t0 > kWaitCycles) break;
       if (!ok) atomicExch(err, 3);
       TS_FLUSH(1, w_epi);
@@ -406,63 +391,59 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     __syncwarp();
   } else {
     // ----------------------------------------------- epilogue ----
-    const int q = warp & 3, ch = warp >> 2;
+    const int q = warp & 3, cq = warp >> 2;
     const int m = q * 32 + lane;
-    const uint32_t tmem_row = tmem_base + ((uint32_t)(q * 32) << 16);
     const bool vec = in_vec != 0;
-    uint32_t acc_ph[2] = {0, 0};
+    const int k0 = layers[0].k_pad;
+    uint32_t acc_ph[kTsSlots] = {0, 0};
     bool ok = true;
-    long long w_acc = 0, c_epi = 0, c_sig = 0, t_ph[3] = {0, 0, 0};
-    (void)w_acc; (void)c_epi; (void)c_sig;
-    int64_t t = blockIdx.x;
-    load_input<T, kTsEpiWarps * 32>(S.stage, in, in_ld, p.nin, t * kTcM, batch, vec, tid);
-    cp_async_commit();
-    cp_async_wait_0();
-    fence_proxy_async();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(S.stage_full);
-    for (; t < ntiles && ok; t += stride) {
-      const int64_t next = t + stride;
-      const int64_t col = t * kTcM + m;
-      for (int l = 0; l < nl && ok; ++l) {
-        const TsLayer& L = layers[l];
-        const bool last = l == nl - 1;
-        const float* bias = reinterpret_cast<const float*>(image + L.bias_off);
-        const uint32_t a_out = S.a[l & 1];
-        for (int nb = 0; nb < L.nblk; ++nb) {
+    long long w_acc = 0, c_epi = 0, t_ph[3] = {0, 0, 0};
+    (void)w_acc; (void)c_epi;
+    for (int s = 0; s < kTsSlots; ++s) {
+      if (jobs.count[s] == 0) continue;
+      ts_load_tile<T>(s_a[s], base_ptr + (s_a[s] - base), in, in_ld, p.nin, k0, jobs.tile(s, 0), batch, vec, tid);
+      cp_async_wait_0();
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_stage + 8u * s);
+    }
+    for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
+      for (int l = 0; l < nl && ok; ++l)
+        for (int s = 0; s < kTsSlots && ok; ++s) {
+          if (r >= jobs.count[s]) continue;
+          const TsLayer& L = layers[l];
+          const bool last = l == nl - 1;
+          const int64_t t = jobs.tile(s, r);
           // One lane waits, the warp follows (the TMEM loads are warp-collective).
-          int got = 0;
           TS_T(t0);
-          if (lane == 0) got = wait_phase(S.accf + 8u * nb, acc_ph[nb], abort_flag) ? 1 : 0;
+          int got = 0;
+          if (lane == 0) got = wait_phase(b_accf + 8u * s, acc_ph[s], abort_flag) ? 1 : 0;
           got = __shfl_sync(0xffffffffu, got, 0);
           if (!(ok = got != 0)) break;
+          acc_ph[s] ^= 1u;
           TS_ACC(w_acc, t0);
           TS_T(t1);
-          acc_ph[nb] ^= 1u;
           tc_fence_after();
-          if (l == 0 && nb == L.nblk - 1 && next < ntiles) {
-            // layer 0 has consumed the stage: fetch the next tile's input
-            load_input<T, kTsEpiWarps * 32>(S.stage, in, in_ld, p.nin, next * kTcM, batch, vec, tid);
-            cp_async_commit();
-          }
-          ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, nb * kTsBlockN + ch * kTsColsPerWarp, bias, a_out, out, out_ld,
-                                  col, batch, m, t_ph);
-          TS_T(t2);
+          const bool refill = last && r + 1 < jobs.count[s];
+          if (refill)  // the slot's MMAs are done with its operand buffer: stage the next tile
+            ts_load_tile<T>(s_a[s], base_ptr + (s_a[s] - base), in, in_ld, p.nin, k0, jobs.tile(s, r + 1), batch,
+                            vec, tid);
+          const uint32_t tmem_row = tmem_base + (uint32_t)(s * kTsMaxN) + ((uint32_t)(q * 32) << 16);
+          ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, cq * kTsColsPerWarp,
+                                  reinterpret_cast<const float*>(image + L.bias_off), s_a[s], out, out_ld,
+                                  t * kTcM + m, batch, m, t_ph);
           fence_proxy_async();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(S.epi_done + 8u * nb);
-          TS_ACC(c_sig, t2);
+          if (lane == 0) mbar_arrive(b_kbar + 8u * (4 * s + cq));
+          if (refill) {
+            cp_async_wait_0();
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_stage + 8u * s);
+          }
           TS_ACC(c_epi, t1);
         }
-      }
-      if (ok && next < ntiles) {
-        cp_async_wait_0();
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(S.stage_full);
-      }
-    }
     cp_async_wait_0();
     if (!ok && lane == 0) atomicExch(err, 4);
     if (tid == 0) {
@@ -477,7 +458,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   __syncthreads();
   if (warp == kTsMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 256);
+    tmem_dealloc(tmem_base, 512);
   }
 }
 

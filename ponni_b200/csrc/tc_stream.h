@@ -2,10 +2,11 @@
 // (tc_stream.cu), for 16-bit chains whose weights exceed shared memory
 // (the 64->256x5->32 bf16 network: 573 KB of weights).
 //
-// Work unit ("job"): one layer's 128-column block of the accumulator for one
-// tile of 128 batch columns, D[128 x N<=128] = A[128 x K] * B[N x K]^T, with
-// B streamed in chunks of K = 64 (one 128-byte swizzle block: N rows x
-// 128 B <= 16 KB) through a ring of shared-memory stages.
+// Work unit ("job"): one layer for one tile of 128 batch columns,
+// D[128 x N<=256] = A[128 x K] * B[N x K]^T, with B streamed in chunks of
+// K = 64 (one 128-byte swizzle block: N rows x 128 B <= 32 KB) through a
+// ring of shared-memory stages.  Two tiles are in flight per CTA and their
+// jobs alternate layer by layer.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -18,11 +19,12 @@ struct ponni_b200_model;
 namespace ponni_b200 {
 
 constexpr int kTsMaxLayers = 16;
-constexpr int kTsBlockN = 128;                  // accumulator columns of one job
+constexpr int kTsMaxN = 256;                    // layer width limit = accumulator columns of one job
 constexpr int kTsBlockK = 64;                   // K elements of one streamed chunk
-constexpr int kTsChunkBytes = kTsBlockN * 128;  // chunk stride (rows x 128 B)
+constexpr int kTsChunkBytes = kTsMaxN * 128;    // ring stage: up to 256 rows x 128 B
+constexpr int kTsSlots = 2;                     // tiles in flight per CTA
 constexpr int kTsEpiWarps = 16;                 // 4 TMEM lane quarters x 4 column quarters
-constexpr int kTsColsPerWarp = kTsBlockN / (kTsEpiWarps / 4);  // accumulator columns per warp and job
+constexpr int kTsColsPerWarp = kTsMaxN / 4;     // accumulator columns per warp and job
 constexpr int kTsProducerWarp = kTsEpiWarps;
 constexpr int kTsMmaWarp = kTsEpiWarps + 1;
 constexpr int kTsThreads = (kTsEpiWarps + 2) * 32;  // + producer warp + MMA warp
@@ -31,12 +33,12 @@ constexpr int kTsMaxStages = 8;
 struct TsLayer {
   int32_t nin, nout;
   int32_t k_pad, n_pad;  // K rounded to 16, N rounded to 16
-  int32_t nblk, kblk;    // column blocks of 128, K chunks of 64
+  int32_t kblk;          // K chunks of 64
   int32_t act, act_flags;
   float s0, s1;
   int32_t has_bias;
   uint32_t bias_off;     // byte offset of float bias[round_up(n_pad, 32)] in the image
-  uint64_t w_off;        // byte offset of chunk (nb = 0, kb = 0); chunk (nb, kb) at + (nb*kblk + kb) * 16 KB
+  uint64_t w_off;        // byte offset of chunk kb = 0; chunk kb at + kb * kTsChunkBytes (n_pad rows x 128 B)
 };
 
 struct TsProgram {
@@ -44,8 +46,8 @@ struct TsProgram {
   int32_t dtype;          // ponni_b200_dtype: 2 f16, 3 bf16
   int32_t nin, nout;
   int32_t fast_act;       // SiLU / sigmoid / tanh through the hardware approximations (fp32 accumulation mode)
-  uint32_t a_bytes;       // one K-major activation operand buffer (two, ping-pong)
-  uint32_t stage_bytes;   // MN-major layer-0 input stage
+  uint32_t a_bytes;       // one tile's activation operand buffer (also holds its MN-major input stage)
+  uint32_t stage_bytes;   // MN-major layer-0 input stage (inside the operand buffer)
   uint32_t ring_stages;   // weight ring stages of kTsChunkBytes
   uint32_t smem_bytes;    // dynamic shared memory requested
   uint64_t image_bytes;   // weight chunks + biases
