@@ -13,21 +13,23 @@
 //     (tcgen05.mma kind::f16, fp32 accumulator in the slot's 256 TMEM
 //     columns), frees each ring stage with tcgen05.commit and signals the
 //     finished job on the slot's "acc full" mbarrier;
-//   epilogue (warps 0-15: 4 TMEM lane quarters x 4 column quarters): per job,
+//   epilogue (warps 0-15: two groups of 8, one per tile slot, each 4 TMEM
+//     lane quarters x 2 column halves): per job of its slot,
 //     tcgen05.ld of the accumulator, bias, activation (reference fused
 //     epilogue, src/ponni_Inference.h:416-444), and the next layer's K-major
 //     operand, written in place into the slot's operand buffer (the job's
-//     MMAs have completed), or the caller's output; each column quarter then
+//     MMAs have completed), or the caller's output; each column half then
 //     signals its own mbarrier.  They also stage each tile's input (cp.async,
 //     the MN-major layer-0 operand, in the same buffer) once the slot's last
 //     layer has consumed the buffer.
 // Two tiles (slots) are in flight and their jobs alternate layer by layer,
-// so one slot's epilogue runs while the tensor core works on the other's.
+// so one slot's epilogue runs while the tensor core works on the other's;
+// the two epilogue groups run independently, which keeps the MUFU unit fed
+// while the other group loads accumulators or stores operands.
 //
-// In this fp32-accumulation mode SiLU and sigmoid use the hardware base-2
-// exponential and reciprocal approximations (two full-rate MUFU operations
-// per value) and tanh the hardware tanh approximation; their errors are far
-// below one unit of the 16-bit model type.
+// In this fp32-accumulation mode SiLU, sigmoid and tanh use the hardware
+// tanh approximation (sigmoid(x) = (1 + tanh(x/2)) / 2), one MUFU operation
+// per value, whose error is below one unit of the 16-bit model type.
 //
 // Every wait is bounded; a role that gives up raises a shared abort flag
 // (the others see it and leave), records an error code, and the CTA drains
@@ -114,15 +116,10 @@ __device__ __forceinline__ float ts_act(float x, int fast, int flags, float s0, 
   }
 }
 
-// sigmoid(x) = 1 / (1 + 2^(-x log2 e)) with the hardware base-2 exponential
-// and reciprocal approximations (relative error near 2^-22 each): two
-// full-rate MUFU operations per value.
-__device__ __forceinline__ float sigmoid_fast(float x) {
-  float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(e) : "f"(x * -1.4426950408889634f));
-  asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(r) : "f"(1.0f + e));
-  return r;
-}
+// sigmoid(x) = (1 + tanh(x / 2)) / 2 with the hardware tanh approximation:
+// one MUFU operation per value (absolute error near 2^-11, below one
+// fp16/bf16 unit of the activations the next layer consumes).
+__device__ __forceinline__ float sigmoid_fast(float x) { return fmaf(0.5f, tanh_fast(0.5f * x), 0.5f); }
 
 // Activation of 32 values; in the fast mode SiLU and sigmoid use
 // sigmoid_fast, tanh the fp32 tanh approximation.
@@ -215,9 +212,9 @@ __device__ __forceinline__ void ts_epilogue_dispatch(const TsLayer& L, int fast,
 template <class T>
 __device__ __forceinline__ void ts_load_tile(uint32_t buf, unsigned char* buf_ptr, const T* in, int64_t in_ld,
                                              int nin, int k0, int64_t t, int64_t batch, bool vec, int tid) {
-  load_input<T, kTsEpiWarps * 32>(buf, in, in_ld, nin, t * kTcM, batch, vec, tid);
+  load_input<T, kTsGroupThreads>(buf, in, in_ld, nin, t * kTcM, batch, vec, tid);
   cp_async_commit();
-  for (int i = tid; i < (k0 - nin) * 16; i += kTsEpiWarps * 32) {
+  for (int i = tid; i < (k0 - nin) * 16; i += kTsGroupThreads) {
     const int f = nin + i / 16, j = i % 16;
     const uint32_t off = (uint32_t)(f >> 3) * 2048 + (uint32_t)(j >> 3) * 1024 + (uint32_t)(f & 7) * 128 +
                          ((((uint32_t)j & 7) ^ ((uint32_t)f & 7)) << 4);
@@ -258,7 +255,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   const uint32_t b_full = s_bars;          // [R]
   const uint32_t b_empty = s_bars + 64;    // [R]
   const uint32_t b_accf = s_bars + 128;    // [slot]
-  const uint32_t b_kbar = s_bars + 144;    // [slot][4 column quarters]
+  const uint32_t b_kbar = s_bars + 144;    // [slot][2 column halves]
   const uint32_t b_stage = s_bars + 208;   // [slot]
   const uint32_t b_drain = s_bars + 224;
   const uint32_t s_tmem = s_bars + 232;
@@ -279,8 +276,8 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     }
     for (int s = 0; s < kTsSlots; ++s) {
       mbar_init(b_accf + 8u * s, 1);
-      for (int q = 0; q < 4; ++q) mbar_init(b_kbar + 8u * (4 * s + q), 4);
-      mbar_init(b_stage + 8u * s, kTsEpiWarps);
+      for (int h = 0; h < 2; ++h) mbar_init(b_kbar + 8u * (2 * s + h), 4);
+      mbar_init(b_stage + 8u * s, kTsGroupWarps);
     }
     mbar_init(b_drain, 1);
     *abort_flag = 0;
@@ -346,9 +343,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
               st_ph[s] ^= 1u;
             }
             // The slot's previous epilogue has read its accumulator and
-            // written the operand (all four column quarters).
+            // written the operand (both column halves).
             if (has_prev[s]) {
-              for (int q = 0; q < 4 && ok; ++q) ok = wait_phase(b_kbar + 8u * (4 * s + q), k_ph[s], abort_flag);
+              for (int h = 0; h < 2 && ok; ++h) ok = wait_phase(b_kbar + 8u * (2 * s + h), k_ph[s], abort_flag);
               k_ph[s] ^= 1u;
             }
             if (!ok) break;
@@ -391,59 +388,62 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     __syncwarp();
   } else {
     // ----------------------------------------------- epilogue ----
-    const int q = warp & 3, cq = warp >> 2;
+    const int s = warp / kTsGroupWarps;  // this group's slot
+    const int q = warp & 3, ch = (warp >> 2) & 1;
+    const int gtid = tid & (kTsGroupThreads - 1);
     const int m = q * 32 + lane;
     const bool vec = in_vec != 0;
     const int k0 = layers[0].k_pad;
-    uint32_t acc_ph[kTsSlots] = {0, 0};
+    uint32_t acc_ph = 0;
     bool ok = true;
     long long w_acc = 0, c_epi = 0, t_ph[3] = {0, 0, 0};
     (void)w_acc; (void)c_epi;
-    for (int s = 0; s < kTsSlots; ++s) {
-      if (jobs.count[s] == 0) continue;
-      ts_load_tile<T>(s_a[s], base_ptr + (s_a[s] - base), in, in_ld, p.nin, k0, jobs.tile(s, 0), batch, vec, tid);
+    unsigned char* a_ptr = base_ptr + (s_a[s] - base);
+    if (jobs.count[s] > 0) {
+      ts_load_tile<T>(s_a[s], a_ptr, in, in_ld, p.nin, k0, jobs.tile(s, 0), batch, vec, gtid);
       cp_async_wait_0();
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(b_stage + 8u * s);
     }
-    for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
-      for (int l = 0; l < nl && ok; ++l)
-        for (int s = 0; s < kTsSlots && ok; ++s) {
-          if (r >= jobs.count[s]) continue;
-          const TsLayer& L = layers[l];
-          const bool last = l == nl - 1;
-          const int64_t t = jobs.tile(s, r);
-          // One lane waits, the warp follows (the TMEM loads are warp-collective).
-          TS_T(t0);
-          int got = 0;
-          if (lane == 0) got = wait_phase(b_accf + 8u * s, acc_ph[s], abort_flag) ? 1 : 0;
-          got = __shfl_sync(0xffffffffu, got, 0);
-          if (!(ok = got != 0)) break;
-          acc_ph[s] ^= 1u;
-          TS_ACC(w_acc, t0);
-          TS_T(t1);
-          tc_fence_after();
-          const bool refill = last && r + 1 < jobs.count[s];
-          if (refill)  // the slot's MMAs are done with its operand buffer: stage the next tile
-            ts_load_tile<T>(s_a[s], base_ptr + (s_a[s] - base), in, in_ld, p.nin, k0, jobs.tile(s, r + 1), batch,
-                            vec, tid);
-          const uint32_t tmem_row = tmem_base + (uint32_t)(s * kTsMaxN) + ((uint32_t)(q * 32) << 16);
-          ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, cq * kTsColsPerWarp,
-                                  reinterpret_cast<const float*>(image + L.bias_off), s_a[s], out, out_ld,
-                                  t * kTcM + m, batch, m, t_ph);
+    for (int64_t r = 0; r < jobs.count[s] && ok; ++r)
+      for (int l = 0; l < nl && ok; ++l) {
+        const TsLayer& L = layers[l];
+        const bool last = l == nl - 1;
+        const int64_t t = jobs.tile(s, r);
+        // One lane waits, the warp follows (the TMEM loads are warp-collective).
+        TS_T(t0);
+        int got = 0;
+        if (lane == 0) got = wait_phase(b_accf + 8u * s, acc_ph, abort_flag) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!(ok = got != 0)) break;
+        acc_ph ^= 1u;
+        TS_ACC(w_acc, t0);
+        TS_T(t1);
+        tc_fence_after();
+        const bool refill = last && r + 1 < jobs.count[s];
+        if (refill)  // the slot's MMAs are done with its operand buffer: stage the next tile
+          ts_load_tile<T>(s_a[s], a_ptr, in, in_ld, p.nin, k0, jobs.tile(s, r + 1), batch, vec, gtid);
+        const uint32_t tmem_row = tmem_base + (uint32_t)(s * kTsMaxN) + ((uint32_t)(q * 32) << 16);
+#ifndef PONNI_B200_TS_NO_EPI  // diagnostic build: handoffs only, no epilogue work
+        ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, ch * kTsColsPerWarp,
+                                reinterpret_cast<const float*>(image + L.bias_off), s_a[s], out, out_ld,
+                                t * kTcM + m, batch, m, t_ph);
+#else
+        (void)tmem_row;
+#endif
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b_kbar + 8u * (2 * s + ch));
+        if (refill) {
+          cp_async_wait_0();
           fence_proxy_async();
-          tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(b_kbar + 8u * (4 * s + cq));
-          if (refill) {
-            cp_async_wait_0();
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(b_stage + 8u * s);
-          }
-          TS_ACC(c_epi, t1);
+          if (lane == 0) mbar_arrive(b_stage + 8u * s);
         }
+        TS_ACC(c_epi, t1);
+      }
     cp_async_wait_0();
     if (!ok && lane == 0) atomicExch(err, 4);
     if (tid == 0) {

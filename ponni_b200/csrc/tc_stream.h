@@ -23,8 +23,10 @@ constexpr int kTsMaxN = 256;                    // layer width limit = accumulat
 constexpr int kTsBlockK = 64;                   // K elements of one streamed chunk
 constexpr int kTsChunkBytes = kTsMaxN * 128;    // ring stage: up to 256 rows x 128 B
 constexpr int kTsSlots = 2;                     // tiles in flight per CTA
-constexpr int kTsEpiWarps = 16;                 // 4 TMEM lane quarters x 4 column quarters
-constexpr int kTsColsPerWarp = kTsMaxN / 4;     // accumulator columns per warp and job
+constexpr int kTsEpiWarps = 16;                 // two groups (one per slot) of 8 warps
+constexpr int kTsGroupWarps = kTsEpiWarps / kTsSlots;  // 4 TMEM lane quarters x 2 column halves
+constexpr int kTsGroupThreads = kTsGroupWarps * 32;
+constexpr int kTsColsPerWarp = kTsMaxN / 2;     // accumulator columns per warp and job
 constexpr int kTsProducerWarp = kTsEpiWarps;
 constexpr int kTsMmaWarp = kTsEpiWarps + 1;
 constexpr int kTsThreads = (kTsEpiWarps + 2) * 32;  // + producer warp + MMA warp
