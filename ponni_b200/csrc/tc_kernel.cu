@@ -195,7 +195,7 @@ __device__ __forceinline__ int wg_sync_or(int wg, int pred) {
   return r;
 }
 
-// Issue the UMMA chain of layer L for one slot (one elected thread).  The
+// Issue the UMMA chain of layer L for one slot (one warp, elected lane).  The
 // descriptors of each operand are built once per layer; the K steps then only
 // add the step offset to the 14-bit start-address field (>> 4), which never
 // carries out of the field for shared-memory addresses.
@@ -219,12 +219,12 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
       const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
       const uint32_t acc = in_group ? 1u : 0u;
       // smallest products first
-      umma_f16(d, a0[1] + ao, b0[1] + bo, idesc, acc);
-      umma_f16(d, a0[0] + ao, b0[2] + bo, idesc, 1u);
-      umma_f16(d, a0[2] + ao, b0[0] + bo, idesc, 1u);
-      umma_f16(d, a0[0] + ao, b0[1] + bo, idesc, 1u);
-      umma_f16(d, a0[1] + ao, b0[0] + bo, idesc, 1u);
-      umma_f16(d, a0[0] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16_warp(d, a0[1] + ao, b0[1] + bo, idesc, acc);
+      umma_f16_warp(d, a0[0] + ao, b0[2] + bo, idesc, 1u);
+      umma_f16_warp(d, a0[2] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16_warp(d, a0[0] + ao, b0[1] + bo, idesc, 1u);
+      umma_f16_warp(d, a0[1] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16_warp(d, a0[0] + ao, b0[0] + bo, idesc, 1u);
       if (++in_group == gstep) {
         in_group = 0;
         d += n_pad;
@@ -238,14 +238,14 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
       const uint64_t a0 = smem_desc(stage, 1024, 2048);
       for (int s = 0; s < nsteps; ++s) {
         const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
-        umma_f16(d, a0 + (uint64_t)s * 256, b0 + bo, L.idesc_mn, s > 0 ? 1u : 0u);
+        umma_f16_warp(d, a0 + (uint64_t)s * 256, b0 + bo, L.idesc_mn, s > 0 ? 1u : 0u);
       }
     } else {
       const uint64_t a0 = smem_desc(s_a[0], 16, 1024);
       for (int s = 0; s < nsteps; ++s) {
         const uint64_t ao = (uint64_t)(s >> 2) * 1024 + (uint64_t)(s & 3) * 2;
         const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
-        umma_f16(d, a0 + ao, b0 + bo, idesc, s > 0 ? 1u : 0u);
+        umma_f16_warp(d, a0 + ao, b0 + bo, idesc, s > 0 ? 1u : 0u);
       }
     }
   }
@@ -367,19 +367,22 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
       fence_proxy_async();
       tc_fence_before();
       wg_sync<TPS>(wg);
-      // One elected thread issues the chain and waits for its completion;
-      // the rest of the warpgroup parks on the named barrier (no issue slots
-      // spent spinning while the other slot's epilogue runs).
+      // The slot's first warp issues the chain (one elected lane per MMA,
+      // descriptors in uniform registers) and waits for its completion; the
+      // rest of the slot parks on the named barrier (no issue slots spent
+      // spinning while the other slots' epilogues run).
       TC_PROF_ADD(2, t_bar);
       bool ok = true;
-      if (lt == 0) {
+      if (lt < 32) {  // the slot's first warp issues (one elected lane per MMA) and waits
         TC_PROF_T(t_issue);
         tc_fence_after();
         issue_layer<SPLIT>(L, l == 0, tmem_base, s_a, s_image, stage);
-        umma_commit(s_bar);
+        umma_commit_warp(s_bar);
         TC_PROF_ADD(3, t_issue);
         TC_PROF_T(t_mma);
-        ok = mbar_wait_bounded(s_bar, phase);
+        int w = 0;
+        if (lane == 0) w = mbar_wait_bounded(s_bar, phase) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, w, 0) != 0;
         TC_PROF_ADD(4, t_mma);
       }
       phase ^= 1u;
