@@ -175,6 +175,15 @@ int ponni_b200_model_kernel(ponni_b200_model* model);
  * cycle sums in a build with -DPONNI_B200_TC_PROFILE, zeros otherwise). */
 ponni_b200_status ponni_b200_model_diagnostics(ponni_b200_model* model, uint64_t* out, int n);
 
+/* In-kernel device API (include/ponni_b200_device.cuh): plans the model and
+ * returns device pointers to its lowered program and packed parameters (valid
+ * until the parameters change or the model is destroyed), the widest state
+ * width and the number of state buffers, for evaluating samples inside an
+ * application's own kernel.  Replaces Inference::forward_batch_parallel_in_kernel
+ * (src/ponni_Inference.h:392-408, :592-604) and the generated model's infer_one. */
+ponni_b200_status ponni_b200_model_device_program(ponni_b200_model* model, const void** program, const void** params,
+                                                  int* max_width, int* num_buffers);
+
 /* Device-resident forward: input [num_inputs, batch] with row stride in_ld
  * elements, output [num_outputs, batch] with row stride out_ld, both device
  * pointers in the model dtype.  Enqueued on `stream`; returns without a fence

@@ -843,6 +843,29 @@ ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* m, int arith
   return PONNI_B200_OK;
 }
 
+ponni_b200_status ponni_b200_model_device_program(ponni_b200_model* m, const void** program, const void** params,
+                                                  int* max_width, int* num_buffers) {
+  if (!m || !program || !params) return PONNI_B200_ERR_INVALID_ARGUMENT;
+  ponni_b200_status st = pb_plan(m);
+  if (st) return st;
+  cudaSetDevice(m->device);
+  cudaError_t e = cudaSuccess;
+  if (!m->prog_dev) {
+    e = cudaMalloc(&m->prog_dev, sizeof(Program));
+    if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(program)");
+  }
+  e = cudaMemcpyAsync(m->prog_dev, &m->prog, sizeof(Program), cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  if (e != cudaSuccess) return cuda_fail(m, e, "program upload");
+  int w = std::max(m->prog.nin, m->prog.nout);
+  for (int b = 0; b < m->prog.n_buffers; ++b) w = std::max(w, m->prog.buf_width[b]);
+  *program = m->prog_dev;
+  *params = m->packed_dev;
+  if (max_width) *max_width = w;
+  if (num_buffers) *num_buffers = m->prog.n_buffers;
+  return PONNI_B200_OK;
+}
+
 int ponni_b200_model_kernel(ponni_b200_model* m) {
   if (!m) return 0;
   return pb_plan(m) == PONNI_B200_OK ? m->kernel : 0;

@@ -1,0 +1,81 @@
+"""In-kernel device API (include/ponni_b200_device.cuh): an application
+kernel evaluates the model one sample per thread through
+forward_batch_parallel_in_kernel (tests/cuda/device_api_kernel.cu).  Results
+are checked against the CPU oracle with the parity gates of the fused
+kernels, and for fp32 / fp64 against the tile kernel, which runs the same
+operations in the same order."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import ponni_b200 as pb
+from ponni_b200 import configs
+from tests import kat_models as K
+from tests.test_gpu_parity import check, from_torch, to_torch
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+LIB = os.path.join(os.path.dirname(os.path.abspath(__file__)), "cuda", "libpb_device_api_test.so")
+
+
+@pytest.fixture(scope="module")
+def embedded():
+    pb._abi.lib()  # the library the test kernel links against
+    lib = ctypes.CDLL(LIB)
+    f = lib.pb_test_embedded_forward
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64]
+    return f
+
+
+def run_embedded(fn, layers, dtype, x_raw):
+    m = pb.Inference(layers, dtype=dtype)
+    x = to_torch(x_raw, dtype).cuda()
+    y = torch.empty((m.get_num_outputs(), x.shape[1]), dtype=x.dtype, device="cuda")
+    rc = fn(m._m, x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), x.shape[1])
+    assert rc == 0, rc
+    return from_torch(y, dtype)
+
+
+def tile_forward(layers, dtype, x_raw, monkeypatch):
+    monkeypatch.setenv("PONNI_B200_FORCE_TILE", "1")
+    m = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_REFERENCE)
+    assert m.kernel() == pb._abi.KERNEL_TILE
+    y = m.forward_batch_parallel(to_torch(x_raw, dtype).cuda())
+    torch.cuda.synchronize()
+    return from_torch(y, dtype)
+
+
+NETS = {
+    "readme": K.readme_mlp,
+    "four_block": K.four_block,
+    "softmax_mixed": K.softmax_mixed,
+    "projection_add": K.projection_add_model,
+    "pytorch_resnet": lambda: K.pytorch_resnet()[0],
+    "cfg2": lambda: configs.cfg2(batch=1).layers,
+    "cfg4": lambda: configs.cfg4(batch=1).layers,
+}
+
+
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F64, pb.F16, pb.BF16])
+@pytest.mark.parametrize("net", list(NETS))
+def test_embedded_matches_oracle(net, dtype, embedded, oracle_lib, monkeypatch):
+    layers = NETS[net]()
+    rng = np.random.default_rng(17)
+    nin = pb.Inference(layers, dtype=dtype).get_num_inputs()
+    x = pb.to_dtype_bytes(rng.normal(0, 1, (nin, 1537)), dtype)
+    y = run_embedded(embedded, layers, dtype, x)
+    check(y, oracle_lib.forward(layers, dtype, x), dtype, layers, x)
+    if dtype in (pb.F32, pb.F64):
+        t = tile_forward(layers, dtype, x, monkeypatch)
+        assert K.normwise_err(y, t) <= (1e-6 if dtype == pb.F32 else 1e-14)
+
+
+def test_embedded_golden_fixture(embedded):
+    """The reference's pytorch_resnet fixture through the device API (abs 1e-5)."""
+    layers, x, expected = K.pytorch_resnet()
+    y = run_embedded(embedded, layers, pb.F32, np.ascontiguousarray(x.astype(np.float32)))
+    assert np.max(np.abs(y - expected)) <= 1e-5
