@@ -154,11 +154,18 @@ ponni_b200_status ponni_b200_model_synchronize(ponni_b200_model* model);
  *   REFERENCE -- always the tile kernel: the reference's arithmetic order
  *                (fp16/bf16 accumulate in the model type, per operation);
  *   TENSOR    -- require the tensor-core kernel (forward fails otherwise);
- *                fp16/bf16 models then accumulate in fp32. */
+ *                fp16/bf16 models then accumulate in fp32;
+ *   GENERATED -- the arithmetic of the reference's generated (AOT) model
+ *                struct (src/generator/kokkos_nn/emitter.py:693-735,
+ *                :967-1010): a Matvec followed by a Bias starts its sum at
+ *                the bias, and fp16/bf16 models accumulate with one fused
+ *                multiply-add per product in the model type (TwoHalf::fma);
+ *                the tile kernel. */
 typedef enum {
   PONNI_B200_ARITH_AUTO = 0,
   PONNI_B200_ARITH_REFERENCE = 1,
-  PONNI_B200_ARITH_TENSOR = 2
+  PONNI_B200_ARITH_TENSOR = 2,
+  PONNI_B200_ARITH_GENERATED = 3
 } ponni_b200_arithmetic;
 ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* model, int arithmetic);
 /* Kernel the next forward uses (plans the model): 1 = tile kernel (SIMT),

@@ -119,6 +119,7 @@ __device__ void infer_one(const Model& m, const T* x, int64_t x_stride, T* y, in
           for (int k = 0; k < s.nin; ++k) {
             const C<T> w = Num<T>::to_c(W[k * s.nout_pad + o]);
             if constexpr (sizeof(T) >= 4) acc = fma(w, buf[src][k], acc);
+            else if (s.flags & DENSE_HALF_FMA) acc = rnd<T>(fmaf(w, buf[src][k], acc));
             else acc = rnd<T>(acc + rnd<T>(w * buf[src][k]));
           }
           if (s.flags & DENSE_ADD_RESIDUAL) acc = rnd<T>(buf[aux][o] + acc);

@@ -40,16 +40,20 @@ def lib():
     return _lib
 
 
-def forward(layers, dtype: int, x: np.ndarray, nthreads: int = 0, acc32: bool = False) -> np.ndarray:
+def forward(layers, dtype: int, x: np.ndarray, nthreads: int = 0, acc32: bool = False,
+            generated: bool = False) -> np.ndarray:
     """x: host array in the model dtype's storage ([nin, batch]; bf16 as uint16 bits).
-    acc32: fp32-accumulation semantics (tensor-core path of 16-bit models)."""
+    acc32: fp32-accumulation semantics (tensor-core path of 16-bit models).
+    generated: the generated-model arithmetic (bias-first sums, fused 16-bit
+    multiply-adds; src/generator/kokkos_nn/emitter.py:704-708, :975-983)."""
     from ponni_b200.inference import build_descriptors
 
     descs, keep = build_descriptors(layers, dtype)
     x = np.ascontiguousarray(x)
     out = np.empty((layers[-1].num_outputs, x.shape[1]), dtype=x.dtype)
     rc = lib().ponni_oracle_forward_ex(ctypes.cast(descs, ctypes.c_void_p), len(layers), dtype, x.ctypes.data,
-                                       x.shape[1], out.ctypes.data, x.shape[1], x.shape[1], nthreads, int(acc32))
+                                       x.shape[1], out.ctypes.data, x.shape[1], x.shape[1], nthreads,
+                                       int(acc32) | (int(generated) << 1))
     if rc != 0:
         raise RuntimeError(f"oracle failed ({rc})")
     del keep

@@ -182,24 +182,36 @@ typedef struct {
     return x;                                                                                              \
   }                                                                                                        \
   /* Run one sample: bufa holds the input; *res points at the result. */                                   \
-  static void sample_##SUF(const OLayer* L, int nl, int smode, int acc32, T* bufa, T* bufb, T** saved,      \
+  static void sample_##SUF(const OLayer* L, int nl, int smode, int mflags, T* bufa, T* bufb, T** saved,     \
                             T** res) {                                                                     \
     T* cur = bufa;                                                                                         \
     T* nxt = bufb;                                                                                         \
+    const int acc32 = mflags & 1, gen = (mflags >> 1) & 1;                                                 \
     const int mode = acc32 ? -1 : smode; /* acc32: no per-operation rounding */                            \
     for (int li = 0; li < nl; ++li) {                                                                      \
       const OLayer* y = &L[li];                                                                            \
       const int n = y->nin;                                                                                \
       switch (y->kind) {                                                                                   \
         case PONNI_B200_MATVEC:                                                                            \
+        {                                                                                                  \
+          /* generated arithmetic: the sum starts at a following Bias, and    */                          \
+          /* 16-bit products are fused multiply-adds (emitter.py:704-708,     */                          \
+          /* :975-983)                                                        */                          \
+          const OLayer* bl = (gen && li + 1 < nl && L[li + 1].kind == PONNI_B200_BIAS) ? &L[li + 1] : 0;   \
+          const int fused = gen && (smode == PONNI_B200_F16 || smode == PONNI_B200_BF16);                 \
           for (int o = 0; o < y->nout; ++o) {                                                              \
-            T v = 0;                                                                                       \
-            for (int k = 0; k < n; ++k)                                                                    \
-              v = rnd_##SUF(mode, v + rnd_##SUF(mode, (T)y->pd[(size_t)k * y->nout + o] * cur[k]));        \
+            T v = bl ? (T)bl->pd[o] : 0;                                                                   \
+            for (int k = 0; k < n; ++k) {                                                                  \
+              const T w = (T)y->pd[(size_t)k * y->nout + o];                                               \
+              if (fused) v = rnd_##SUF(mode, (T)((double)w * (double)cur[k] + (double)v));                 \
+              else v = rnd_##SUF(mode, v + rnd_##SUF(mode, w * cur[k]));                                   \
+            }                                                                                              \
             nxt[o] = v;                                                                                    \
           }                                                                                                \
           { T* t = cur; cur = nxt; nxt = t; }                                                              \
+          if (bl) ++li; /* the Bias is consumed */                                                         \
           break;                                                                                           \
+        }                                                                                                  \
         case PONNI_B200_BIAS:                                                                              \
           for (int f = 0; f < n; ++f) cur[f] = rnd_##SUF(mode, cur[f] + (T)y->pd[f]);                      \
           break;                                                                                           \
@@ -325,7 +337,10 @@ static double round_scalar(int dtype, double v) {
 }
 
 /*
- * out[f][c] = model(in[:, c]) for c in [0, batch).  acc32 != 0 selects the
+ * out[f][c] = model(in[:, c]) for c in [0, batch).  Bit 1 of acc32 selects
+ * the arithmetic of the reference's generated model (a Matvec followed by a
+ * Bias starts its sum at the bias; 16-bit products are fused multiply-adds,
+ * emitter.py:704-708, :975-983).  Bit 0 of acc32 selects the
  * fp32-accumulation semantics of the tensor-core path for 16-bit models:
  * every operation in float, the state rounded to the model type where each
  * fused block (dense layer + following pointwise layers, or a barrier) ends.  Same descriptor list and
@@ -335,6 +350,7 @@ static double round_scalar(int dtype, double v) {
  */
 int ponni_oracle_forward_ex(const ponni_b200_layer_desc* layers, int n_layers, int dtype, const void* in,
                             int64_t in_ld, void* out, int64_t out_ld, int64_t batch, int nthreads, int acc32) {
+  /* acc32: bit 0 fp32-accumulation semantics; bit 1 generated-model arithmetic */
   if (!layers || n_layers <= 0 || batch < 0) return 1;
   for (int i = 0; i < n_layers; ++i)
     if (layers[i].save_index >= MAXSAVE) return 2;

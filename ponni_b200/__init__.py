@@ -10,6 +10,7 @@ from .layers import (Layer, Matvec, Bias, Relu, ReLU, LeakyRelu, LeakyReLU, Elu,
                      GELU, Silu, SiLU, Sigmoid, Tanh, Softplus, HardSigmoid, HardSwish, Mish, LayerNorm,
                      MinMaxNorm, Softmax, LogSoftmax, Save_State, Binop_Add, Binop_Concatenate,
                      Binop_Projection_Add)
+from .generated import Dense, GeneratedModel
 from .inference import (Inference, create_inference_model, create_inference_model_single_precision,
                         create_inference_model_double_precision, create_inference_model_half_precision,
                         create_inference_model_bhalf_precision, build_descriptors, to_dtype_bytes,

@@ -28,7 +28,7 @@ F32, F64, F16, BF16 = 0, 1, 2, 3
  HARD_SWISH, MISH, LAYER_NORM, MIN_MAX_NORM, SOFTMAX, LOG_SOFTMAX, SAVE_STATE, BINOP_ADD,
  BINOP_CONCATENATE, BINOP_PROJECTION_ADD) = range(22)
 
-ARITH_AUTO, ARITH_REFERENCE, ARITH_TENSOR = 0, 1, 2
+ARITH_AUTO, ARITH_REFERENCE, ARITH_TENSOR, ARITH_GENERATED = 0, 1, 2, 3
 KERNEL_TILE, KERNEL_TENSOR, KERNEL_NARROW, KERNEL_NARROW_JIT, KERNEL_TENSOR_STREAM = 1, 2, 3, 4, 5
 
 FLAG_TRAINABLE = 0x1

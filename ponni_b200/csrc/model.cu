@@ -287,7 +287,19 @@ struct Planner {
         s.nout_pad = (int)align_up(d.num_outputs, kTO);
         s.src = cur;
         s.w_off = append_matrix(Ly.params.data(), d.num_inputs, d.num_outputs, s.nout_pad);
-        ponni_b200_status st = add_epilogue(s, i + 1, end);
+        int epi_begin = i + 1;
+        if (m->arithmetic == PONNI_B200_ARITH_GENERATED) {
+          // Generated-model arithmetic (emitter.py:704-708, :975-983): the sum
+          // starts at the bias that follows the Matvec; 16-bit products are
+          // accumulated with one fused multiply-add each.
+          if (epi_begin < end && m->layers[epi_begin].d.kind == PONNI_B200_BIAS) {
+            s.flags |= DENSE_INIT_BIAS;
+            s.b_off = append(m->layers[epi_begin].params.data(), d.num_outputs);
+            ++epi_begin;
+          }
+          if (m->dtype == PONNI_B200_F16 || m->dtype == PONNI_B200_BF16) s.flags |= DENSE_HALF_FMA;
+        }
+        ponni_b200_status st = add_epilogue(s, epi_begin, end);
         if (st) return st;
         if (end == L) {
           s.flags |= DENSE_TO_GLOBAL;
@@ -834,7 +846,7 @@ int ponni_b200_saved_state_size(const ponni_b200_model* m, int index) {
 }
 
 ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* m, int arithmetic) {
-  if (!m || arithmetic < PONNI_B200_ARITH_AUTO || arithmetic > PONNI_B200_ARITH_TENSOR)
+  if (!m || arithmetic < PONNI_B200_ARITH_AUTO || arithmetic > PONNI_B200_ARITH_GENERATED)
     return PONNI_B200_ERR_INVALID_ARGUMENT;
   if (m->arithmetic != arithmetic) {
     m->arithmetic = arithmetic;

@@ -40,6 +40,7 @@ constexpr int32_t DENSE_INIT_BIAS = 0x1;    // accumulator starts at bias (Proje
 constexpr int32_t DENSE_ADD_RESIDUAL = 0x2; // out = res[o][c] + acc (Projection_Add)
 constexpr int32_t DENSE_TO_GLOBAL = 0x4;    // final block: write the caller's output
 constexpr int32_t DENSE_FAST_EPI = 0x8;     // epilogue is [Bias?][activation?]: fast path
+constexpr int32_t DENSE_HALF_FMA = 0x10;    // 16-bit: one fused multiply-add per product (generated arithmetic)
 constexpr int32_t CONCAT_AFTER = 0x4;
 
 struct EpiDesc {

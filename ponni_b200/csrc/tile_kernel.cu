@@ -288,6 +288,7 @@ __device__ __forceinline__ void dense_step_pair(const Program& p, const StepDesc
     const T* wp = W + o0;
     const T* xp = src + c0;
     const int nout_pad = s.nout_pad;
+    const bool half_fma = (s.flags & DENSE_HALF_FMA) != 0;  // generated arithmetic: fused per product
 #pragma unroll 4
     for (int k = 0; k < s.nin; ++k) {
       uint4 wr = *reinterpret_cast<const uint4*>(wp + k * nout_pad);
@@ -299,7 +300,8 @@ __device__ __forceinline__ void dense_step_pair(const Program& p, const StepDesc
       for (int i = 0; i < kTO; ++i) {
         const T2 wb = (i & 1) ? P::hi(w2[i >> 1]) : P::lo(w2[i >> 1]);
 #pragma unroll
-        for (int j = 0; j < kTB / 2; ++j) acc[i][j] = __hadd2_rn(acc[i][j], __hmul2_rn(wb, x2[j]));
+        for (int j = 0; j < kTB / 2; ++j)
+          acc[i][j] = half_fma ? __hfma2(wb, x2[j], acc[i][j]) : __hadd2_rn(acc[i][j], __hmul2_rn(wb, x2[j]));
       }
     }
     float accf[kTO][kTB];

@@ -1,0 +1,185 @@
+"""The reference's generated (AOT) model struct on libponni_b200.
+
+PONNI's generator (src/generator/kokkos_nn/emitter.py) emits a C++ struct per
+model with load_weights / infer_batch / infer_batch_half2 / infer_one /
+get_parameters / set_parameters (emitter.py:1724-1955).  Its arithmetic
+differs from the template path in two ways, both reproduced here through
+ARITH_GENERATED:
+
+* dense layers store W as [out, in] (the PyTorch / ONNX convention) and start
+  each sum at the bias (emitter.py:704-708: ``Scalar sum = bias(i); sum +=
+  W(i, j) * x(j)``);
+* infer_batch_half2 takes and returns fp32 values but keeps fp16 parameters
+  and accumulates with one fused multiply-add per product
+  (TwoHalf::fma, emitter.py:975-983).
+
+The ONNX import and graph compiler of the generator are not rebuilt: a model
+is given as a list of ``Dense`` layers (the fused DenseBiasActivation nodes
+the generator produces for MLPs).  Named weights load from a .ponni file as
+``<name>.weight`` [out, in] and ``<name>.bias`` [out].
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _abi
+from . import layers as L
+from .inference import Inference, from_dtype_bytes, to_dtype_bytes
+
+_ACT = {
+    None: None,
+    "relu": lambda n, a: L.Relu(n),
+    "leaky_relu": lambda n, a: L.LeakyRelu(n, a),
+    "elu": lambda n, a: L.Elu(n, a),
+    "selu": lambda n, a: L.Selu(n),
+    "gelu": lambda n, a: L.Gelu(n),
+    "gelu_tanh": lambda n, a: L.Gelu(n, True),
+    "silu": lambda n, a: L.Silu(n),
+    "sigmoid": lambda n, a: L.Sigmoid(n),
+    "tanh": lambda n, a: L.Tanh(n),
+    "softplus": lambda n, a: L.Softplus(n, 1.0),
+    "hard_swish": lambda n, a: L.HardSwish(n),
+    "mish": lambda n, a: L.Mish(n),
+}
+
+
+@dataclass
+class Dense:
+    """One fused dense node: y = activation(bias + W x), W[out, in]."""
+    name: str
+    weight: np.ndarray
+    bias: np.ndarray | None = None
+    activation: str | None = None
+    alpha: float = 0.01  # LeakyReLU slope / ELU alpha
+
+    def __post_init__(self):
+        self.weight = np.asarray(self.weight, dtype=np.float64)
+        if self.weight.ndim != 2:
+            raise ValueError(f"{self.name}: weight must be [out, in]")
+        if self.bias is not None:
+            self.bias = np.asarray(self.bias, dtype=np.float64).reshape(-1)
+            if self.bias.size != self.weight.shape[0]:
+                raise ValueError(f"{self.name}: bias size differs from the output width")
+        if self.activation not in _ACT:
+            raise ValueError(f"{self.name}: unsupported activation {self.activation!r}")
+
+
+def _read_tensor(path: str, name: str) -> np.ndarray:
+    lib = _abi.lib()
+    shape = (ctypes.c_int64 * 4)()
+    rank = ctypes.c_int()
+    err = ctypes.create_string_buffer(512)
+    st = lib.ponni_b200_read_ponni_tensor(path.encode(), name.encode(), None, 0, shape, ctypes.byref(rank), err, 512)
+    if st != 0:
+        raise _abi.PonniError(st, err.value.decode())
+    dims = [shape[i] for i in range(rank.value)]
+    out = np.empty(int(np.prod(dims)) if dims else 1, dtype=np.float32)
+    st = lib.ponni_b200_read_ponni_tensor(path.encode(), name.encode(), out.ctypes.data, out.size, shape,
+                                          ctypes.byref(rank), err, 512)
+    if st != 0:
+        raise _abi.PonniError(st, err.value.decode())
+    return out.reshape(dims)
+
+
+class GeneratedModel:
+    """Mirror of the generated model struct (``Scalar`` = float or double)."""
+
+    def __init__(self, dense: list[Dense], scalar=np.float32, device: int = 0):
+        if not dense:
+            raise ValueError("a generated model needs at least one dense layer")
+        for a, b in zip(dense, dense[1:]):
+            if a.weight.shape[0] != b.weight.shape[1]:
+                raise ValueError(f"{a.name} -> {b.name}: width mismatch")
+        self.dense = list(dense)
+        self.scalar = np.dtype(scalar)
+        if self.scalar not in (np.dtype(np.float32), np.dtype(np.float64)):
+            raise ValueError("GeneratedModel Scalar must be float or double")
+        self.device = device
+        self.num_inputs = self.dense[0].weight.shape[1]
+        self.num_outputs = self.dense[-1].weight.shape[0]
+        self._models: dict[int, Inference] = {}
+
+    # -- parameters (emitter.py:1724-1895) --
+    @staticmethod
+    def _layer_list(dense):
+        out = []
+        for d in dense:
+            out.append(L.Matvec(d.weight.T))
+            if d.bias is not None:
+                out.append(L.Bias(d.bias))
+            if d.activation is not None:
+                out.append(_ACT[d.activation](d.weight.shape[0], d.alpha))
+        return out
+
+    def get_num_parameters(self) -> int:
+        return int(sum(d.weight.size + (d.bias.size if d.bias is not None else 0) for d in self.dense))
+
+    def get_parameters(self) -> np.ndarray:
+        """Learned parameters in layer order: W[out, in] row-major, then the bias."""
+        parts = []
+        for d in self.dense:
+            parts.append(d.weight.reshape(-1))
+            if d.bias is not None:
+                parts.append(d.bias)
+        return np.concatenate(parts).astype(self.scalar)
+
+    def set_parameters(self, values) -> None:
+        v = np.asarray(values, dtype=np.float64).reshape(-1)
+        if v.size != self.get_num_parameters():
+            raise _abi.PonniError(2, "GeneratedModel::set_parameters source extent is incorrect")
+        if not np.all(np.isfinite(v)):
+            raise _abi.PonniError(2, "GeneratedModel::set_parameters received non-finite values")
+        off = 0
+        for d in self.dense:
+            n = d.weight.size
+            d.weight = v[off:off + n].reshape(d.weight.shape).copy()
+            off += n
+            if d.bias is not None:
+                d.bias = v[off:off + d.bias.size].copy()
+                off += d.bias.size
+        self._models.clear()
+
+    def load_weights(self, path: str) -> None:
+        """Named tensors <name>.weight [out, in] and <name>.bias of a .ponni file."""
+        for d in self.dense:
+            w = _read_tensor(path, f"{d.name}.weight").astype(np.float64)
+            if w.shape != d.weight.shape:
+                raise _abi.PonniError(2, f"{d.name}.weight has shape {w.shape}, expected {d.weight.shape}")
+            d.weight = w
+            if d.bias is not None:
+                d.bias = _read_tensor(path, f"{d.name}.bias").astype(np.float64).reshape(-1)
+        self._models.clear()
+
+    # -- inference --
+    def _model(self, dtype: int) -> Inference:
+        m = self._models.get(dtype)
+        if m is None:
+            m = Inference(self._layer_list(self.dense), dtype=dtype, device=self.device,
+                          arithmetic=_abi.ARITH_GENERATED)
+            self._models[dtype] = m
+        return m
+
+    def infer_batch(self, inputs):
+        """inputs [num_inputs, batch] in Scalar (numpy, or a CUDA torch tensor) -> outputs."""
+        dt = _abi.F32 if self.scalar == np.float32 else _abi.F64
+        return self._model(dt).forward_batch_parallel(inputs)
+
+    def infer_batch_half2(self, inputs):
+        """fp32 inputs -> fp32 outputs with fp16 parameters and fused fp16
+        accumulation (the generated infer_batch_half2)."""
+        m = self._model(_abi.F16)
+        try:
+            import torch
+            if isinstance(inputs, torch.Tensor) and inputs.is_cuda:
+                return m.forward_batch_parallel(inputs.to(torch.float16)).to(torch.float32)
+        except ImportError:
+            pass
+        x = to_dtype_bytes(np.asarray(inputs, dtype=np.float64), _abi.F16)
+        return from_dtype_bytes(m.forward_batch_parallel(x), _abi.F16).astype(np.float32)
+
+    def infer_one(self, inputs) -> np.ndarray:
+        x = np.asarray(inputs, dtype=self.scalar).reshape(self.num_inputs, 1)
+        return np.asarray(self.infer_batch(x)).reshape(-1)

@@ -1,0 +1,133 @@
+"""Generated-model arithmetic (ARITH_GENERATED) and the GeneratedModel
+mirror of the reference's generated struct (emitter.py:693-735, :967-1010,
+:1724-1955): dense sums start at the bias, 16-bit products are fused
+multiply-adds, weights are [out, in]."""
+import os
+
+import numpy as np
+import pytest
+
+import ponni_b200 as pb
+from oracle import oracle
+from tests import kat_models as K
+
+
+def dense_chain(rng, dims=(6, 9, 7, 3), acts=("silu", "relu", None)):
+    out = []
+    for i in range(len(dims) - 1):
+        w = rng.normal(0, 1 / np.sqrt(dims[i]), (dims[i + 1], dims[i]))
+        b = rng.normal(0, 0.2, dims[i + 1]) if i != 1 else None  # one layer without bias
+        out.append(pb.Dense(f"fc{i}", w, b, acts[i]))
+    return out
+
+
+def numpy_generated(dense, x, dtype):
+    """Direct restatement of the emitted loops: sum = b(i); sum += W(i,j) * x(j)."""
+    if dtype == pb.F16:
+        cur = x.astype(np.float16)
+        for d in dense:
+            w = d.weight.astype(np.float16)
+            nxt = np.empty((w.shape[0], cur.shape[1]), np.float16)
+            for i in range(w.shape[0]):
+                s = (d.bias.astype(np.float16)[i] if d.bias is not None else np.float16(0)) * np.ones(cur.shape[1], np.float16)
+                for j in range(w.shape[1]):  # one rounding per fused multiply-add
+                    s = (w[i, j].astype(np.float64) * cur[j].astype(np.float64) + s.astype(np.float64)).astype(np.float16)
+                nxt[i] = s
+            cur = act_np(d.activation, nxt.astype(np.float32)).astype(np.float16)
+        return cur
+    cur = x.astype(np.float64)
+    for d in dense:
+        s = d.weight @ cur + (d.bias[:, None] if d.bias is not None else 0.0)
+        cur = act_np(d.activation, s)
+    return cur
+
+
+def act_np(a, v):
+    if a is None:
+        return v
+    if a == "relu":
+        return np.maximum(v, 0)
+    if a == "silu":
+        return v / (1 + np.exp(-v))
+    raise ValueError(a)
+
+
+def test_oracle_generated_fp64_closed_form():
+    rng = np.random.default_rng(1)
+    dense = dense_chain(rng)
+    x = rng.normal(0, 1, (6, 50))
+    layers = pb.GeneratedModel(dense, np.float64)._layer_list(dense)
+    y = oracle.forward(layers, pb.F64, x, generated=True)
+    assert np.max(np.abs(y - numpy_generated(dense, x, pb.F64))) <= 1e-12
+
+
+def test_oracle_generated_half_fused():
+    rng = np.random.default_rng(2)
+    dense = dense_chain(rng)
+    x = rng.normal(0, 1, (6, 40))
+    layers = pb.GeneratedModel(dense)._layer_list(dense)
+    y = pb.from_dtype_bytes(oracle.forward(layers, pb.F16, pb.to_dtype_bytes(x, pb.F16), generated=True), pb.F16)
+    ref = numpy_generated(dense, x, pb.F16).astype(np.float32)
+    assert np.max(np.abs(y - ref)) <= 2e-3 * np.max(np.abs(ref))  # transcendental rounding may differ by a unit
+
+
+def test_generated_parameters_round_trip():
+    rng = np.random.default_rng(3)
+    g = pb.GeneratedModel(dense_chain(rng))
+    n = g.get_num_parameters()
+    assert n == 6 * 9 + 9 + 9 * 7 + 7 * 3 + 3
+    v = g.get_parameters()
+    g.set_parameters(v[::-1].copy())
+    assert np.array_equal(g.get_parameters(), v[::-1])
+    with pytest.raises(pb.PonniError):
+        g.set_parameters(v[:-1])
+    bad = v.copy()
+    bad[0] = np.nan
+    with pytest.raises(pb.PonniError):
+        g.set_parameters(bad)
+
+
+def test_generated_load_named_weights():
+    """Named tensors of a .ponni file (the reference-generated pytorch_resnet
+    fixture) load by name, shape-checked."""
+    path = os.path.join(K.GOLDEN, "pytorch_resnet.ponni")
+    for i in range(1, 6):
+        t = K.read_tensor(path, f"fc{i}.weight").astype(np.float64)
+        g = pb.GeneratedModel([pb.Dense(f"fc{i}", np.zeros(t.shape))])
+        g.load_weights(path)
+        assert np.array_equal(g.dense[0].weight, t)
+    g = pb.GeneratedModel([pb.Dense("fc1", np.zeros((3, 3)))])
+    with pytest.raises(pb.PonniError):
+        g.load_weights(path)  # wrong shape
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F64, pb.F16, pb.BF16])
+def test_gpu_generated_arithmetic(dtype):
+    import torch
+    from tests.test_gpu_parity import check, from_torch, to_torch
+    rng = np.random.default_rng(4)
+    dense = dense_chain(rng, dims=(12, 40, 33, 5))
+    layers = pb.GeneratedModel(dense)._layer_list(dense)
+    m = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_GENERATED)
+    assert m.kernel() == pb._abi.KERNEL_TILE
+    x = pb.to_dtype_bytes(rng.normal(0, 1, (12, 3001)), dtype)
+    y = from_torch(m.forward_batch_parallel(to_torch(x, dtype).cuda()), dtype)
+    torch.cuda.synchronize()
+    check(y, oracle.forward(layers, dtype, x, generated=True), dtype, layers, x)
+
+
+@pytest.mark.gpu
+def test_gpu_generated_model_api():
+    rng = np.random.default_rng(5)
+    dense = dense_chain(rng, dims=(12, 40, 33, 5))
+    g = pb.GeneratedModel(dense)
+    x = rng.normal(0, 1, (12, 2000)).astype(np.float32)
+    layers = g._layer_list(dense)
+    y = g.infer_batch(x)
+    ref = oracle.forward(layers, pb.F32, x, generated=True)
+    assert K.normwise_err(y, ref) <= 1e-5
+    yh = g.infer_batch_half2(x)
+    refh = pb.from_dtype_bytes(oracle.forward(layers, pb.F16, pb.to_dtype_bytes(x, pb.F16), generated=True), pb.F16)
+    assert yh.dtype == np.float32 and K.normwise_err(yh, refh) <= 2e-3
+    assert np.allclose(g.infer_one(x[:, 7]), y[:, 7], rtol=1e-6, atol=1e-7)
