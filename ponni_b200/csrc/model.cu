@@ -439,16 +439,27 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
   p.n_params = (int32_t)(param_bytes / esz);
 
   // Candidates: batch tile 128 / 64 / 32, parameters in shared or global
-  // memory.  The largest tile wins (a 256-thread CTA needs 128 columns to keep
-  // every thread busy on 64-wide layers); within it the higher occupancy, and
-  // on a tie the parameters on chip.  Measured on cfg2 (fp32 30-64-64-64-10):
-  // 128 columns with parameters in L1/L2 at 2 CTAs/SM beats the same tile with
-  // parameters in shared memory at 1 CTA/SM by 1.24x.
+  // memory.  Preferred: at least two resident CTAs (16 warps per SM to hide
+  // shared-memory and FMA latency), then the largest tile (a 256-thread CTA
+  // needs 128 columns to keep every thread busy on 64-wide layers), then the
+  // higher occupancy, then the parameters on chip.  Measured: cfg2 (fp32
+  // 30-64-64-64-10) 128 columns with parameters in L1/L2 at 2 CTAs/SM beat
+  // the same tile with parameters in shared memory at 1 CTA/SM by 1.24x; cfg4
+  // (128-wide residual blocks) 64 columns at 2 CTAs/SM beat 128 columns at 1
+  // CTA/SM by 1.69x.
   // PONNI_B200_TILE="bt,params_in_smem" overrides (tuning aid).
   int force_bt = 0, force_psm = -1;
   if (const char* env = getenv("PONNI_B200_TILE")) sscanf(env, "%d,%d", &force_bt, &force_psm);
   int best_bt = 0, best_occ = 0, best_psm = 0;
   size_t best_smem = 0;
+  auto better = [&](int bt, int occ, int psm) {
+    if (best_bt == 0) return true;
+    const int a = std::min(occ, 2), b = std::min(best_occ, 2);
+    if (a != b) return a > b;
+    if (bt != best_bt) return bt > best_bt;
+    if (occ != best_occ) return occ > best_occ;
+    return psm > best_psm;
+  };
   for (int bt : {128, 64, 32}) {
     if (force_bt && bt != force_bt) continue;
     for (int psm : {1, 0}) {
@@ -458,13 +469,12 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       if (psm) smem += param_bytes;
       if (smem > 227 * 1024) continue;
       int occ = tile_forward_occupancy((int)m->dtype, smem);
-      if (occ <= 0 || occ <= best_occ) continue;
+      if (occ <= 0 || !better(bt, occ, psm)) continue;
       best_bt = bt;
       best_occ = occ;
       best_psm = psm;
       best_smem = smem;
     }
-    if (best_bt) break;
   }
   if (best_bt == 0)
     return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED,
