@@ -92,7 +92,7 @@ __device__ __forceinline__ void epilogue(const EpiArgs E, bool last, uint32_t tm
     const long long t_ld = clock64();
 #endif
     int g = 1;
-    if (E.groups == 1) {
+    if (sizeof(T) != 4 || E.groups == 1) {  // 16-bit models keep one accumulator per layer
       tmem_ld32(tmem_lane + (uint32_t)c0, v);
     } else {
       float w[32];
@@ -101,13 +101,13 @@ __device__ __forceinline__ void epilogue(const EpiArgs E, bool last, uint32_t tm
       for (int j = 0; j < 32; ++j) v[j] += w[j];
       g = 2;
     }
-    for (; g + 1 < E.groups; g += 2) {
+    for (; sizeof(T) == 4 && g + 1 < E.groups; g += 2) {
       float w0[32], w1[32];
       tmem_ld32x2(tmem_lane + (uint32_t)(g * E.n_pad + c0), tmem_lane + (uint32_t)((g + 1) * E.n_pad + c0), w0, w1);
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] += w0[j] + w1[j];
     }
-    for (; g < E.groups; ++g) {
+    for (; sizeof(T) == 4 && g < E.groups; ++g) {
       float w[32];
       tmem_ld32(tmem_lane + (uint32_t)(g * E.n_pad + c0), w);
 #pragma unroll
@@ -268,7 +268,7 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
 // accumulators and walk their own tiles; while one slot runs its epilogue the
 // tensor core works on the other's chain.
 template <class T, int TPS>
-__global__ void __launch_bounds__(kTcMaxThreads, 1)
+__global__ void __launch_bounds__(TPS == 128 && sizeof(T) == 2 ? kTcMaxThreads : kTcMaxThreads / 2, 1)
     tc_forward_kernel(const __grid_constant__ TcProgram p, const unsigned char* __restrict__ image,
                       const T* __restrict__ in, int64_t in_ld, T* __restrict__ out, int64_t out_ld, int64_t batch,
                       int in_vec, int* __restrict__ err) {
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
   // Layer table copied to shared memory: the layer loop indexes it with a
   // run-time index, which on the kernel-parameter copy would go through the
   // constant cache's slow address-divergence path.
-  TcLayer* layers = reinterpret_cast<TcLayer*>(base_ptr + (s_bars + 64u - base));
+  TcLayer* layers = reinterpret_cast<TcLayer*>(base_ptr + (s_bars + 128u - base));
 
   const int64_t ntiles = (batch + kTcM - 1) / kTcM;
   if ((int64_t)blockIdx.x * nslots >= ntiles) return;
@@ -386,6 +386,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
         TC_PROF_ADD(4, t_mma);
       }
       phase ^= 1u;
+      TC_PROF_T(t_post);
       const int bad = wg_sync_or<TPS>(wg, !ok);
       tc_fence_after();
       if (bad) {
@@ -398,6 +399,7 @@ __global__ void __launch_bounds__(kTcMaxThreads, 1)
           if (next < ntiles) load_input<T, TPS>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
           cp_async_commit();
         }
+        TC_PROF_ADD(1, t_post);  // 16-bit models have no split phase: slot 1 times the hand-off
       }
       const float* bias = reinterpret_cast<const float*>(base_ptr + bias_off);
       TC_PROF_T(t_epi);

@@ -163,6 +163,9 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   if (const char* env = getenv("PONNI_B200_TC_GROUP_STEPS")) gs_req = std::max(1, atoi(env));
   for (int pass = 0; pass < 2; ++pass) {
     for (int slots = kTcMaxSlots; slots >= 1; --slots) {
+      // 128-thread slots: up to 8 for 16-bit models (64 registers a thread),
+      // up to 4 for fp32 split models (their epilogue needs 128 registers)
+      if (slots * (slots >= 3 ? 128 : 256) > (split ? kTcMaxThreads / 2 : kTcMaxThreads)) continue;
       const int col_budget = 512 / slots;
       max_npad = 0;
       bool longer = false;
@@ -180,7 +183,7 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
       p.slot_cols = (uint32_t)round_up(max_npad, 32);
       uint32_t cols = 32;
       while (cols < (uint32_t)slots * p.slot_cols) cols <<= 1;
-      p.smem_bytes = 1024 + p.image_bytes + (uint32_t)slots * p.slot_bytes + 64 +
+      p.smem_bytes = 1024 + p.image_bytes + (uint32_t)slots * p.slot_bytes + 128 +
                      (uint32_t)(kTcMaxLayers * sizeof(TcLayer));
       if (cols <= 512 && p.smem_bytes <= 227 * 1024) {
         p.tmem_cols = cols;

@@ -22,8 +22,8 @@
 namespace ponni_b200 {
 
 constexpr int kTcMaxLayers = 16;
-constexpr int kTcMaxSlots = 4;     // tiles in flight per CTA (TcProgram::slots = 1..4)
-constexpr int kTcMaxThreads = 512;  // slots x slot_threads
+constexpr int kTcMaxSlots = 8;      // tiles in flight per CTA (TcProgram::slots = 1..8; 5..8 for 16-bit models)
+constexpr int kTcMaxThreads = 1024; // slots x slot_threads (fp32 split models: at most 512)
 // Threads of one slot (TcProgram::slot_threads): 128 = 4 warps, one per TMEM
 // lane quarter, each thread walking all accumulator columns of its lane; or
 // 256 = 8 warps, 4 lane quarters x 2 column halves (used with <= 2 slots).
@@ -55,7 +55,7 @@ struct TcProgram {
   uint32_t slot_bytes;   // shared memory of one slot: parts x a_bytes + stage_bytes
   uint32_t slot_cols;    // TMEM columns of one tile slot (max over layers of groups * n_pad)
   uint32_t tmem_cols;    // allocated TMEM columns: power of two >= slots * slot_cols
-  int32_t slots;         // tile slots per CTA (1..4); the CTA runs slots * slot_threads threads
+  int32_t slots;         // tile slots per CTA (1..8); the CTA runs slots * slot_threads threads
   int32_t slot_threads;  // 128 or 256
   uint32_t smem_bytes;   // total dynamic shared memory requested (incl. 1 KB alignment slack,
                          // mbarriers, the TMEM address and a copy of the layer table)
