@@ -214,17 +214,22 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
       a0[q] = smem_desc(s_a[q], 16, 1024);
       b0[q] = smem_desc(s_image + L.w_off[q], 16, 1024);
     }
+    // Accumulators: groups - 1 "main" ones, each summing the dominant
+    // products a0*b0 of gstep consecutive K steps, and one "correction"
+    // accumulator for the five smaller products of every step (their
+    // truncation errors are 2^-8 smaller).  The tensor core's fp32
+    // accumulation truncates, so bounding the additions into each main
+    // accumulator keeps the result fp32-accurate; the epilogue sums all.
+    const uint32_t dc = d_tmem + (uint32_t)(L.groups - 1) * n_pad;
     for (int s = 0; s < nsteps; ++s) {
       const uint64_t ao = (uint64_t)(s >> 2) * 1024 + (uint64_t)(s & 3) * 2;
       const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
-      const uint32_t acc = in_group ? 1u : 0u;
-      // smallest products first
-      umma_f16_warp(d, a0[1] + ao, b0[1] + bo, idesc, acc);
-      umma_f16_warp(d, a0[0] + ao, b0[2] + bo, idesc, 1u);
-      umma_f16_warp(d, a0[2] + ao, b0[0] + bo, idesc, 1u);
-      umma_f16_warp(d, a0[0] + ao, b0[1] + bo, idesc, 1u);
-      umma_f16_warp(d, a0[1] + ao, b0[0] + bo, idesc, 1u);
-      umma_f16_warp(d, a0[0] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16_warp(dc, a0[1] + ao, b0[1] + bo, idesc, s > 0 ? 1u : 0u);  // smallest products first
+      umma_f16_warp(dc, a0[0] + ao, b0[2] + bo, idesc, 1u);
+      umma_f16_warp(dc, a0[2] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16_warp(dc, a0[0] + ao, b0[1] + bo, idesc, 1u);
+      umma_f16_warp(dc, a0[1] + ao, b0[0] + bo, idesc, 1u);
+      umma_f16_warp(d, a0[0] + ao, b0[0] + bo, idesc, in_group ? 1u : 0u);
       if (++in_group == gstep) {
         in_group = 0;
         d += n_pad;

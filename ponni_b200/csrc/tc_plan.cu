@@ -154,12 +154,13 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   p.a_bytes = std::max(a_kmajor, 1024u);
   p.slot_bytes = p.a_bytes * (uint32_t)nparts + p.stage_bytes;
   // As many tile slots (tiles in flight per SM) as shared and tensor memory
-  // allow, up to four.  fp32 (split) models spread the K steps over separate
-  // accumulators summed in the epilogue (PONNI_B200_TC_GROUP_STEPS steps
-  // each; default 1): the tensor core's fp32 accumulation truncates, so short
-  // chains keep the result fp32-accurate; a slot count that would force
+  // allow.  fp32 (split) models use ceil(steps / gs) main accumulators of
+  // the dominant products (PONNI_B200_TC_GROUP_STEPS K steps each; default 4)
+  // plus one accumulator of the smaller products, summed in the epilogue: the
+  // tensor core's fp32 accumulation truncates, so short chains into each main
+  // accumulator keep the result fp32-accurate; a slot count that would force
   // longer chains is skipped unless nothing else fits.
-  int gs_req = 1;
+  int gs_req = 4;
   if (const char* env = getenv("PONNI_B200_TC_GROUP_STEPS")) gs_req = std::max(1, atoi(env));
   for (int pass = 0; pass < 2; ++pass) {
     for (int slots = kTcMaxSlots; slots >= 1; --slots) {
@@ -172,11 +173,12 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
       for (int l = 0; l < p.n_layers; ++l) {
         TcLayer& L = p.layers[l];
         const int nsteps = L.k_pad / 16;
-        int gs = split ? gs_req : nsteps;
-        while (gs < nsteps && round_up((int64_t)((nsteps + gs - 1) / gs) * L.n_pad, 32) > col_budget) ++gs;
+        const int extra = split ? 1 : 0;  // the correction accumulator
+        int gs = split ? std::min(gs_req, nsteps) : nsteps;
+        while (gs < nsteps && round_up((int64_t)((nsteps + gs - 1) / gs + extra) * L.n_pad, 32) > col_budget) ++gs;
         if (split && gs > gs_req && gs < nsteps) longer = true;
         L.group_steps = std::min(gs, nsteps);
-        L.groups = (nsteps + L.group_steps - 1) / L.group_steps;
+        L.groups = (nsteps + L.group_steps - 1) / L.group_steps + extra;
         max_npad = std::max(max_npad, L.groups * L.n_pad);
       }
       if (longer && pass == 0) continue;

@@ -40,8 +40,8 @@ struct TcLayer {
   uint32_t w_off[3];     // byte offsets of the K-major B operand parts (1, or 3 for split fp32)
   uint32_t idesc;        // UMMA instruction descriptor (A K-major)
   uint32_t idesc_mn;     // same with A MN-major (layer 0)
-  int32_t groups;        // fp32 accumulators the K steps are spread over (summed in the epilogue)
-  int32_t group_steps;   // consecutive K steps per accumulator
+  int32_t groups;        // fp32 accumulators summed in the epilogue (split models: main ones + one correction)
+  int32_t group_steps;   // consecutive K steps per (main) accumulator
 };
 
 struct TcProgram {
