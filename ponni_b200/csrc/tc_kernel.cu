@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(TPS == 128 && sizeof(T) == 2 ? kTcMaxThreads :
   const int64_t stride = (int64_t)gridDim.x * nslots;
   int64_t tile = (int64_t)blockIdx.x * nslots + wg;
   uint32_t phase = 0;
-  if (tile < ntiles) {
+  if (!SPLIT && tile < ntiles) {
     load_input<T, TPS>(stage, in, in_ld, p.nin, tile * kTcM, batch, in_vec != 0, lt);
     cp_async_commit();
   }
@@ -347,19 +347,22 @@ __global__ void __launch_bounds__(TPS == 128 && sizeof(T) == 2 ? kTcMaxThreads :
     TC_PROF_ADD(0, t_in);
     TC_PROF_T(t_split);
     if constexpr (SPLIT) {
-      // Thread m splits column m of the staged fp32 tile into the K-major
-      // bf16 operand parts of layer 0; then the stage is free for the next tile.
-      const int k0 = p.layers[0].k_pad;
-      const float* st = reinterpret_cast<const float*>(base_ptr + (stage - base));
-      for (int f = 8 * half; f < k0; f += 8 * (TPS / 128)) {
-        float v[8];
+      // Thread m reads column m of the input straight from global memory (a
+      // warp reads 32 consecutive columns of a feature row: coalesced) and
+      // splits it into the K-major bf16 operand parts of layer 0.  No input
+      // stage: the shared memory goes to more tile slots, whose work hides
+      // this load's latency.
+      const int k0 = p.layers[0].k_pad, nin = p.nin;
+      const int64_t col = col0 + m;
+      const bool live = col < batch;
+      const float* src = reinterpret_cast<const float*>(in) + col;
+      for (int f = 16 * half; f < k0; f += 16 * (TPS / 128)) {
+        float v[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = st[(f + e) * kTcM + m];
+        for (int e = 0; e < 16; ++e) v[e] = (live && f + e < nin) ? __ldg(src + (int64_t)(f + e) * in_ld) : 0.0f;
         store_row8<T>(s_a, m, f, v);
+        if (f + 8 < k0) store_row8<T>(s_a, m, f + 8, v + 8);
       }
-      wg_sync<TPS>(wg);
-      if (next < ntiles) load_input<T, TPS>(stage, in, in_ld, p.nin, next * kTcM, batch, in_vec != 0, lt);
-      cp_async_commit();
     }
     TC_PROF_ADD(1, t_split);
     bool failed = false;

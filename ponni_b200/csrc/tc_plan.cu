@@ -148,8 +148,8 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   }
   const int k0 = p.layers[0].k_pad;
   if (split) max_w32 = std::max(max_w32, (int)round_up(k0, 32));  // fp32 layer 0 is K-major
-  // fp32: row-major [k0][128] fp32 staging; 16-bit: MN-major operand (k0/8 atoms of 2 KB).
-  p.stage_bytes = split ? (uint32_t)k0 * kTcM * 4 : (uint32_t)(k0 / 8) * 2048;
+  // 16-bit: the staged input is the MN-major layer-0 operand (k0/8 atoms of 2 KB).
+  p.stage_bytes = split ? 0u : (uint32_t)(k0 / 8) * 2048;  // fp32: input read straight into the split
   const uint32_t a_kmajor = (uint32_t)((max_w32 * 2 + 127) / 128) * kTcM * 128;
   p.a_bytes = std::max(a_kmajor, 1024u);
   p.slot_bytes = p.a_bytes * (uint32_t)nparts + p.stage_bytes;
