@@ -248,6 +248,39 @@ ponni_b200_status ponni_b200_set_trainable_parameters(ponni_b200_model* model, c
 ponni_b200_status ponni_b200_get_trainable_parameters(ponni_b200_model* model, void* host,
                                                       int64_t count);
 
+/* Parameter updates of a planned model (one that has run a forward or been
+ * prepared by ponni_b200_model_kernel) go straight into its device images:
+ * ponni_b200_set_trainable_parameters stages the host values in pinned memory
+ * and scatters them on the model stream without a re-plan (replaces the
+ * reference's set_trainable_parameters + re-upload, src/ponni_Inference.h:689-703,
+ * and the load path of load_weights, :295-316).
+ *
+ * _device: `src` is device-accessible memory holding `count` >= the
+ * trainable count values of `src_dtype` in tuple order; each is converted to
+ * the model dtype (fp64 kept, other types through fp32) and written into
+ * every device image on `stream` (NULL: the model stream; another stream is
+ * joined into the model stream).  Counterpart of the generated model's
+ * set_parameters(View, execution space), emitter.py:1826-1866.  The host
+ * copy is read back only when needed (get_trainable_parameters, save, a
+ * re-plan). */
+ponni_b200_status ponni_b200_set_trainable_parameters_device(ponni_b200_model* model, const void* src,
+                                                             ponni_b200_dtype src_dtype, int64_t count,
+                                                             void* stream);
+/* Trainable parameters in tuple order converted to `dst_dtype` into
+ * device-accessible `dst`, on `stream` (generated get_parameters,
+ * emitter.py:1787-1825). */
+ponni_b200_status ponni_b200_get_trainable_parameters_device(ponni_b200_model* model, void* dst,
+                                                             ponni_b200_dtype dst_dtype, int64_t count,
+                                                             void* stream);
+/* Synchronous check of the device images: `mismatches` = image locations
+ * (tensor-core weight parts and biases, the specialised narrow kernel's
+ * argument block) that differ from the encoding of the packed parameter;
+ * `nonfinite` = trainable values that are NaN or infinite.  Counterparts of
+ * parameters_synchronized and parameters_are_finite, emitter.py:1868-1895.
+ * Either pointer may be NULL. */
+ponni_b200_status ponni_b200_check_parameters(ponni_b200_model* model, int64_t* mismatches,
+                                              int64_t* nonfinite);
+
 /* "fnv1a64:%016x" of the reference's template schema text; buf >= 25 bytes. */
 ponni_b200_status ponni_b200_weight_schema_fingerprint(const ponni_b200_model* model, char* buf,
                                                        size_t len);

@@ -86,6 +86,9 @@ SIGNATURES = {
     "ponni_b200_num_trainable_parameters": (_I64, [_P]),
     "ponni_b200_set_trainable_parameters": (_STATUS, [_P, _P, _I64]),
     "ponni_b200_get_trainable_parameters": (_STATUS, [_P, _P, _I64]),
+    "ponni_b200_set_trainable_parameters_device": (_STATUS, [_P, _P, ctypes.c_int, _I64, _P]),
+    "ponni_b200_get_trainable_parameters_device": (_STATUS, [_P, _P, ctypes.c_int, _I64, _P]),
+    "ponni_b200_check_parameters": (_STATUS, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     "ponni_b200_weight_schema_fingerprint": (_STATUS, [_P, ctypes.c_char_p, ctypes.c_size_t]),
     "ponni_b200_model_save_weights": (_STATUS, [_P, ctypes.c_char_p]),
     "ponni_b200_model_load_weights": (_STATUS, [_P, ctypes.c_char_p]),

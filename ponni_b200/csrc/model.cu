@@ -193,6 +193,7 @@ struct Planner {
   std::vector<unsigned char>& packed;
   size_t esz;
   int width[kMaxBuffers] = {0};
+  ParamMap* rec = nullptr;  // receives the packed location of every trainable parameter
 
   // Append `n` parameters (canonical, model dtype) to the packed buffer,
   // 16-element aligned; returns the element offset.
@@ -200,14 +201,21 @@ struct Planner {
     int64_t off = align_up((int64_t)(packed.size() / esz), 16);
     packed.resize((size_t)(off + n) * esz, 0);
     if (n) memcpy(packed.data() + off * esz, src, (size_t)n * esz);
+    if (rec)
+      for (int64_t i = 0; i < n; ++i) rec->add(src + i * esz, PIMG_PACKED, PENC_MODEL, (size_t)(off + i) * esz);
     return off;
   }
   // Append W[k][o] (rows of nout) padded to rows of nout_pad with zeros.
   int64_t append_matrix(const unsigned char* src, int nin, int nout, int nout_pad) {
     int64_t off = align_up((int64_t)(packed.size() / esz), 16);
     packed.resize((size_t)(off + (int64_t)nin * nout_pad) * esz, 0);
-    for (int k = 0; k < nin; ++k)
+    for (int k = 0; k < nin; ++k) {
       memcpy(packed.data() + (off + (int64_t)k * nout_pad) * esz, src + (size_t)k * nout * esz, (size_t)nout * esz);
+      if (rec)
+        for (int o = 0; o < nout; ++o)
+          rec->add(src + ((size_t)k * nout + o) * esz, PIMG_PACKED, PENC_MODEL,
+                   (size_t)(off + (int64_t)k * nout_pad + o) * esz);
+    }
     return off;
   }
   ponni_b200_status fail(const std::string& s) { return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED, s); }
@@ -428,9 +436,25 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
   if (st) return st;
   st = pb_ensure_cuda(m);
   if (st) return st;
+  // Parameters updated from device memory: read them back before re-packing.
+  st = pb_pull_params(m);
+  if (st) return st;
   const size_t esz = dtype_bytes(m->dtype);
   std::vector<unsigned char> packed;
+  m->pmap.clear();
+  m->pmap.esz = esz;
+  m->pmap_uploaded = false;
+  {
+    int64_t base = 0;
+    for (const auto& L : m->layers) {
+      const int64_t n = L.num_trainable();
+      if (n == 0) continue;
+      m->pmap.ranges.push_back({L.params.data(), L.params.data() + (size_t)n * esz, base});
+      base += n;
+    }
+  }
   Planner pl{m, m->prog, packed, esz};
+  pl.rec = &m->pmap;
   st = pl.run();
   if (st) return st;
   Program& p = m->prog;
@@ -528,7 +552,10 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
     // streamed-weights kernel even when their weights fit shared memory.
     const char* force_stream = getenv("PONNI_B200_TC_STREAM");
     const bool stream_first = force_stream && force_stream[0] == '1' && m->dtype != PONNI_B200_F32;
-    if (!stream_first && tc_plan(m, m->tcp, image, m->tc_why)) {
+    ParamMap tc_rec;
+    tc_rec.ranges = m->pmap.ranges;
+    tc_rec.esz = esz;
+    if (!stream_first && tc_plan(m, m->tcp, image, m->tc_why, &tc_rec)) {
       if (image.size() > m->tc_image_bytes) {
         if (m->tc_image_dev) cudaFree(m->tc_image_dev);
         m->tc_image_dev = nullptr;
@@ -550,10 +577,13 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       if (e != cudaSuccess) return cuda_fail(m, e, "tensor-core parameter upload");
       m->tc_grid = m->num_sms;  // one persistent CTA (up to four tile slots) per SM
       m->kernel = 2;
+      m->pmap.recs.insert(m->pmap.recs.end(), tc_rec.recs.begin(), tc_rec.recs.end());
+      m->pmap.overflow |= tc_rec.overflow;
     } else if (m->arithmetic == PONNI_B200_ARITH_TENSOR) {
       // Weights beyond shared memory: stream them per layer (16-bit models).
       std::string why2;
-      if (!ts_plan(m, m->tsp, image, why2))
+      tc_rec.recs.clear();
+      if (!ts_plan(m, m->tsp, image, why2, &tc_rec))
         return pb_fail(m, PONNI_B200_ERR_UNSUPPORTED,
                        "tensor-core kernel unavailable: " + (m->tc_why.empty() ? why2 : m->tc_why + "; " + why2));
       if (image.size() > m->ts_image_bytes) {
@@ -575,6 +605,8 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       if (e != cudaSuccess) return cuda_fail(m, e, "streamed tensor-core parameter upload");
       m->tc_grid = m->num_sms;
       m->kernel = 5;
+      m->pmap.recs.insert(m->pmap.recs.end(), tc_rec.recs.begin(), tc_rec.recs.end());
+      m->pmap.overflow |= tc_rec.overflow;
     }
   }
   // Narrow chains (every width <= 32) stream through registers, unless the
@@ -717,7 +749,7 @@ ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, i
 void ponni_b200_model_destroy(ponni_b200_model* m) {
   if (!m) return;
   if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev || m->prog_dev ||
-      m->ts_image_dev) {
+      m->ts_image_dev || m->pmap_dev.recs || m->pmap_dev.staging) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
@@ -727,6 +759,7 @@ void ponni_b200_model_destroy(ponni_b200_model* m) {
     if (m->stage_dev) cudaFree(m->stage_dev);
     if (m->tc_image_dev) cudaFree(m->tc_image_dev);
     if (m->err_dev) cudaFree(m->err_dev);
+    pb_free_param_map(m);
     if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
     if (m->own_stream) cudaStreamDestroy(m->own_stream);
   }
@@ -934,6 +967,10 @@ ponni_b200_status ponni_b200_set_trainable_parameters(ponni_b200_model* m, const
     memcpy(L.params.data(), src, (size_t)n * esz);
     src += (size_t)n * esz;
   }
+  m->host_params_stale = false;  // every trainable value was just written
+  // A planned model takes the values into its device images directly
+  // (pinned staging + device scatter); otherwise the next forward re-plans.
+  if (pb_update_params_from_host(m, host, need) == PONNI_B200_OK) return PONNI_B200_OK;
   m->params_dirty = true;
   return PONNI_B200_OK;
 }
@@ -942,6 +979,8 @@ ponni_b200_status ponni_b200_get_trainable_parameters(ponni_b200_model* m, void*
   if (!m || (!host && count > 0)) return PONNI_B200_ERR_INVALID_ARGUMENT;
   const int64_t need = ponni_b200_num_trainable_parameters(m);
   if (count < need) return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "output buffer too small");
+  ponni_b200_status st = pb_pull_params(m);  // after updates from device memory
+  if (st) return st;
   const size_t esz = dtype_bytes(m->dtype);
   unsigned char* dst = static_cast<unsigned char*>(host);
   for (auto& L : m->layers) {

@@ -9,6 +9,7 @@
 #include "program.h"
 #include "narrow_jit.h"
 #include "narrow_kernel.h"
+#include "param_map.h"
 #include "tc_program.h"
 #include "tc_stream.h"
 
@@ -77,6 +78,14 @@ struct ponni_b200_model {
   int64_t capacity = 0;  // reference internal_state_capacity()
   void* stage_dev = nullptr;  // forward_host staging buffers
   size_t stage_bytes = 0;
+  // Device-side parameter updates: where each trainable parameter lives in
+  // the planned images (rebuilt by every plan) and its device copy.
+  ponni_b200::ParamMap pmap;
+  ponni_b200::ParamMapDev pmap_dev;
+  bool pmap_uploaded = false;
+  // The device images hold newer parameters than `layers[].params` and
+  // `packed_host` (after an update from device memory); read back on demand.
+  bool host_params_stale = false;
 };
 
 // Helpers shared by the C ABI translation units.
@@ -85,3 +94,6 @@ ponni_b200_status pb_validate(ponni_b200_model* m);
 ponni_b200_status pb_plan(ponni_b200_model* m);
 ponni_b200_status pb_ensure_cuda(ponni_b200_model* m);
 std::string pb_schema_fingerprint(const ponni_b200_model* m);
+ponni_b200_status pb_pull_params(ponni_b200_model* m);
+ponni_b200_status pb_update_params_from_host(ponni_b200_model* m, const void* host, int64_t n);
+void pb_free_param_map(ponni_b200_model* m);

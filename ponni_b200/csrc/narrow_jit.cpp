@@ -332,6 +332,10 @@ void to_compute(int dtype, const std::vector<unsigned char>& packed, int n, std:
 
 }  // namespace
 
+void narrow_jit_refresh(int dtype, const Program& p, const std::vector<unsigned char>& packed, NarrowJit* J) {
+  to_compute(dtype, packed, p.n_params, &J->params);
+}
+
 bool narrow_jit_build(int dtype, const Program& p, int maxw, const std::vector<unsigned char>& packed, int num_sms,
                       NarrowJit* J, std::string* why) {
   if ((size_t)std::max(p.n_params, 1) * compute_bytes(dtype) > kMaxParamBytes) {

@@ -39,6 +39,10 @@ std::string narrow_jit_source(int dtype, const Program& p, int maxw, int* cols);
 bool narrow_jit_build(int dtype, const Program& p, int maxw, const std::vector<unsigned char>& packed, int num_sms,
                       NarrowJit* J, std::string* why);
 
+// Re-derive the kernel's parameter block from new packed parameters (the
+// compiled kernel is kept).
+void narrow_jit_refresh(int dtype, const Program& p, const std::vector<unsigned char>& packed, NarrowJit* J);
+
 cudaError_t narrow_jit_launch(const NarrowJit& J, const void* in, int64_t in_ld, void* out, int64_t out_ld,
                               int64_t batch, cudaStream_t stream);
 

@@ -24,13 +24,14 @@ bool tc_activation(int k) {
 }
 
 // Place one element into a K-major SW128 operand with `rows` rows.
-void put_kmajor(std::vector<unsigned char>& img, size_t base, int rows, int n, int k, int esz, const void* val) {
+size_t put_kmajor(std::vector<unsigned char>& img, size_t base, int rows, int n, int k, int esz, const void* val) {
   const int kper = 128 / esz;
   const int kb = k / kper;
   const int wb = (k % kper) * esz;
   const int chunk = wb / 16;
   const size_t off = base + (size_t)kb * rows * 128 + (size_t)n * 128 + (size_t)((chunk ^ (n & 7)) * 16) + (wb % 16);
   memcpy(img.data() + off, val, esz);
+  return off;
 }
 
 uint32_t make_idesc(int dtype, int n_pad, bool a_mn_major) {
@@ -42,7 +43,8 @@ uint32_t make_idesc(int dtype, int n_pad, bool a_mn_major) {
 
 }  // namespace
 
-bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>& image, std::string& why) {
+bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>& image, std::string& why,
+             ParamMap* rec) {
   memset(&p, 0, sizeof(p));
   image.clear();
   const ponni_b200_dtype dt = m->dtype;
@@ -124,7 +126,10 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
     const Layer& mv = *blocks[l].mv;
     if (blocks[l].bias) {
       float* b = reinterpret_cast<float*>(image.data() + L.bias_off);
-      for (int f = 0; f < L.nout; ++f) b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
+      for (int f = 0; f < L.nout; ++f) {
+        b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
+        if (rec) rec->add(blocks[l].bias->params.data() + f * msz, PIMG_TC, PENC_F32, L.bias_off + 4 * (size_t)f);
+      }
     }
     for (int k = 0; k < L.nin; ++k) {
       for (int n = 0; n < L.nout; ++n) {
@@ -137,11 +142,17 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
           const float r = w - __bfloat162float(b0);
           const __nv_bfloat16 b1 = __float2bfloat16_rn(r);
           const __nv_bfloat16 b2 = __float2bfloat16_rn(r - __bfloat162float(b1));
-          put_kmajor(image, L.w_off[0], L.n_pad, n, k, 2, &b0);
-          put_kmajor(image, L.w_off[1], L.n_pad, n, k, 2, &b1);
-          put_kmajor(image, L.w_off[2], L.n_pad, n, k, 2, &b2);
+          const size_t o0 = put_kmajor(image, L.w_off[0], L.n_pad, n, k, 2, &b0);
+          const size_t o1 = put_kmajor(image, L.w_off[1], L.n_pad, n, k, 2, &b1);
+          const size_t o2 = put_kmajor(image, L.w_off[2], L.n_pad, n, k, 2, &b2);
+          if (rec) {
+            rec->add(src, PIMG_TC, PENC_SPLIT0, o0);
+            rec->add(src, PIMG_TC, PENC_SPLIT1, o1);
+            rec->add(src, PIMG_TC, PENC_SPLIT2, o2);
+          }
         } else {
-          put_kmajor(image, L.w_off[0], L.n_pad, n, k, 2, src);
+          const size_t o = put_kmajor(image, L.w_off[0], L.n_pad, n, k, 2, src);
+          if (rec) rec->add(src, PIMG_TC, PENC_MODEL, o);
         }
       }
     }
@@ -199,7 +210,8 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   return false;
 }
 
-bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>& image, std::string& why) {
+bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>& image, std::string& why,
+             ParamMap* rec) {
   memset(&p, 0, sizeof(p));
   image.clear();
   const ponni_b200_dtype dt = m->dtype;
@@ -265,12 +277,17 @@ bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>
     const Layer& mv = *blocks[l].mv;
     if (blocks[l].bias) {
       float* b = reinterpret_cast<float*>(image.data() + L.bias_off);
-      for (int f = 0; f < L.nout; ++f) b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
+      for (int f = 0; f < L.nout; ++f) {
+        b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
+        if (rec) rec->add(blocks[l].bias->params.data() + f * msz, PIMG_TS, PENC_F32, L.bias_off + 4 * (size_t)f);
+      }
     }
     for (int n = 0; n < L.nout; ++n)
       for (int k = 0; k < L.nin; ++k) {
         const size_t chunk = L.w_off + (size_t)(k / kTsBlockK) * kTsChunkBytes;
-        put_kmajor(image, chunk, L.n_pad, n, k % kTsBlockK, 2, mv.params.data() + ((size_t)k * L.nout + n) * msz);
+        const unsigned char* src = mv.params.data() + ((size_t)k * L.nout + n) * msz;
+        const size_t o = put_kmajor(image, chunk, L.n_pad, n, k % kTsBlockK, 2, src);
+        if (rec) rec->add(src, PIMG_TS, PENC_MODEL, o);
       }
   }
   p.stage_bytes = (uint32_t)(p.layers[0].k_pad / 8) * 2048;

@@ -10,6 +10,8 @@ namespace ponni_b200 {
 
 // Build the TcProgram and the staged parameter image for `m`; false (with
 // the reason in `why`) when the model is not a dense chain the kernel supports.
-bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>& image, std::string& why);
+// `rec` (optional) receives the image location of every trainable parameter.
+bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>& image, std::string& why,
+             ParamMap* rec = nullptr);
 
 }  // namespace ponni_b200

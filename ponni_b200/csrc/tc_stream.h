@@ -59,7 +59,10 @@ struct TsProgram {
 // Plan the streamed kernel for a Matvec[Bias][activation] chain of a 16-bit
 // model; builds the chunked, pre-swizzled weight image.  False with `why`
 // when not eligible.
-bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>& image, std::string& why);
+// `rec` (optional) receives the image location of every trainable parameter.
+struct ParamMap;
+bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>& image, std::string& why,
+             ParamMap* rec = nullptr);
 
 cudaError_t launch_ts_forward(const TsProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
                               int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream);

@@ -104,21 +104,37 @@ class GeneratedModel:
 
     # -- parameters (emitter.py:1724-1895) --
     @staticmethod
-    def _layer_list(dense):
+    def _layer_list(dense, rnd=lambda a: a):
         out = []
         for d in dense:
-            out.append(L.Matvec(d.weight.T))
+            out.append(L.Matvec(rnd(d.weight).T))
             if d.bias is not None:
-                out.append(L.Bias(d.bias))
+                out.append(L.Bias(rnd(d.bias)))
             if d.activation is not None:
                 out.append(_ACT[d.activation](d.weight.shape[0], d.alpha))
         return out
+
+    def _trainable_order(self) -> np.ndarray:
+        """Index of each trainable value (Inference tuple order: Matvec W[in][out],
+        then the bias) in the generated order (W[out, in], then the bias)."""
+        if getattr(self, "_perm", None) is None:
+            parts, g = [], 0
+            for d in self.dense:
+                o, i = d.weight.shape
+                parts.append(g + np.arange(o * i, dtype=np.int64).reshape(o, i).T.reshape(-1))
+                g += o * i
+                if d.bias is not None:
+                    parts.append(g + np.arange(o, dtype=np.int64))
+                    g += o
+            self._perm = np.concatenate(parts)
+        return self._perm
 
     def get_num_parameters(self) -> int:
         return int(sum(d.weight.size + (d.bias.size if d.bias is not None else 0) for d in self.dense))
 
     def get_parameters(self) -> np.ndarray:
         """Learned parameters in layer order: W[out, in] row-major, then the bias."""
+        self._pull_dense()
         parts = []
         for d in self.dense:
             parts.append(d.weight.reshape(-1))
@@ -132,6 +148,24 @@ class GeneratedModel:
             raise _abi.PonniError(2, "GeneratedModel::set_parameters source extent is incorrect")
         if not np.all(np.isfinite(v)):
             raise _abi.PonniError(2, "GeneratedModel::set_parameters received non-finite values")
+        self._set_dense(v)
+        # Planned models take the values into their device images (pinned
+        # staging + device scatter, no re-plan); the fp16 mirror follows.
+        self._dense_stale = False
+        self._push_host()
+
+    def _mirror_values(self, a):
+        """The fp16 mirror is fp16(float(Scalar value)) (emitter.py:1742-1743, 1779-1783):
+        round to Scalar and to float first, so that the final rounding to fp16
+        is the only one left."""
+        return np.asarray(a).astype(self.scalar).astype(np.float32).astype(np.float64)
+
+    def _push_host(self):
+        t = self.get_parameters().astype(np.float64)[self._trainable_order()]
+        for dt, m in self._models.items():
+            m.set_trainable_parameters(self._mirror_values(t) if dt == _abi.F16 else t)
+
+    def _set_dense(self, v):
         off = 0
         for d in self.dense:
             n = d.weight.size
@@ -140,7 +174,72 @@ class GeneratedModel:
             if d.bias is not None:
                 d.bias = v[off:off + d.bias.size].copy()
                 off += d.bias.size
-        self._models.clear()
+
+    def _scalar_dtype(self) -> int:
+        return _abi.F32 if self.scalar == np.float32 else _abi.F64
+
+    def _pull_dense(self):
+        """After a device update the scalar model holds the parameters."""
+        if getattr(self, "_dense_stale", False):
+            t = self._models[self._scalar_dtype()].get_trainable_parameters()
+            v = np.empty_like(t)
+            v[self._trainable_order()] = t
+            self._set_dense(v)
+            self._dense_stale = False
+
+    # -- device-resident parameters (emitter.py:1769-1895) --
+    def set_parameters_device(self, values) -> None:
+        """Learned parameters (generated order) from a CUDA tensor of fp32 or
+        fp64: converted to Scalar and scattered into the scalar model's device
+        images, then into the fp16 mirror (refresh_half_parameters), all on
+        the device and the current torch stream."""
+        import torch
+        if not (isinstance(values, torch.Tensor) and values.is_cuda):
+            raise _abi.PonniError(1, "set_parameters_device needs a CUDA tensor")
+        if values.numel() != self.get_num_parameters():
+            raise _abi.PonniError(2, "GeneratedModel::set_parameters source extent is incorrect")
+        if getattr(self, "_perm_dev", None) is None or self._perm_dev.device != values.device:
+            self._perm_dev = torch.from_numpy(self._trainable_order()).to(values.device)
+        t = values.reshape(-1).index_select(0, self._perm_dev)
+        self._model(self._scalar_dtype()).set_trainable_parameters_device(t)
+        self._dense_stale = True
+        self.refresh_half_parameters()
+
+    def get_parameters_device(self, dtype=None):
+        """Learned parameters (generated order) as a CUDA tensor."""
+        import torch
+        t = self._model(self._scalar_dtype()).get_trainable_parameters_device(dtype)
+        if getattr(self, "_perm_dev", None) is None or self._perm_dev.device != t.device:
+            self._perm_dev = torch.from_numpy(self._trainable_order()).to(t.device)
+        out = torch.empty_like(t)
+        out[self._perm_dev] = t
+        return out
+
+    def refresh_half_parameters(self) -> None:
+        """fp16 mirror <- fp16(float(parameters)), device to device."""
+        half = self._models.get(_abi.F16)
+        if half is None:
+            return
+        scalar = self._model(self._scalar_dtype())
+        half.set_trainable_parameters_device(scalar.get_trainable_parameters_device())
+
+    def parameters_are_finite(self) -> bool:
+        return self._model(self._scalar_dtype()).parameters_are_finite()
+
+    def parameters_synchronized(self) -> bool:
+        """Every device image agrees with the parameters, and the fp16 mirror
+        holds fp16(float(parameters)) (emitter.py:1882-1895)."""
+        import torch
+        scalar = self._model(self._scalar_dtype())
+        if not scalar.parameters_synchronized():
+            return False
+        half = self._models.get(_abi.F16)
+        if half is None:
+            return True
+        if not half.parameters_synchronized():
+            return False
+        return bool(torch.equal(half.get_trainable_parameters_device(torch.float16),
+                                scalar.get_trainable_parameters_device(torch.float16)))
 
     def load_weights(self, path: str) -> None:
         """Named tensors <name>.weight [out, in] and <name>.bias of a .ponni file."""
@@ -151,13 +250,16 @@ class GeneratedModel:
             d.weight = w
             if d.bias is not None:
                 d.bias = _read_tensor(path, f"{d.name}.bias").astype(np.float64).reshape(-1)
-        self._models.clear()
+        self._dense_stale = False
+        self._push_host()
 
     # -- inference --
     def _model(self, dtype: int) -> Inference:
         m = self._models.get(dtype)
         if m is None:
-            m = Inference(self._layer_list(self.dense), dtype=dtype, device=self.device,
+            self._pull_dense()
+            rnd = self._mirror_values if dtype == _abi.F16 else (lambda a: a)
+            m = Inference(self._layer_list(self.dense, rnd), dtype=dtype, device=self.device,
                           arithmetic=_abi.ARITH_GENERATED)
             self._models[dtype] = m
         return m

@@ -308,6 +308,55 @@ class Inference:
         _check(_abi.lib().ponni_b200_set_trainable_parameters(self._m, raw.ctypes.data, v.size), self._m)
         self._sync_layers(v)
 
+    # -- parameters in device memory (no re-plan) -----------------------------
+    def _torch_code(self, t) -> int:
+        import torch
+        codes = {torch.float32: _abi.F32, torch.float64: _abi.F64, torch.float16: _abi.F16,
+                 torch.bfloat16: _abi.BF16}
+        if t.dtype not in codes:
+            raise _abi.PonniError(1, f"parameter dtype {t.dtype} is not fp32, fp64, fp16 or bf16")
+        return codes[t.dtype]
+
+    def set_trainable_parameters_device(self, values) -> None:
+        """Trainable parameters (tuple order) from a CUDA tensor of fp32, fp64,
+        fp16 or bf16 on this model's device, converted to the model dtype and
+        written into the planned device images on the current torch stream
+        (generated set_parameters, emitter.py:1826-1866).  The Python layer
+        objects keep their earlier values; get_trainable_parameters() reads
+        the model."""
+        if not (hasattr(values, "is_cuda") and values.is_cuda):
+            raise _abi.PonniError(1, "set_trainable_parameters_device needs a CUDA tensor")
+        if values.device.index != self.device:
+            raise _abi.PonniError(1, f"parameters are on {values.device}, the model on cuda:{self.device}")
+        v = values.reshape(-1)
+        if not v.is_contiguous():
+            v = v.contiguous()
+        _check(_abi.lib().ponni_b200_set_trainable_parameters_device(
+            self._m, v.data_ptr(), self._torch_code(v), v.numel(), torch_stream_handle(self.device)), self._m)
+
+    def get_trainable_parameters_device(self, dtype=None):
+        """Trainable parameters (tuple order) as a CUDA tensor of `dtype`
+        (default: the model dtype), on the current torch stream."""
+        import torch
+        dt = self.torch_dtype() if dtype is None else dtype
+        out = torch.empty(self.get_num_trainable_parameters(), dtype=dt, device=f"cuda:{self.device}")
+        _check(_abi.lib().ponni_b200_get_trainable_parameters_device(
+            self._m, out.data_ptr(), self._torch_code(out), out.numel(), torch_stream_handle(self.device)), self._m)
+        return out
+
+    def check_parameters(self) -> tuple[int, int]:
+        """(device image locations that disagree with the parameters,
+        trainable values that are not finite)."""
+        mism, nonfinite = ctypes.c_int64(), ctypes.c_int64()
+        _check(_abi.lib().ponni_b200_check_parameters(self._m, ctypes.byref(mism), ctypes.byref(nonfinite)), self._m)
+        return int(mism.value), int(nonfinite.value)
+
+    def parameters_synchronized(self) -> bool:
+        return self.check_parameters()[0] == 0
+
+    def parameters_are_finite(self) -> bool:
+        return self.check_parameters()[1] == 0
+
     def weight_schema_fingerprint(self) -> str:
         buf = ctypes.create_string_buffer(64)
         _check(_abi.lib().ponni_b200_weight_schema_fingerprint(self._m, buf, len(buf)), self._m)

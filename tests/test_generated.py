@@ -87,6 +87,25 @@ def test_generated_parameters_round_trip():
         g.set_parameters(bad)
 
 
+def test_generated_trainable_order():
+    """Generated order (W[out, in], then bias) -> Inference tuple order
+    (Matvec W[in][out], then Bias): the permutation device updates use."""
+    rng = np.random.default_rng(4)
+    g = pb.GeneratedModel(dense_chain(rng))
+    perm = g._trainable_order()
+    want = np.concatenate([L.parameters().reshape(-1) for L in g._layer_list(g.dense)
+                           if L.get_num_trainable_parameters()])
+    assert np.array_equal(g.get_parameters().astype(np.float64)[perm], want.astype(np.float32).astype(np.float64))
+    assert np.array_equal(np.sort(perm), np.arange(g.get_num_parameters()))
+
+
+def test_generated_half_mirror_rounds_through_scalar():
+    """The fp16 mirror is fp16(float(Scalar value)) (emitter.py:1742-1743)."""
+    g = pb.GeneratedModel([pb.Dense("a", np.zeros((1, 1)))], np.float64)
+    v = np.array([1.0 + 2.0 ** -11 + 2.0 ** -40])  # a tie for fp16 only after rounding to float
+    assert g._mirror_values(v)[0] == np.float32(v[0])
+
+
 def test_generated_load_named_weights():
     """Named tensors of a .ponni file (the reference-generated pytorch_resnet
     fixture) load by name, shape-checked."""
