@@ -146,6 +146,42 @@ def run_reference(args, cfg, rank, metric, unit, dtype_name):
 L2_FLUSH_BYTES = 256 << 20
 
 
+def param_update_latency(model, reps=20):
+    """Wall-clock latency of one parameter update of the planned model
+    (synchronized, measured after the timed region): from device memory,
+    from host memory (pinned staging + device scatter), and through a full
+    re-plan (PONNI_B200_PARAM_SCATTER=0: re-pack and re-upload every image)."""
+    import numpy as np
+    import torch
+
+    n = model.get_num_trainable_parameters()
+    if n == 0:
+        return None
+    saved = model.get_trainable_parameters()
+    hv = np.random.default_rng(1).normal(0, 0.1, n)
+    dv = torch.from_numpy(hv).to(model.torch_dtype()).cuda(model.device)
+
+    def wall_us(fn, k):
+        fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(k):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / k * 1e6
+
+    out = {"params": n, "device_update_us": wall_us(lambda: model.set_trainable_parameters_device(dv), reps),
+           "host_update_us": wall_us(lambda: model.set_trainable_parameters(hv), reps)}
+    os.environ["PONNI_B200_PARAM_SCATTER"] = "0"
+    try:
+        out["replan_update_us"] = wall_us(lambda: (model.set_trainable_parameters(hv), model.kernel()), 3)
+    finally:
+        del os.environ["PONNI_B200_PARAM_SCATTER"]
+    model.set_trainable_parameters(saved)
+    out["timing"] = "wall clock per update incl. host work, synchronized, after the timed region"
+    return out
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -285,6 +321,8 @@ def main():
         v, cores, sample, _ = cpu_reference(cfg)
         cpu = {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": sample}
 
+    upd = param_update_latency(model) if rank == 0 else None
+
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -297,6 +335,7 @@ def main():
                        "l2": ("L2 flushed (256 MB write) before each step, outside the timed events" if flush
                               else "inputs larger than L2 (no flush)")},
             "kernel": kernel_name, "arithmetic": arith_name, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,
+            "param_update": upd,
         }), flush=True)
     if world > 1:
         dist.destroy_process_group()

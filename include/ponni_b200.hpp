@@ -315,6 +315,28 @@ class Inference {
     check(ponni_b200_get_trainable_parameters(model_.get(), out.data(), (int64_t)out.size()));
     return out;
   }
+  // Parameters in device memory (tuple order), written into the planned
+  // model's device images on `stream` without a re-plan (generated
+  // set_parameters / get_parameters, emitter.py:1787-1866).
+  template <class S>
+  void set_trainable_parameters_device(const S* d_src, int64_t count, void* stream = nullptr) {
+    check(ponni_b200_set_trainable_parameters_device(model_.get(), d_src, dtype_of<S>::value, count, stream));
+  }
+  template <class S>
+  void get_trainable_parameters_device(S* d_dst, int64_t count, void* stream = nullptr) const {
+    check(ponni_b200_get_trainable_parameters_device(model_.get(), d_dst, dtype_of<S>::value, count, stream));
+  }
+  // Device checks (emitter.py:1868-1895).
+  bool parameters_synchronized() const {
+    int64_t mism = 0;
+    check(ponni_b200_check_parameters(model_.get(), &mism, nullptr));
+    return mism == 0;
+  }
+  bool parameters_are_finite() const {
+    int64_t bad = 0;
+    check(ponni_b200_check_parameters(model_.get(), nullptr, &bad));
+    return bad == 0;
+  }
   std::string weight_schema_fingerprint() const {
     char buf[64];
     check(ponni_b200_weight_schema_fingerprint(model_.get(), buf, sizeof buf));

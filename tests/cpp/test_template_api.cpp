@@ -94,6 +94,14 @@ static void gpu_tests() {
   ponni::deep_copy(x, 1.0f);
   auto y = readme.forward_batch_parallel(x);
   REQUIRE(near(y(0, 0), 0.7f, 1e-6f) && near(y(0, 99999), 0.7f, 1e-6f), "README -> 0.7");
+  // parameter update of the planned model (device scatter, no re-plan)
+  auto p = readme.get_trainable_parameters();
+  REQUIRE(p.size() == 2 * 3 + 3 + 3 + 1, "trainable count");
+  p(p.size() - 1) = 0.8f;  // b2: -0.2 -> 0.8
+  readme.set_trainable_parameters(p);
+  y = readme.forward_batch_parallel(x);
+  REQUIRE(near(y(0, 0), 1.7f, 1e-6f) && near(y(0, 99999), 1.7f, 1e-6f), "updated bias -> 1.7");
+  REQUIRE(readme.parameters_synchronized() && readme.parameters_are_finite(), "device images in step");
   // double and half models
   ponni::View<double> wd("wd", 2, 2);
   ponni::deep_copy(wd, 1.0);
