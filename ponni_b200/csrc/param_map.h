@@ -88,6 +88,7 @@ struct ParamMapDev {
   void* pinned = nullptr;           // pinned host staging of host updates
   cudaEvent_t pinned_free = nullptr;  // recorded after the copy out of `pinned`
   cudaEvent_t done = nullptr;         // orders the model stream after updates on another stream
+  std::vector<uint32_t> packed_of_host;  // host copy of packed_of
   int64_t n_recs = 0;
   int64_t n_trainable = 0;
   size_t staging_bytes = 0;

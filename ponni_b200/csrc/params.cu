@@ -64,18 +64,27 @@ void images_of(const ponni_b200_model* m, void* img[PIMG_COUNT]) {
   img[PIMG_TS] = m->kernel == 5 ? m->ts_image_dev : nullptr;
 }
 
-// Copy the packed locations of `values` (model dtype, tuple order) into the
-// layers' canonical arrays.
+// Element copies between tuple order and packed positions (esz 2, 4 or 8).
+template <class W>
+void gather_packed(W* dst, const W* packed, const uint32_t* packed_of, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) dst[i] = packed[packed_of[i]];
+}
+template <class W>
+void scatter_packed(W* packed, const W* src, const uint32_t* packed_of, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) packed[packed_of[i]] = src[i];
+}
+
+// The layers' canonical arrays from the packed image (host copy).  Needs the
+// uploaded map.
 void unpack_to_layers(ponni_b200_model* m, const unsigned char* packed) {
-  const auto& R = m->pmap.ranges;
   const size_t esz = m->pmap.esz;
-  for (const ParamRec& r : m->pmap.recs) {
-    if (r.img != PIMG_PACKED) continue;
-    auto it = std::upper_bound(R.begin(), R.end(), (int64_t)r.src,
-                               [](int64_t v, const ParamMap::Range& x) { return v < x.base; });
-    const ParamMap::Range& rg = *(it - 1);
-    unsigned char* dst = const_cast<unsigned char*>(rg.begin) + (size_t)(r.src - rg.base) * esz;
-    memcpy(dst, packed + r.dst, esz);
+  const uint32_t* po = m->pmap_dev.packed_of_host.data();
+  for (const ParamMap::Range& r : m->pmap.ranges) {
+    unsigned char* dst = const_cast<unsigned char*>(r.begin);
+    const int64_t n = (int64_t)((r.end - r.begin) / (ptrdiff_t)esz);
+    if (esz == 8) gather_packed((uint64_t*)dst, (const uint64_t*)packed, po + r.base, n);
+    else if (esz == 4) gather_packed((uint32_t*)dst, (const uint32_t*)packed, po + r.base, n);
+    else gather_packed((uint16_t*)dst, (const uint16_t*)packed, po + r.base, n);
   }
 }
 
@@ -136,6 +145,7 @@ ponni_b200_status upload_map(ponni_b200_model* m) {
   }
   d.n_recs = (int64_t)recs.size();
   d.n_trainable = nt;
+  d.packed_of_host.swap(packed_of);
   m->pmap_uploaded = true;
   return PONNI_B200_OK;
 }
@@ -226,9 +236,11 @@ ponni_b200_status pb_update_params_from_host(ponni_b200_model* m, const void* ho
   if (e == cudaSuccess) e = launch_param_scatter(d, d.staging, dtype_code(m->dtype), dtype_code(m->dtype), img, m->stream);
   if (e != cudaSuccess) return cfail(m, e, "parameter scatter");
   // The host mirror of the packed image follows the same map.
-  const unsigned char* src = static_cast<const unsigned char*>(host);
-  for (const ParamRec& r : m->pmap.recs)
-    if (r.img == PIMG_PACKED) memcpy(m->packed_host.data() + r.dst, src + (size_t)r.src * esz, esz);
+  const uint32_t* po = d.packed_of_host.data();
+  unsigned char* ph = m->packed_host.data();
+  if (esz == 8) scatter_packed((uint64_t*)ph, (const uint64_t*)host, po, n);
+  else if (esz == 4) scatter_packed((uint32_t*)ph, (const uint32_t*)host, po, n);
+  else scatter_packed((uint16_t*)ph, (const uint16_t*)host, po, n);
   if (m->kernel == 4) narrow_jit_refresh((int)m->dtype, m->prog, m->packed_host, &m->jit);
   return PONNI_B200_OK;
 }
