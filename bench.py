@@ -313,6 +313,8 @@ def main():
         esz = x.element_size()
         e2e = {"value": world * B / e2e_s, "unit": unit, "h2d_bytes_per_step": world * nin * B * esz,
                "d2h_bytes_per_step": world * nout * B * esz,
+               "host_link_gbs": {"h2d": nin * B * esz / e2e_s / 1e9, "d2h": nout * B * esz / e2e_s / 1e9,
+                                 "note": "per GPU; the copies of one step overlap its kernel chunk by chunk"},
                "path": "ponni_b200_forward_host (C ABI), pinned host buffers, chunked copy/compute overlap"}
         del xh, yh
 
