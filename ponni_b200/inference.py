@@ -317,6 +317,11 @@ class Inference:
             raise _abi.PonniError(1, f"parameter dtype {t.dtype} is not fp32, fp64, fp16 or bf16")
         return codes[t.dtype]
 
+    def parameter_device(self):
+        """The torch device of this model's parameters."""
+        import torch
+        return torch.device(f"cuda:{self.device}")
+
     def set_trainable_parameters_device(self, values) -> None:
         """Trainable parameters (tuple order) from a CUDA tensor of fp32, fp64,
         fp16 or bf16 on this model's device, converted to the model dtype and

@@ -1,9 +1,10 @@
 """Column sharding of a batch across the ranks of one node (weak scaling).
 
 Samples (batch columns) are independent, so rank r of `world` owns the
-global columns [r * per_rank, (r + 1) * per_rank) and no data crosses ranks;
-the only collective is the reduction of each rank's timing to the job's
-(the slowest rank's) time, outside the timed region.
+global columns [r * per_rank, (r + 1) * per_rank) and no data crosses ranks
+on the forward path; the collectives are the reduction of each rank's timing
+to the job's (the slowest rank's) time, outside the timed region, and the
+broadcast of a parameter update to every rank's replica of the model.
 """
 from __future__ import annotations
 
@@ -26,3 +27,37 @@ def job_time(seconds: float, world: int, device=None) -> float:
     t = torch.tensor([float(seconds)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def broadcast_parameters(model, values=None, src: int = 0, world: int | None = None) -> None:
+    """Replace the trainable parameters of every rank's replica with `values`
+    from rank `src` (tuple order; a tensor on this rank's device, any of
+    fp32 / fp64 / fp16 / bf16; ignored on the other ranks).
+
+    One broadcast of the values in device memory (NCCL over NVLink on GPUs),
+    then each rank writes them into its own planned device images
+    (`set_trainable_parameters_device`: converted to the model dtype on the
+    device, no re-plan).  Collective: every rank calls it.
+    """
+    import torch
+    import torch.distributed as dist
+
+    if world is None:
+        world = dist.get_world_size() if dist.is_initialized() else 1
+    n = model.get_num_trainable_parameters()
+    if world > 1:
+        rank = dist.get_rank()
+        # Every rank needs the source dtype to size its receive buffer.
+        codes = [torch.float32, torch.float64, torch.float16, torch.bfloat16]
+        dev = values.device if (rank == src and values is not None) else model.parameter_device()
+        hdr = torch.zeros(1, dtype=torch.int64, device=dev)
+        if rank == src:
+            if values is None or values.numel() != n:
+                raise ValueError(f"rank {src} must pass {n} parameter values")
+            hdr[0] = codes.index(values.dtype)
+        dist.broadcast(hdr, src)
+        dtype = codes[int(hdr.item())]
+        buf = values.reshape(-1).contiguous() if rank == src else torch.empty(n, dtype=dtype, device=dev)
+        dist.broadcast(buf, src)
+        values = buf
+    model.set_trainable_parameters_device(values)

@@ -92,3 +92,36 @@ def test_embedded_golden_fixture(embedded):
     layers, x, expected = K.pytorch_resnet()
     y = run_embedded(embedded, layers, pb.F32, np.ascontiguousarray(x.astype(np.float32)))
     assert np.max(np.abs(y - expected)) <= 1e-5
+
+
+def device_params_ptr(m):
+    prog, params = ctypes.c_void_p(), ctypes.c_void_p()
+    maxw, nbuf = ctypes.c_int(), ctypes.c_int()
+    assert pb._abi.lib().ponni_b200_model_device_program(m._m, ctypes.byref(prog), ctypes.byref(params),
+                                                         ctypes.byref(maxw), ctypes.byref(nbuf)) == 0
+    return params.value
+
+
+def test_device_parameter_update_is_seen_by_application_kernels(embedded):
+    """The device view points at the packed parameters, which parameter
+    updates rewrite in place: the view's pointers stay valid and an
+    application kernel sees the new values."""
+    layers = configs.cfg2(batch=1).layers
+    rng = np.random.default_rng(21)
+    x_raw = rng.normal(0, 1, (30, 513)).astype(np.float32)
+    m = pb.Inference(layers, dtype=pb.F32)
+    x = to_torch(x_raw, pb.F32).cuda()
+    y = torch.empty((m.get_num_outputs(), x.shape[1]), dtype=x.dtype, device="cuda")
+    assert embedded(m._m, x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), x.shape[1]) == 0
+    v = rng.normal(0, 0.2, m.get_num_trainable_parameters())
+    before = device_params_ptr(m)
+    m.set_trainable_parameters_device(torch.from_numpy(v).cuda())
+    torch.cuda.synchronize()
+    assert device_params_ptr(m) == before
+    assert embedded(m._m, x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), x.shape[1]) == 0
+    fresh = pb.Inference(layers, dtype=pb.F32)
+    fresh.set_trainable_parameters(v)
+    y2 = torch.empty_like(y)
+    assert embedded(fresh._m, x.data_ptr(), x.stride(0), y2.data_ptr(), y2.stride(0), x.shape[1]) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int32), y2.view(torch.int32))

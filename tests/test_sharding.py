@@ -1,6 +1,7 @@
 """The multi-GPU path's host logic on CPU: two gloo ranks shard the batch by
 columns (no data exchange), compute their shards, and reduce their timings to
-the slowest rank's; the gathered shards equal the one-process result."""
+the slowest rank's; the gathered shards equal the one-process result.  A
+parameter update from rank 0 reaches every rank's replica."""
 from __future__ import annotations
 
 import os
@@ -80,3 +81,56 @@ def test_two_gloo_ranks_match_one_process(oracle_lib):
     y_full = oracle.forward(layers(), 0, keyed_inputs(0, world * PER_RANK), 1)
     assert np.array_equal(y_sharded, y_full)
     assert t == 1.5  # the slowest rank's time
+
+
+class _Replica:
+    """Stands in for a model on CPU ranks: records the device update."""
+
+    def __init__(self, n):
+        self.n, self.got = n, None
+
+    def get_num_trainable_parameters(self):
+        return self.n
+
+    def parameter_device(self):
+        import torch
+        return torch.device("cpu")
+
+    def set_trainable_parameters_device(self, values):
+        self.got = values.clone()
+
+
+def _bcast_rank(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    m = _Replica(11)
+    vals = torch.arange(11, dtype=torch.float64) * 0.5 if rank == 0 else None
+    sharding.broadcast_parameters(m, vals, src=0)
+    out.put((rank, m.got.dtype == torch.float64, m.got.tolist()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_parameter_broadcast_two_gloo_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bcast_rank, args=(r, world, port, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [out.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, is_f64, vals in got:
+        assert is_f64 and vals == [0.5 * i for i in range(11)], rank
+
+
+def test_parameter_broadcast_single_process():
+    m = _Replica(3)
+    import torch
+    sharding.broadcast_parameters(m, torch.ones(3), world=1)
+    assert m.got.tolist() == [1.0, 1.0, 1.0]
