@@ -33,6 +33,14 @@
  *                                     (.ponni Safetensors profile, src/utils/ponni_safetensors.h:175-407)
  *   ponni_b200_read_ponni_tensor   <- load_ponni_tensor<N> src/utils/ponni_safetensors.h:409-444
  *   ponni_b200_model_summary       <- Inference::print src/ponni_Inference.h:671-683
+ *   ponni_b200_set/_get_trainable_parameters_device, ponni_b200_check_parameters
+ *                                  <- generated GeneratedModel::set_parameters / get_parameters /
+ *                                     refresh_half_parameters / parameters_are_finite /
+ *                                     parameters_synchronized, src/generator/kokkos_nn/emitter.py:1769-1895
+ *   ponni_b200_model_set_arithmetic(PONNI_B200_ARITH_GENERATED)
+ *                                  <- the generated struct's infer_batch / infer_batch_half2 arithmetic,
+ *                                     emitter.py:704-708, 975-983
+ *   ponni_b200_model_device_program <- forward_batch_parallel_in_kernel src/ponni_Inference.h:392-408, 592-604
  */
 #ifndef PONNI_B200_H
 #define PONNI_B200_H
