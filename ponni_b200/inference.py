@@ -31,12 +31,20 @@ def dtype_code(dtype) -> int:
 
 
 def bf16_bits(f32: np.ndarray) -> np.ndarray:
-    """float32 -> bfloat16 bit patterns (uint16), round to nearest even."""
-    u = np.ascontiguousarray(f32, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    """float32 -> bfloat16 bit patterns (uint16), round to nearest even.
+    32-bit arithmetic: u + 0x7FFF + lsb cannot wrap below the NaN patterns,
+    which are replaced afterwards (quiet NaN, payload kept)."""
+    u = np.ascontiguousarray(f32, dtype=np.float32).view(np.uint32)
+    r = u >> 16
+    r &= 1
+    r += 0x7FFF
+    r += u
+    r >>= 16
+    out = r.astype(np.uint16)
     nan = (u & 0x7FFFFFFF) > 0x7F800000
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
-    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
-    return r
+    if nan.any():
+        out[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return out
 
 
 def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
