@@ -220,7 +220,8 @@ def main():
     kernel_name = {1: "tile_forward_kernel (SIMT)", 2: "tc_forward_kernel (tcgen05)",
                    3: "narrow_forward_kernel (streaming)",
                    4: "ponni_narrow_jit (streaming, model-specialised)",
-                   5: "ts_forward_kernel (tcgen05, streamed weights)"}[model.kernel()]
+                   5: "ts_forward_kernel (tcgen05, streamed weights)",
+                   6: "tr_forward_kernel (tcgen05, LayerNorm/residual epilogue)"}[model.kernel()]
     tdt = model.torch_dtype()
     x = torch.empty((nin, B), dtype=tdt, device=dev)
     y = torch.empty((nout, B), dtype=tdt, device=dev)

@@ -29,7 +29,7 @@ F32, F64, F16, BF16 = 0, 1, 2, 3
  BINOP_CONCATENATE, BINOP_PROJECTION_ADD) = range(22)
 
 ARITH_AUTO, ARITH_REFERENCE, ARITH_TENSOR, ARITH_GENERATED = 0, 1, 2, 3
-KERNEL_TILE, KERNEL_TENSOR, KERNEL_NARROW, KERNEL_NARROW_JIT, KERNEL_TENSOR_STREAM = 1, 2, 3, 4, 5
+KERNEL_TILE, KERNEL_TENSOR, KERNEL_NARROW, KERNEL_NARROW_JIT, KERNEL_TENSOR_STREAM, KERNEL_TENSOR_RESID = 1, 2, 3, 4, 5, 6
 
 FLAG_TRAINABLE = 0x1
 FLAG_APPROXIMATE = 0x2

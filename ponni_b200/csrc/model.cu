@@ -552,6 +552,7 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
     // streamed-weights kernel even when their weights fit shared memory.
     const char* force_stream = getenv("PONNI_B200_TC_STREAM");
     const bool stream_first = force_stream && force_stream[0] == '1' && m->dtype != PONNI_B200_F32;
+    std::string why_tr;
     ParamMap tc_rec;
     tc_rec.ranges = m->pmap.ranges;
     tc_rec.esz = esz;
@@ -577,6 +578,43 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       if (e != cudaSuccess) return cuda_fail(m, e, "tensor-core parameter upload");
       m->tc_grid = m->num_sms;  // one persistent CTA (up to four tile slots) per SM
       m->kernel = 2;
+      m->pmap.recs.insert(m->pmap.recs.end(), tc_rec.recs.begin(), tc_rec.recs.end());
+      m->pmap.overflow |= tc_rec.overflow;
+    } else if (m->dtype == PONNI_B200_F32 && !(getenv("PONNI_B200_TC_RESID") && getenv("PONNI_B200_TC_RESID")[0] == '0') &&
+               (tc_rec.recs.clear(), tr_plan(m, m->trp, image, why_tr, &tc_rec))) {
+      // LayerNorm / residual chains (and fp32 chains too wide for the
+      // resident kernel): weights streamed, barriers in the epilogue.
+      if (image.size() > m->ts_image_bytes) {
+        if (m->ts_image_dev) cudaFree(m->ts_image_dev);
+        m->ts_image_dev = nullptr;
+        m->ts_image_bytes = 0;
+        e = cudaMalloc(&m->ts_image_dev, image.size());
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(streamed tensor-core parameters)");
+        m->ts_image_bytes = image.size();
+      }
+      const size_t scratch = (size_t)m->num_sms * m->trp.scratch_per_cta;
+      if (scratch > m->scratch_bytes) {
+        if (m->scratch_dev) cudaFree(m->scratch_dev);
+        m->scratch_dev = nullptr;
+        m->scratch_bytes = 0;
+        e = cudaMalloc(&m->scratch_dev, scratch);
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(saved-state scratch)");
+        m->scratch_bytes = scratch;
+      }
+      if (!m->err_dev) {
+        e = cudaMalloc(&m->err_dev, 64);
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMalloc(error word)");
+        e = cudaMemsetAsync(m->err_dev, 0, 64, m->stream);
+        if (e != cudaSuccess) return cuda_fail(m, e, "cudaMemset(error word)");
+      }
+      e = cudaMemcpyAsync(m->ts_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+      if (e != cudaSuccess) return cuda_fail(m, e, "residual tensor-core parameter upload");
+      m->tc_grid = m->num_sms;
+      // PONNI_B200_TC_GRID=n caps the persistent grid (a test aid: several
+      // tiles per CTA, both tile slots busy, on a small batch).
+      if (const char* g = getenv("PONNI_B200_TC_GRID")) m->tc_grid = std::max(1, std::min(m->num_sms, atoi(g)));
+      m->kernel = 6;
       m->pmap.recs.insert(m->pmap.recs.end(), tc_rec.recs.begin(), tc_rec.recs.end());
       m->pmap.overflow |= tc_rec.overflow;
     } else if (m->arithmetic == PONNI_B200_ARITH_TENSOR) {
@@ -749,13 +787,14 @@ ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, i
 void ponni_b200_model_destroy(ponni_b200_model* m) {
   if (!m) return;
   if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev || m->prog_dev ||
-      m->ts_image_dev || m->pmap_dev.recs || m->pmap_dev.staging) {
+      m->ts_image_dev || m->scratch_dev || m->pmap_dev.recs || m->pmap_dev.staging) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
     if (m->packed_dev) cudaFree(m->packed_dev);
     if (m->prog_dev) cudaFree(m->prog_dev);
     if (m->ts_image_dev) cudaFree(m->ts_image_dev);
+    if (m->scratch_dev) cudaFree(m->scratch_dev);
     if (m->stage_dev) cudaFree(m->stage_dev);
     if (m->tc_image_dev) cudaFree(m->tc_image_dev);
     if (m->err_dev) cudaFree(m->err_dev);
@@ -838,6 +877,11 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
     e = launch_ts_forward(m->tsp, m->ts_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
+  } else if (m->kernel == 6) {
+    const int64_t ntiles = (batch + kTcM - 1) / kTcM;
+    const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
+    e = launch_tr_forward(m->trp, m->ts_image_dev, m->scratch_dev, input, in_ld, output, out_ld, batch, grid,
+                          m->err_dev, s);
   } else if (m->kernel == 4) {
     e = narrow_jit_launch(m->jit, input, in_ld, output, out_ld, batch, s);
   } else if (m->kernel == 3) {
@@ -939,10 +983,7 @@ ponni_b200_status ponni_b200_model_diagnostics(ponni_b200_model* m, uint64_t* ou
   return PONNI_B200_OK;
 }
 
-int64_t ponni_b200_scratch_bytes(const ponni_b200_model* m) {
-  (void)m;
-  return 0;
-}
+int64_t ponni_b200_scratch_bytes(const ponni_b200_model* m) { return m ? (int64_t)m->scratch_bytes : 0; }
 
 // Tuple-order flattening of set/get_trainable_parameters
 // (src/ponni_Inference.h:689-716): each trainable layer consumes the prefix of

@@ -11,6 +11,7 @@
 #include "narrow_kernel.h"
 #include "param_map.h"
 #include "tc_program.h"
+#include "tc_resid.h"
 #include "tc_stream.h"
 
 namespace ponni_b200 {
@@ -58,7 +59,8 @@ struct ponni_b200_model {
   // Tensor-core dense-chain kernel (planned when eligible and allowed).
   int arithmetic = PONNI_B200_ARITH_AUTO;  // ponni_b200_arithmetic requested
   int kernel = 0;       // 1 tile (SIMT), 2 tensor-core, 3 narrow streaming kernel, 4 its model-specialised
-                        // (NVRTC-compiled) form, 5 tensor-core kernel with streamed weights;
+                        // (NVRTC-compiled) form, 5 tensor-core kernel with streamed weights,
+                        // 6 tensor-core kernel for LayerNorm / residual chains (fp32 split);
                         // 0 = not planned yet
   int narrow_maxw = 0;
   ponni_b200::NarrowLaunch narrow;     // narrow kernel launch configuration
@@ -71,7 +73,10 @@ struct ponni_b200_model {
   int tc_grid = 0;
   ponni_b200::TsProgram tsp;            // streamed-weights tensor-core kernel (kernel 5)
   void* ts_image_dev = nullptr;
-  size_t ts_image_bytes = 0;
+  size_t ts_image_bytes = 0;             // (also the image of kernel 6)
+  ponni_b200::TrProgram trp;            // LayerNorm / residual tensor-core kernel (kernel 6)
+  void* scratch_dev = nullptr;          // its saved-state scratch (num_sms x scratch_per_cta)
+  size_t scratch_bytes = 0;
   int* err_dev = nullptr;  // device error word (bounded waits that gave up)
   std::string tc_why;      // why the tensor-core kernel is not used
 

@@ -61,7 +61,7 @@ bool valid_dtype(int t) {
 void images_of(const ponni_b200_model* m, void* img[PIMG_COUNT]) {
   img[PIMG_PACKED] = m->packed_dev;
   img[PIMG_TC] = m->kernel == 2 ? m->tc_image_dev : nullptr;
-  img[PIMG_TS] = m->kernel == 5 ? m->ts_image_dev : nullptr;
+  img[PIMG_TS] = (m->kernel == 5 || m->kernel == 6) ? m->ts_image_dev : nullptr;
 }
 
 // Element copies between tuple order and packed positions (esz 2, 4 or 8).

@@ -11,6 +11,7 @@
 
 #include "model.h"
 #include "tc_plan.h"
+#include "tc_resid.h"
 #include "tc_stream.h"
 
 namespace ponni_b200 {
@@ -300,6 +301,203 @@ bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>
   }
   p.ring_stages = std::min<uint32_t>(kTsMaxStages, (budget - fixed) / kTsChunkBytes);
   p.smem_bytes = fixed + p.ring_stages * kTsChunkBytes;
+  return true;
+}
+
+// Residual / LayerNorm chains (tc_resid.cu): one job per Matvec, every
+// layer up to the next Matvec lowered to the job's epilogue operations.
+bool tr_plan(const ponni_b200_model* m, TrProgram& p, std::vector<unsigned char>& image, std::string& why,
+             ParamMap* rec) {
+  memset(&p, 0, sizeof(p));
+  image.clear();
+  const ponni_b200_dtype dt = m->dtype;
+  if (dt != PONNI_B200_F32) {
+    why = "the residual tensor-core path supports fp32 models (bf16 3-way split)";
+    return false;
+  }
+  const size_t msz = dtype_bytes(dt);
+  const auto& Ls = m->layers;
+  if (Ls.empty() || Ls[0].d.kind != PONNI_B200_MATVEC) {
+    why = "the chain must start with a Matvec";
+    return false;
+  }
+  int save_slot_of[64];
+  for (int& v : save_slot_of) v = -1;
+  std::vector<std::pair<int, const Layer*>> vec_ops;  // (op index, layer) of BIAS and LN operations
+  int nl = 0, nops = 0;
+  for (size_t i = 0; i < Ls.size();) {
+    const auto& d = Ls[i].d;
+    if (d.kind != PONNI_B200_MATVEC) {
+      why = std::string("layer ") + layer_label(d.kind) + " cannot start a dense job";
+      return false;
+    }
+    if (nl == kTrMaxLayers) {
+      why = "too many Matvec layers";
+      return false;
+    }
+    if (d.num_inputs > kTrMaxN || d.num_outputs > kTrMaxN) {
+      why = "layer wider than 128";
+      return false;
+    }
+    TrLayer& L = p.layers[nl];
+    L.nin = d.num_inputs;
+    L.nout = d.num_outputs;
+    L.k_pad = (int)round_up(L.nin, 16);
+    L.n_pad = (int)round_up(L.nout, 16);
+    L.kblk = (L.k_pad + 63) / 64;
+    L.nsteps = L.k_pad / 16;
+    L.op_first = nops;
+    L.ln = -1;
+    L.idesc = make_idesc(dt, L.n_pad, false);
+    // Accumulators: main groups of the dominant products plus one correction
+    // accumulator, within the slot's 256 TMEM columns.
+    int gs = std::min(4, L.nsteps);
+    while ((int64_t)((L.nsteps + gs - 1) / gs + 1) * L.n_pad > (int64_t)kTrSlotTmem) ++gs;
+    L.group_steps = gs;
+    L.groups = (L.nsteps + gs - 1) / gs + 1;
+    ++i;
+    for (; i < Ls.size() && Ls[i].d.kind != PONNI_B200_MATVEC; ++i) {
+      const auto& e = Ls[i].d;
+      if (nops == kTrMaxOps) {
+        why = "too many epilogue layers";
+        return false;
+      }
+      if (e.num_inputs != L.nout && e.kind != PONNI_B200_BIAS) {
+        why = std::string("layer ") + layer_label(e.kind) + " changes the width inside an epilogue";
+        return false;
+      }
+      TrOp& o = p.ops[nops];
+      o.flags = e.flags;
+      o.s0 = (float)e.scalar[0];
+      o.s1 = (float)e.scalar[1];
+      if (e.kind == PONNI_B200_BIAS) {
+        if (e.num_outputs != L.nout) {
+          why = "Bias width differs from the Matvec output";
+          return false;
+        }
+        o.kind = TR_BIAS;
+        vec_ops.push_back({nops, &Ls[i]});
+      } else if (e.kind >= PONNI_B200_RELU && e.kind <= PONNI_B200_MISH) {
+        o.kind = TR_ACT;
+        o.arg = e.kind;
+      } else if (e.kind == PONNI_B200_SAVE_STATE || e.kind == PONNI_B200_BINOP_ADD) {
+        if (e.save_index < 0 || e.save_index >= 64) {
+          why = "saved-state index out of range";
+          return false;
+        }
+        int& slot = save_slot_of[e.save_index];
+        if (e.kind == PONNI_B200_SAVE_STATE && slot < 0) {
+          if (p.n_saved == kTrMaxSaved) {
+            why = "more than two saved states";
+            return false;
+          }
+          slot = p.n_saved++;
+        }
+        if (slot < 0) {
+          why = "Binop_Add of a state that was not saved";
+          return false;
+        }
+        o.kind = e.kind == PONNI_B200_SAVE_STATE ? TR_SAVE : TR_ADD;
+        o.arg = slot;
+      } else if (e.kind == PONNI_B200_LAYER_NORM) {
+        if (L.ln >= 0) {
+          why = "two LayerNorms between Matvecs";
+          return false;
+        }
+        if (L.n_pad % 32 != 0) {
+          // The row is parked in the layer's first accumulator (32-column chunks).
+          why = "LayerNorm width not a multiple of 32 after a Matvec";
+          return false;
+        }
+        o.kind = TR_LN;
+        L.ln = nops - L.op_first;
+        vec_ops.push_back({nops, &Ls[i]});
+      } else {
+        why = std::string("layer ") + layer_label(e.kind) + " is not supported by the residual tensor-core path";
+        return false;
+      }
+      ++nops;
+    }
+    L.n_ops = nops - L.op_first;
+    ++nl;
+  }
+  for (int l = 0; l + 1 < nl; ++l)
+    if (p.layers[l].nout != p.layers[l + 1].nin) {
+      why = "Matvec widths do not chain";
+      return false;
+    }
+  p.n_layers = nl;
+  p.dtype = (int)dt;
+  p.nparts = 3;
+  p.nin = p.layers[0].nin;
+  p.nout = p.layers[nl - 1].nout;
+  // Image: per layer, per K block, the three weight parts as chunks of
+  // n_pad rows x 128 B (SW128 K-major), in the order the MMAs consume them
+  // (part 2, part 1, part 0); then the float vectors (bias[128] or
+  // gamma[128] beta[128]).
+  uint64_t off = 0;
+  for (int l = 0; l < nl; ++l) {
+    p.layers[l].w_off = off;
+    off += (uint64_t)p.layers[l].kblk * 3 * (uint64_t)p.layers[l].n_pad * 128;
+  }
+  for (auto& v : vec_ops) {
+    p.ops[v.first].off = (uint32_t)off;
+    off += p.ops[v.first].kind == TR_LN ? 1024 : 512;
+  }
+  p.image_bytes = (uint64_t)round_up((int64_t)off, 1024);
+  image.assign(p.image_bytes, 0);
+  for (int l = 0; l < nl; ++l) {
+    const TrLayer& L = p.layers[l];
+    // The l-th Matvec of the tuple.
+    const Layer* mv = nullptr;
+    for (int i = 0, c = 0; i < (int)Ls.size(); ++i)
+      if (Ls[i].d.kind == PONNI_B200_MATVEC && c++ == l) {
+        mv = &Ls[i];
+        break;
+      }
+    const size_t chunk = (size_t)L.n_pad * 128;
+    for (int k = 0; k < L.nin; ++k)
+      for (int n = 0; n < L.nout; ++n) {
+        const unsigned char* src = mv->params.data() + ((size_t)k * L.nout + n) * msz;  // W[k][n]
+        float w;
+        memcpy(&w, src, 4);
+        const __nv_bfloat16 b0 = __float2bfloat16_rn(w);
+        const float r = w - __bfloat162float(b0);
+        const __nv_bfloat16 b1 = __float2bfloat16_rn(r);
+        const __nv_bfloat16 b2 = __float2bfloat16_rn(r - __bfloat162float(b1));
+        const size_t kb_base = L.w_off + (size_t)(k / 64) * 3 * chunk;
+        const size_t o2 = put_kmajor(image, kb_base + 0 * chunk, L.n_pad, n, k % 64, 2, &b2);
+        const size_t o1 = put_kmajor(image, kb_base + 1 * chunk, L.n_pad, n, k % 64, 2, &b1);
+        const size_t o0 = put_kmajor(image, kb_base + 2 * chunk, L.n_pad, n, k % 64, 2, &b0);
+        if (rec) {
+          rec->add(src, PIMG_TS, PENC_SPLIT0, o0);
+          rec->add(src, PIMG_TS, PENC_SPLIT1, o1);
+          rec->add(src, PIMG_TS, PENC_SPLIT2, o2);
+        }
+      }
+  }
+  for (auto& v : vec_ops) {
+    const TrOp& o = p.ops[v.first];
+    const Layer& L = *v.second;
+    float* f = reinterpret_cast<float*>(image.data() + o.off);
+    const int n = L.d.num_outputs;
+    const int nvec = o.kind == TR_LN ? 2 : 1;  // LayerNorm: gamma then beta
+    for (int q = 0; q < nvec; ++q)
+      for (int i = 0; i < n; ++i) {
+        const unsigned char* src = L.params.data() + ((size_t)q * n + i) * msz;
+        f[q * 128 + i] = (float)load_scalar(dt, src);
+        if (rec) rec->add(src, PIMG_TS, PENC_F32, o.off + 4 * ((size_t)q * 128 + i));
+      }
+  }
+  p.scratch_per_cta = (uint64_t)kTrSlots * (uint64_t)p.n_saved * kTrMaxN * 128 * 4;
+  // Shared memory: per slot three operand parts of 2 K blocks, the weight
+  // ring, the LayerNorm exchange and the mbarriers.  The dynamic shared
+  // memory base is 1024-byte aligned (checked by the kernel), so no slack.
+  p.smem_bytes = kTrSlots * 3 * kTrPartBytes + kTrStages * kTrChunkBytes + kTrSlots * 2 * 128 * 4 + 128;
+  if (p.smem_bytes > 227 * 1024) {
+    why = "operand tiles exceed shared memory";
+    return false;
+  }
   return true;
 }
 

@@ -1,0 +1,511 @@
+// Tensor-core kernel for fp32 dense chains with LayerNorm and residual
+// barriers (sm_100a, tcgen05 + TMEM), weights streamed from L2.
+//
+// One persistent CTA per SM, warp-specialised (576 threads):
+//   producer (warp 16, one thread): streams the weight chunks of every job in
+//     job order into a two-stage shared-memory ring with 1-D bulk copies
+//     (cp.async.bulk, byte-counted mbarriers, no multicast).  A chunk is one
+//     bf16 part of one K block of 64 of a layer's weights, N rows x 128 B,
+//     pre-swizzled (SW128 K-major) on the host;
+//   MMA issuer (warp 17, one thread): per job (one Matvec of one tile of 128
+//     batch columns) issues the six split products chunk by chunk
+//     (tcgen05.mma kind::f16, bf16 operands, fp32 accumulators in the slot's
+//     256 TMEM columns): x0*w0 into the main accumulator, the five smaller
+//     products into a correction accumulator (the tensor core's fp32
+//     accumulation truncates; keeping the small products apart keeps the
+//     result fp32-accurate);
+//   epilogue (warps 0-15: two groups of 8, one per tile slot, each 4 TMEM
+//     lane quarters x 2 column halves; thread = one batch column = one row of
+//     the tile): sums the accumulators and runs the job's epilogue
+//     operations in tuple order (reference src/ponni_Inference.h:416-555):
+//       Bias                    v += b                (ponni_Bias.h:66-68)
+//       activations             v = f(v)              (activation.cuh)
+//       Binop_Add<I>            v += saved[I]         (ponni_Binop_Add.h:58-68)
+//       Save_State<I>           saved[I] = v          (ponni_Save_State.h:58-67)
+//       LayerNorm               two-pass mean / biased variance,
+//                               gamma * (v - mean) / sqrt(var + eps) + beta
+//                               (ponni_LayerNorm.h:77-99)
+//     then splits the result into the three bf16 parts of the next job's A
+//     operand (shared memory, K-major SW128) or writes the caller's output.
+//     LayerNorm parks the row's values in the (already read) main
+//     accumulator columns and exchanges the two column halves' partial sums
+//     through shared memory.  Saved states live in a per-CTA, per-slot
+//     global scratch area (64 KB per slot and state; L2-resident), written
+//     and read back by the same thread.
+// Two tiles are in flight and their jobs alternate Matvec by Matvec, so one
+// tile's epilogue overlaps the other's MMAs.
+//
+// Arithmetic: fp32 model values; each operand x = x0 + x1 + x2 exactly
+// (bf16 truncation parts); products of order <= 2 are kept (the dropped ones
+// are below 2^-24 relative).  Epilogue arithmetic is IEEE fp32 without
+// contraction where the reference rounds each operation (LayerNorm).
+//
+// Every wait is bounded: a role that gives up raises the CTA's abort flag,
+// records an error code and the CTA drains its copies and MMAs before it
+// frees TMEM; the epilogue warps of a slot decide to leave together (a
+// barrier reduction), so none is left waiting at a named barrier.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "device_math.cuh"
+#include "tc_common.cuh"
+#include "tc_resid.h"
+
+namespace ponni_b200 {
+namespace {
+using namespace tc;
+
+constexpr long long kWaitCycles = 1ll << 31;
+
+// 32 fp32 values into 32 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+// Named barrier over one slot's epilogue warps (ids 1, 2; 0 is __syncthreads).
+__device__ __forceinline__ void slot_sync(int s) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(s + 1), "r"(kTrGroupThreads) : "memory");
+}
+__device__ __forceinline__ int slot_sync_or(int s, int pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %2, 0;\n\t"
+      "bar.red.or.pred q, %1, %3, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(s + 1), "r"(pred), "r"(kTrGroupThreads)
+      : "memory");
+  return r;
+}
+
+template <int K>
+__device__ __forceinline__ void act32(float (&v)[32], int flags, float s0, float s1) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = activation<float>(K, flags, v[j], s0, s1);
+}
+
+__device__ __forceinline__ void act_dispatch(int kind, float (&v)[32], int flags, float s0, float s1) {
+  switch (kind) {
+    case EPI_RELU: act32<EPI_RELU>(v, flags, s0, s1); break;
+    case EPI_LEAKY_RELU: act32<EPI_LEAKY_RELU>(v, flags, s0, s1); break;
+    case EPI_ELU: act32<EPI_ELU>(v, flags, s0, s1); break;
+    case EPI_SELU: act32<EPI_SELU>(v, flags, s0, s1); break;
+    case EPI_GELU: act32<EPI_GELU>(v, flags, s0, s1); break;
+    case EPI_SILU: act32<EPI_SILU>(v, flags, s0, s1); break;
+    case EPI_SIGMOID: act32<EPI_SIGMOID>(v, flags, s0, s1); break;
+    case EPI_TANH: act32<EPI_TANH>(v, flags, s0, s1); break;
+    case EPI_SOFTPLUS: act32<EPI_SOFTPLUS>(v, flags, s0, s1); break;
+    case EPI_HARD_SIGMOID: act32<EPI_HARD_SIGMOID>(v, flags, s0, s1); break;
+    case EPI_HARD_SWISH: act32<EPI_HARD_SWISH>(v, flags, s0, s1); break;
+    case EPI_MISH: act32<EPI_MISH>(v, flags, s0, s1); break;
+    default: break;
+  }
+}
+
+// Per-thread context of the epilogue.
+struct TrEpi {
+  const unsigned char* image;
+  float4* saved;      // this CTA's and slot's saved states: [state][f / 4][128 rows] float4
+  uint32_t a[3];      // the slot's A operand parts
+  uint32_t tmem_row;  // slot accumulator base + this warp's lane quarter
+  float* xch;         // the slot's LayerNorm exchange [2 halves][128 rows]
+  int s, h, m;        // slot, column half, row
+};
+
+// Element-wise operations [o0, o1) on the 32 columns c0.. of this row.
+__device__ __forceinline__ void tr_ops(const TrOp* ops, int o0, int o1, float (&v)[32], int c0, const TrEpi& E) {
+  for (int i = o0; i < o1; ++i) {
+    const TrOp o = ops[i];
+    if (o.kind == TR_BIAS) {
+      const float4* b4 = reinterpret_cast<const float4*>(E.image + o.off) + c0 / 4;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 b = __ldg(b4 + q);
+        v[4 * q] = __fadd_rn(v[4 * q], b.x);
+        v[4 * q + 1] = __fadd_rn(v[4 * q + 1], b.y);
+        v[4 * q + 2] = __fadd_rn(v[4 * q + 2], b.z);
+        v[4 * q + 3] = __fadd_rn(v[4 * q + 3], b.w);
+      }
+    } else if (o.kind == TR_ACT) {
+      act_dispatch(o.arg, v, o.flags, o.s0, o.s1);
+    } else if (o.kind == TR_ADD) {
+      const float4* sv = E.saved + (size_t)o.arg * (kTrMaxN / 4) * 128 + (c0 / 4) * 128 + E.m;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 t = sv[q * 128];
+        v[4 * q] = __fadd_rn(v[4 * q], t.x);
+        v[4 * q + 1] = __fadd_rn(v[4 * q + 1], t.y);
+        v[4 * q + 2] = __fadd_rn(v[4 * q + 2], t.z);
+        v[4 * q + 3] = __fadd_rn(v[4 * q + 3], t.w);
+      }
+    } else if (o.kind == TR_SAVE) {
+      float4* sv = E.saved + (size_t)o.arg * (kTrMaxN / 4) * 128 + (c0 / 4) * 128 + E.m;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) sv[q * 128] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  }
+}
+
+// The row's 32 values c0.. go to the next job's A operand (split into three
+// bf16 parts) or, after the last Matvec, to the caller's output.
+__device__ __forceinline__ void tr_finish(const float (&v)[32], int c0, bool last, int nout, const TrEpi& E,
+                                          float* __restrict__ out, int64_t out_ld, int64_t col, int64_t batch) {
+  if (last) {
+    if (col < batch) {
+      const int nv = min(32, nout - c0);
+      float* o = out + (int64_t)c0 * out_ld + col;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j >= nv) break;
+        o[(int64_t)j * out_ld] = v[j];
+      }
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) store_row8<float>(E.a, E.m, c0 + 8 * q, v + 8 * q);
+  }
+}
+
+// Epilogue of job (layer l) for this thread's row and column half.
+__device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrEpi& E, float* __restrict__ out, int64_t out_ld,
+                            int64_t col, int64_t batch) {
+  const TrLayer& L = p.layers[l];
+  const int n_pad = L.n_pad, nout = L.nout, groups = L.groups;
+  const bool last = l == p.n_layers - 1;
+  const int o0 = L.op_first, o_end = o0 + L.n_ops;
+  const bool has_ln = L.ln >= 0;
+  const int o_ln = has_ln ? o0 + L.ln : o_end;
+  const int cb = E.h * kTrHalfCols, ce = min(cb + kTrHalfCols, n_pad);
+  const uint32_t corr = E.tmem_row + (uint32_t)((groups - 1) * n_pad);
+  float psum = 0.f;
+#pragma unroll 1
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    float v[32], w[32];
+    tmem_ld32x2(corr + (uint32_t)c0, E.tmem_row + (uint32_t)c0, v, w);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += w[j];
+#pragma unroll 1
+    for (int g = 1; g + 1 < groups; ++g) {
+      tmem_ld32(E.tmem_row + (uint32_t)(g * n_pad + c0), w);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += w[j];
+    }
+    tr_ops(p.ops, o0, o_ln, v, c0, E);
+    if (has_ln) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < nout) psum = __fadd_rn(psum, v[j]);
+      tmem_st32(E.tmem_row + (uint32_t)c0, v);  // park the row in the read main accumulator
+    } else {
+      tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
+    }
+  }
+  if (!has_ln) return;
+  // LayerNorm over the row (src/layers/ponni_LayerNorm.h:77-99): the two
+  // column halves exchange partial sums.
+  const TrOp ln = p.ops[o_ln];
+  const float n = (float)nout;
+  tmem_wait_st();
+  E.xch[E.h * 128 + E.m] = psum;
+  slot_sync(E.s);
+  const float mean = __fdiv_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), n);
+  slot_sync(E.s);
+  float pvar = 0.f;
+#pragma unroll 1
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    float v[32];
+    tmem_ld32(E.tmem_row + (uint32_t)c0, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (c0 + j < nout) {
+        const float d = __fsub_rn(v[j], mean);
+        pvar = __fadd_rn(pvar, __fmul_rn(d, d));
+      }
+  }
+  E.xch[E.h * 128 + E.m] = pvar;
+  slot_sync(E.s);
+  const float var = __fdiv_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), n);
+  const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, ln.s0)));
+  const float4* g4 = reinterpret_cast<const float4*>(E.image + ln.off);
+  const float4* b4 = g4 + 32;
+#pragma unroll 1
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    float v[32];
+    tmem_ld32(E.tmem_row + (uint32_t)c0, v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 g = __ldg(g4 + c0 / 4 + q), b = __ldg(b4 + c0 / 4 + q);
+      const float gg[4] = {g.x, g.y, g.z, g.w}, bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float xhat = __fmul_rn(__fsub_rn(v[4 * q + e], mean), inv_std);
+        v[4 * q + e] = __fadd_rn(__fmul_rn(gg[e], xhat), bb[e]);
+      }
+    }
+    tr_ops(p.ops, o_ln + 1, o_end, v, c0, E);
+    tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
+  }
+}
+
+// Stage this row's input column as layer 0's A operand (three bf16 parts);
+// column half h takes the 8-feature groups h, h + 2, ...
+__device__ __forceinline__ void tr_stage_input(const float* __restrict__ in, int64_t in_ld, int nin, int k_pad,
+                                               int64_t col, int64_t batch, const TrEpi& E) {
+  const bool live = col < batch;
+  const float* src = in + col;
+#pragma unroll 1
+  for (int g = E.h; g < k_pad / 8; g += 2) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int f = 8 * g + e;
+      v[e] = (live && f < nin) ? __ldg(src + (int64_t)f * in_ld) : 0.0f;
+    }
+    store_row8<float>(E.a, E.m, 8 * g, v);
+  }
+}
+
+// Tile order shared by the three roles: rounds of two tiles (one per slot);
+// within a round, Matvec by Matvec, slot 0's job then slot 1's.
+struct TrJobs {
+  int64_t first, stride;
+  int64_t count[kTrSlots];
+  __device__ TrJobs(int64_t ntiles, int64_t first_, int64_t stride_) : first(first_), stride(stride_) {
+    const int64_t mine = first_ < ntiles ? (ntiles - first_ + stride_ - 1) / stride_ : 0;
+    count[0] = (mine + 1) / 2;
+    count[1] = mine / 2;
+  }
+  __device__ int64_t tile(int s, int64_t r) const { return first + (2 * r + s) * stride; }
+};
+
+__global__ void __launch_bounds__(kTrThreads, 1)
+    tr_forward_kernel(const __grid_constant__ TrProgram p, const unsigned char* __restrict__ image,
+                      float* __restrict__ scratch, const float* __restrict__ in, int64_t in_ld,
+                      float* __restrict__ out, int64_t out_ld, int64_t batch, int* __restrict__ err) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t base = smem_u32(smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (base & 1023u) {  // the operand layouts need 1024-byte alignment
+    if (tid == 0) atomicExch(err, 5);
+    return;
+  }
+  const uint32_t s_ring = base + kTrSlots * 3 * kTrPartBytes;
+  const uint32_t s_xch = s_ring + kTrStages * kTrChunkBytes;
+  const uint32_t s_bars = s_xch + kTrSlots * 2 * 128 * 4;
+  const uint32_t b_full = s_bars;        // [stage]
+  const uint32_t b_empty = s_bars + 16;  // [stage]
+  const uint32_t b_accf = s_bars + 32;   // [slot] accumulator ready (MMA -> epilogue)
+  const uint32_t b_epid = s_bars + 48;   // [slot] operand written and TMEM free (epilogue -> MMA)
+  const uint32_t b_drain = s_bars + 64;
+  const uint32_t s_tmem = s_bars + 72;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem_raw + (s_tmem - base));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem_raw + (s_tmem + 4 - base));
+
+  const int64_t ntiles = (batch + kTcM - 1) / kTcM;
+  if ((int64_t)blockIdx.x >= ntiles) return;
+  const TrJobs jobs(ntiles, blockIdx.x, gridDim.x);
+  const int nl = p.n_layers;
+
+  if (warp == kTrMmaWarp) tmem_alloc(s_tmem, 2 * kTrSlotTmem);
+  if (tid == 0) {
+    for (int r = 0; r < kTrStages; ++r) {
+      mbar_init(b_full + 8u * r, 1);
+      mbar_init(b_empty + 8u * r, 1);
+    }
+    for (int s = 0; s < kTrSlots; ++s) {
+      mbar_init(b_accf + 8u * s, 1);
+      mbar_init(b_epid + 8u * s, kTrGroupWarps);
+    }
+    mbar_init(b_drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == kTrProducerWarp) {
+    // ------------------------------------------------ producer ----
+    if (lane == 0) {
+      uint32_t use = 0;
+      bool ok = true;
+      for (int64_t r = 0; r < jobs.count[0] && ok; ++r)
+        for (int l = 0; l < nl && ok; ++l)
+          for (int s = 0; s < kTrSlots && ok; ++s) {
+            if (r >= jobs.count[s]) continue;
+            const TrLayer& L = p.layers[l];
+            const uint32_t bytes = (uint32_t)L.n_pad * 128u;
+            for (int c = 0; c < L.kblk * 3; ++c) {
+              const uint32_t st = use % kTrStages;
+              if (use >= (uint32_t)kTrStages &&
+                  !wait_phase_abort(b_empty + 8u * st, ((use / kTrStages) - 1) & 1u, abort_flag, kWaitCycles)) {
+                ok = false;
+                break;
+              }
+              mbar_expect_tx(b_full + 8u * st, bytes);
+              bulk_load(s_ring + st * kTrChunkBytes, image + L.w_off + (uint64_t)c * bytes, bytes, b_full + 8u * st);
+              ++use;
+            }
+          }
+      // Drain: the copies issued last must have landed before the CTA exits.
+      const uint32_t n = use < (uint32_t)kTrStages ? use : (uint32_t)kTrStages;
+      for (uint32_t u = use - n; u < use; ++u) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(b_full + 8u * (u % kTrStages), (u / kTrStages) & 1u))
+          if (clock64() - t0 > kWaitCycles) break;
+      }
+      if (!ok) atomicExch(err, 2);
+    }
+    __syncwarp();
+  } else if (warp == kTrMmaWarp) {
+    // --------------------------------------------- MMA issuer ----
+    if (lane == 0) {
+      uint32_t use = 0, ep[kTrSlots] = {0, 0};
+      bool ok = true;
+      for (int64_t r = 0; r < jobs.count[0] && ok; ++r)
+        for (int l = 0; l < nl && ok; ++l)
+          for (int s = 0; s < kTrSlots && ok; ++s) {
+            if (r >= jobs.count[s]) continue;
+            const TrLayer& L = p.layers[l];
+            // The slot's operand is written and its accumulators are free.
+            if (!(ok = wait_phase_abort(b_epid + 8u * s, ep[s], abort_flag, kWaitCycles))) break;
+            ep[s] ^= 1u;
+            tc_fence_after();
+            const uint32_t n_pad = (uint32_t)L.n_pad, gs = (uint32_t)L.group_steps, idesc = L.idesc;
+            const uint32_t d = tmem_base + (uint32_t)s * kTrSlotTmem;
+            const uint32_t dc = d + (uint32_t)(L.groups - 1) * n_pad;
+            const uint32_t a_base = base + (uint32_t)(s * 3) * kTrPartBytes;
+            const uint64_t a0 = smem_desc(a_base, 16, 1024), a1 = smem_desc(a_base + kTrPartBytes, 16, 1024),
+                           a2 = smem_desc(a_base + 2 * kTrPartBytes, 16, 1024);
+            for (int kb = 0; kb < L.kblk && ok; ++kb)
+              for (int j = 0; j < 3; ++j) {  // weight part 2, 1, 0
+                const uint32_t st = use % kTrStages;
+                if (!(ok = wait_phase_abort(b_full + 8u * st, (use / kTrStages) & 1u, abort_flag, kWaitCycles)))
+                  break;
+                tc_fence_after();
+                const uint64_t b = smem_desc(s_ring + st * kTrChunkBytes, 16, 1024);
+                const int k_end = min(L.nsteps, kb * 4 + 4);
+                for (int k = kb * 4; k < k_end; ++k) {
+                  const uint64_t ao = (uint64_t)(k >> 2) * 1024 + (uint64_t)(k & 3) * 2;
+                  const uint64_t bk = b + (uint64_t)(k & 3) * 2;
+                  if (j == 0) {
+                    umma_f16(dc, a0 + ao, bk, idesc, k > 0 ? 1u : 0u);  // x0 * w2 (first into the correction)
+                  } else if (j == 1) {
+                    umma_f16(dc, a1 + ao, bk, idesc, 1u);  // x1 * w1
+                    umma_f16(dc, a0 + ao, bk, idesc, 1u);  // x0 * w1
+                  } else {
+                    umma_f16(dc, a2 + ao, bk, idesc, 1u);  // x2 * w0
+                    umma_f16(dc, a1 + ao, bk, idesc, 1u);  // x1 * w0
+                    umma_f16(d + ((uint32_t)k / gs) * n_pad, a0 + ao, bk, idesc, ((uint32_t)k % gs) ? 1u : 0u);
+                  }
+                }
+                umma_commit(b_empty + 8u * st);
+                ++use;
+              }
+            if (ok) umma_commit(b_accf + 8u * s);
+          }
+      // Drain: every MMA issued has completed before TMEM is freed.
+      umma_commit(b_drain);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(b_drain, 0))
+        if (clock64() - t0 > kWaitCycles) break;
+      if (!ok) atomicExch(err, 3);
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------- epilogue ----
+    TrEpi E;
+    E.s = warp / kTrGroupWarps;
+    E.h = (warp >> 2) & 1;
+    E.m = (warp & 3) * 32 + lane;
+    E.image = image;
+    E.saved = reinterpret_cast<float4*>(scratch + (size_t)blockIdx.x * (p.scratch_per_cta / 4)) +
+              (size_t)E.s * p.n_saved * (kTrMaxN / 4) * 128;
+    for (int q = 0; q < 3; ++q) E.a[q] = base + (uint32_t)(E.s * 3 + q) * kTrPartBytes;
+    E.tmem_row = tmem_base + (uint32_t)E.s * kTrSlotTmem + ((uint32_t)((warp & 3) * 32) << 16);
+    E.xch = reinterpret_cast<float*>(smem_raw + (s_xch - base)) + E.s * 256;
+    const int s = E.s;
+    const int k0 = p.layers[0].k_pad;
+    uint32_t acc_ph = 0;
+    if (jobs.count[s] > 0) {
+      tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, 0) * kTcM + E.m, batch, E);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_epid + 8u * s);
+    }
+    bool ok = true;
+    for (int64_t r = 0; r < jobs.count[s] && ok; ++r) {
+      const int64_t col = jobs.tile(s, r) * kTcM + E.m;
+      for (int l = 0; l < nl; ++l) {
+        int got = 0;
+        if (lane == 0) got = wait_phase_abort(b_accf + 8u * s, acc_ph, abort_flag, kWaitCycles) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        // The slot's warps leave together (none is left at a named barrier).
+        if (slot_sync_or(s, !got)) {
+          ok = false;
+          break;
+        }
+        acc_ph ^= 1u;
+        tc_fence_after();
+        tr_epilogue(p, l, E, out, out_ld, col, batch);
+        if (l + 1 < nl) {
+          fence_proxy_async();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(b_epid + 8u * s);
+        }
+      }
+      if (ok && r + 1 < jobs.count[s]) {
+        // The slot's MMAs are done with its operand and its accumulators are
+        // read: stage the next tile.
+        tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, r + 1) * kTcM + E.m, batch, E);
+        fence_proxy_async();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b_epid + 8u * s);
+      }
+    }
+    if (!ok && tid % kTrGroupThreads == 0) atomicExch(err, 4);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kTrMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * kTrSlotTmem);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_tr_forward(const TrProgram& p, const void* image, void* scratch, const void* in, int64_t in_ld,
+                              void* out, int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream) {
+  if (p.dtype != 0) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(tr_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)p.smem_bytes);
+  if (e != cudaSuccess) return e;
+  tr_forward_kernel<<<grid, kTrThreads, p.smem_bytes, stream>>>(
+      p, static_cast<const unsigned char*>(image), static_cast<float*>(scratch), static_cast<const float*>(in), in_ld,
+      static_cast<float*>(out), out_ld, batch, err);
+  return cudaGetLastError();
+}
+
+}  // namespace ponni_b200

@@ -45,6 +45,7 @@ CASES = {
                        {"PONNI_B200_NARROW_JIT": "0"}),
     "tensor_f32_split": (lambda r: _cfg_layers("cfg2"), pb.F32, None, A.KERNEL_TENSOR, {}),
     "tensor_f32_frozen_layer": (_mixed_trainable, pb.F32, None, A.KERNEL_TENSOR, {}),
+    "tensor_resid_cfg4": (lambda r: _cfg_layers("cfg4"), pb.F32, None, A.KERNEL_TENSOR_RESID, {}),
     "tensor_f16": (lambda r: _cfg_layers("cfg3"), pb.F16, A.ARITH_TENSOR, A.KERNEL_TENSOR, {}),
     "tensor_streamed_bf16": (lambda r: _cfg_layers("cfg5"), pb.BF16, A.ARITH_TENSOR, A.KERNEL_TENSOR_STREAM, {}),
     "tensor_streamed_f16": (lambda r: _cfg_layers("cfg3"), pb.F16, A.ARITH_TENSOR, A.KERNEL_TENSOR_STREAM,

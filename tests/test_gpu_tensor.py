@@ -110,12 +110,20 @@ def test_auto_policy():
 
 
 def test_tc_ineligible_falls_back_or_errors():
-    cfg = configs.cfg4(batch=10)  # LayerNorm / residual: tile kernel
+    # LayerNorm / residual fp32 chains: the residual tensor-core kernel
+    cfg = configs.cfg4(batch=10)
     m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=pb._abi.ARITH_AUTO)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_RESID
+    # 16-bit LayerNorm chains stay on the tile kernel; fp32 accumulation is refused
+    m = pb.Inference(cfg.layers, dtype=pb.F16, arithmetic=pb._abi.ARITH_AUTO)
     assert m.kernel() == pb._abi.KERNEL_TILE
-    m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    m = pb.Inference(cfg.layers, dtype=pb.F16, arithmetic=pb._abi.ARITH_TENSOR)
     with pytest.raises(pb.PonniError):
         m.kernel()
+    # a barrier the residual kernel does not fuse (Softmax): tile kernel
+    rng = np.random.default_rng(3)
+    layers = [pb.Matvec(rng.normal(0, 0.3, (8, 64))), pb.Softmax(64), pb.Matvec(rng.normal(0, 0.3, (64, 4)))]
+    assert pb.Inference(layers, dtype=pb.F32).kernel() == pb._abi.KERNEL_TILE
 
 
 # ---- streamed-weights kernel (weights beyond shared memory) ----
@@ -178,3 +186,116 @@ def test_ts_strided_misaligned(oracle_lib):
     m.synchronize()
     check_acc32(from_torch(out_big[:, 1:1001].contiguous(), cfg.dtype), cfg.layers, cfg.dtype, x, oracle_lib)
     assert torch.isnan(out_big[:, 0].float()).all() and torch.isnan(out_big[:, 1001:].float()).all()
+
+
+# ---- LayerNorm / residual chains (fp32 split, weights streamed) ----
+
+def run_tr(layers, x_raw, monkeypatch=None, grid=None, arithmetic=None):
+    if monkeypatch is not None and grid is not None:
+        monkeypatch.setenv("PONNI_B200_TC_GRID", str(grid))
+    m = pb.Inference(layers, dtype=pb.F32, arithmetic=arithmetic)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_RESID
+    y = m.forward_batch_parallel(to_torch(x_raw, pb.F32).cuda())
+    m.synchronize()
+    torch.cuda.synchronize()
+    return from_torch(y, pb.F32)
+
+
+@pytest.mark.parametrize("batch", [1, 3, 127, 128, 129, 300, 4099])
+def test_tr_cfg4(batch, oracle_lib):
+    """The residual MLP (LayerNorm, GELU, Save_State / Binop_Add) on tensor cores."""
+    cfg = configs.cfg4(batch=batch)
+    x = configs.host_inputs(cfg, batch)
+    y = run_tr(cfg.layers, x)
+    check(y, oracle_lib.forward(cfg.layers, cfg.dtype, x), cfg.dtype, cfg.layers, x)
+
+
+def test_tr_scratch_is_reported():
+    m = pb.Inference(configs.cfg4(batch=10).layers, dtype=pb.F32)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_RESID
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert m.scratch_bytes() == sms * 2 * 1 * 128 * 128 * 4  # two tile slots x one saved state
+
+
+@pytest.mark.parametrize("grid,batch", [(1, 1000), (2, 1537), (3, 4099)])
+def test_tr_cfg4_many_tiles_per_cta(grid, batch, oracle_lib, monkeypatch):
+    """A capped grid runs several tiles per CTA, both tile slots alternating."""
+    cfg = configs.cfg4(batch=batch)
+    x = configs.host_inputs(cfg, batch)
+    y = run_tr(cfg.layers, x, monkeypatch, grid)
+    check(y, oracle_lib.forward(cfg.layers, cfg.dtype, x), cfg.dtype, cfg.layers, x)
+
+
+def resid_model(rng, widths=(24, 64, 96, 128, 40, 32), n_out=7):
+    """Residual chain with every fused operation: LayerNorm with non-trivial
+    gamma/beta at several widths, two saved states, Binop_Add before and after
+    activations and LayerNorm, all activations, widths that are not multiples
+    of 16."""
+    acts = [pb.Relu, pb.Gelu, lambda n: pb.Gelu(n, True), pb.Silu, pb.Tanh, pb.Sigmoid, pb.Elu, pb.Selu,
+            lambda n: pb.Softplus(n, 1.5), lambda n: pb.HardSigmoid(n, 0.2, 0.5), pb.HardSwish, pb.Mish,
+            lambda n: pb.LeakyRelu(n, 0.1)]
+    ln = lambda n: pb.LayerNorm(rng.normal(1, 0.2, n), rng.normal(0, 0.2, n))  # noqa: E731
+    w0 = widths[0]
+    layers = [pb.Matvec(rng.normal(0, 1 / np.sqrt(w0), (w0, 64))), pb.Bias(rng.normal(0, 0.1, 64)),
+              pb.Save_State(64, 0), ln(64)]
+    layers += [pb.Matvec(rng.normal(0, 0.15, (64, 64))), pb.Bias(rng.normal(0, 0.1, 64)), acts[0](64),
+               pb.Binop_Add(64, 0), pb.Save_State(64, 3), acts[1](64)]
+    layers += [pb.Matvec(rng.normal(0, 0.15, (64, 96))), pb.Bias(rng.normal(0, 0.1, 96)), acts[2](96), ln(96),
+               acts[3](96), pb.Save_State(96, 0)]
+    layers += [pb.Matvec(rng.normal(0, 0.12, (96, 128))), acts[4](128), ln(128), acts[5](128)]
+    layers += [pb.Matvec(rng.normal(0, 0.1, (128, 96))), pb.Bias(rng.normal(0, 0.1, 96)), acts[6](96),
+               acts[7](96), pb.Binop_Add(96, 0), acts[8](96), acts[9](96)]
+    layers += [pb.Matvec(rng.normal(0, 0.12, (96, 64))), acts[10](64), acts[11](64), pb.Binop_Add(64, 3),
+               acts[12](64), ln(64)]
+    layers += [pb.Matvec(rng.normal(0, 0.15, (64, 40))), pb.Bias(rng.normal(0, 0.1, 40)), pb.Relu(40),
+               pb.Matvec(rng.normal(0, 0.2, (40, n_out))), pb.Bias(rng.normal(0, 0.1, n_out))]
+    return layers
+
+
+@pytest.mark.parametrize("batch,grid", [(5, None), (777, None), (3001, 2)])
+def test_tr_all_fused_operations(batch, grid, oracle_lib, monkeypatch):
+    rng = np.random.default_rng(21)
+    layers = resid_model(rng)
+    x = rng.normal(0, 1, (24, batch)).astype(np.float32)
+    y = run_tr(layers, x, monkeypatch, grid)
+    check(y, oracle_lib.forward(layers, pb.F32, x), pb.F32, layers, x)
+
+
+def test_tr_pytorch_resnet_fixture():
+    """The reference's pytorch_resnet fixture (5-wide Save_State / Binop_Add
+    chain) through the residual kernel, abs tol 1e-5 as in
+    unit/pytorch_resnet/test_pytorch_resnet.cpp:69-77."""
+    layers, x, expected = K.pytorch_resnet()
+    # 5 wide: the default policy keeps such narrow models off tensor cores
+    y = run_tr(layers, np.ascontiguousarray(x, dtype=np.float32), arithmetic=pb._abi.ARITH_TENSOR)
+    assert np.max(np.abs(y - expected)) <= 1e-5
+
+
+def test_tr_strided_misaligned(oracle_lib):
+    cfg = configs.cfg4(batch=1000)
+    x = configs.host_inputs(cfg, 1000)
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_RESID
+    big = torch.zeros((16, 1000 + 17), dtype=torch.float32, device="cuda")
+    big[:, 3:1003] = torch.from_numpy(x).cuda()
+    out_big = torch.full((8, 1009), float("nan"), device="cuda")
+    m.forward_batch_parallel(big[:, 3:1003], out_big[:, 1:1001])
+    m.synchronize()
+    check(out_big[:, 1:1001].cpu().numpy(), oracle_lib.forward(cfg.layers, cfg.dtype, x), cfg.dtype, cfg.layers, x)
+    assert torch.isnan(out_big[:, 0]).all() and torch.isnan(out_big[:, 1001:]).all()
+
+
+def test_tr_matches_tile_kernel(oracle_lib, monkeypatch):
+    """Both kernels pass the same gate on the same inputs, and agree to fp32 accuracy."""
+    cfg = configs.cfg4(batch=2000)
+    x = configs.host_inputs(cfg, 2000)
+    y_tr = run_tr(cfg.layers, x)
+    monkeypatch.setenv("PONNI_B200_TC_RESID", "0")
+    m = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    assert m.kernel() == pb._abi.KERNEL_TILE
+    y_tile = from_torch(m.forward_batch_parallel(to_torch(x, pb.F32).cuda()), pb.F32)
+    torch.cuda.synchronize()
+    ref = oracle_lib.forward(cfg.layers, cfg.dtype, x)
+    check(y_tile, ref, cfg.dtype, cfg.layers, x)
+    assert K.normwise_err(y_tr, y_tile) <= 1e-5
+    assert m.scratch_bytes() == 0
