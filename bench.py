@@ -273,7 +273,7 @@ def main():
     if cfg.bound == "hbm":
         roof = {"bound": "hbm", "achieved": cfg.bytes_per_sample * B / launch_s / 1e9, "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "peak_source": f"hbm_gbs ({pk_src})"}
-    elif kernel in (pb._abi.KERNEL_TENSOR, pb._abi.KERNEL_TENSOR_STREAM):
+    elif kernel in (pb._abi.KERNEL_TENSOR, pb._abi.KERNEL_TENSOR_STREAM, pb._abi.KERNEL_TENSOR_RESID):
         # fp32 models run six bf16 MMAs per multiply-add (exact 3-way operand
         # split), so their tensor roofline is a sixth of the bf16 peak.
         passes = 6 if cfg.dtype == pb.F32 else 1
