@@ -107,6 +107,21 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                : "memory");
 }
 
+// Same, with both descriptors given as 32-bit halves: `alo` / `blo` carry
+// the start address (advanced by the caller, no carry out of the 14-bit
+// field), `hi` the shared upper half (stride, version, swizzle).
+__device__ __forceinline__ void umma_f16_lh(uint32_t d_tmem, uint32_t alo, uint32_t blo, uint32_t hi, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(alo), "r"(blo), "r"(hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Warp-level forms: every lane of a converged warp calls them (elect.sync
 // over the full warp), one elected lane issues; the whole warp runs the issue
 // loop so the descriptors stay in uniform registers.  Never call these from

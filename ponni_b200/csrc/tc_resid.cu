@@ -57,6 +57,22 @@ using namespace tc;
 
 constexpr long long kWaitCycles = 1ll << 31;
 
+// Optional phase timing (compiled only with -DPONNI_B200_TC_PROFILE): each
+// role sums the cycles of its phases and adds them once per CTA to the
+// diagnostic counters after the error word (1: MMA waits for the epilogue,
+// 2: MMA waits for weights, 3: producer waits for a free stage, 4: epilogue
+// waits for accumulators, 5: epilogue work, 6: LayerNorm passes 2-3,
+// 7: MMA thread total).
+#ifdef PONNI_B200_TC_PROFILE
+#define TR_T(var) const long long var = clock64()
+#define TR_ACC(acc, t0) acc += clock64() - (t0)
+#define TR_FLUSH(idx, acc) atomicAdd(reinterpret_cast<unsigned long long*>(err) + (idx), (unsigned long long)(acc))
+#else
+#define TR_T(var)
+#define TR_ACC(acc, t0)
+#define TR_FLUSH(idx, acc)
+#endif
+
 // 32 fp32 values into 32 consecutive TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
@@ -97,6 +113,16 @@ __device__ __forceinline__ int slot_sync_or(int s, int pred) {
 
 template <int K>
 __device__ __forceinline__ void act32(float (&v)[32], int flags, float s0, float s1) {
+  if constexpr (K == EPI_GELU) {
+    if (!(flags & 0x2)) {
+      // exact GELU, 0.5 x (1 + erf(x / sqrt 2)) (src/layers/ponni_Gelu.h:47-57),
+      // with x / sqrt 2 as a product by the rounded 1 / sqrt 2 (within one
+      // unit of the quotient)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.0f + erff(v[j] * 0.70710678118654752f));
+      return;
+    }
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = activation<float>(K, flags, v[j], s0, s1);
 }
@@ -209,9 +235,14 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
     }
     tr_ops(p.ops, o0, o_ln, v, c0, E);
     if (has_ln) {
+      if (nout - c0 >= 32) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < nout) psum = __fadd_rn(psum, v[j]);
+        for (int j = 0; j < 32; ++j) psum = __fadd_rn(psum, v[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < nout) psum = __fadd_rn(psum, v[j]);
+      }
       tmem_st32(E.tmem_row + (uint32_t)c0, v);  // park the row in the read main accumulator
     } else {
       tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
@@ -232,12 +263,20 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
   for (int c0 = cb; c0 < ce; c0 += 32) {
     float v[32];
     tmem_ld32(E.tmem_row + (uint32_t)c0, v);
+    if (nout - c0 >= 32) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (c0 + j < nout) {
+      for (int j = 0; j < 32; ++j) {
         const float d = __fsub_rn(v[j], mean);
         pvar = __fadd_rn(pvar, __fmul_rn(d, d));
       }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < nout) {
+          const float d = __fsub_rn(v[j], mean);
+          pvar = __fadd_rn(pvar, __fmul_rn(d, d));
+        }
+    }
   }
   E.xch[E.h * 128 + E.m] = pvar;
   slot_sync(E.s);
@@ -282,15 +321,64 @@ __device__ __forceinline__ void tr_stage_input(const float* __restrict__ in, int
   }
 }
 
+// MMA issue state of one job.
+struct TrIssue {
+  uint32_t a0, a1, a2;  // low descriptor halves of the slot's A operand parts
+  uint32_t hi;          // shared upper descriptor half
+  uint32_t d_main, dc;  // current main accumulator, correction accumulator
+  uint32_t g_in, gs;    // K steps issued into the current main accumulator, steps per main accumulator
+  uint32_t n_pad, idesc;
+};
+
+// One weight chunk (part 2 - J of K block kb): wait for it, issue its
+// products (x0 w2 | x1 w1, x0 w1 | x2 w0, x1 w0, x0 w0; smallest first
+// into the correction accumulator), release the ring stage.
+template <int J>
+__device__ __forceinline__ bool tr_chunk(TrIssue& I, int kb, int nsteps, uint32_t& use, uint32_t ring_lo,
+                                         uint32_t b_full, uint32_t b_empty, volatile int* abort_flag,
+                                         long long& w_full) {
+  (void)w_full;
+  const uint32_t st = use & 1u;
+  TR_T(tf);
+  if (!wait_phase_abort(b_full + 8u * st, (use >> 1) & 1u, abort_flag, kWaitCycles)) return false;
+  TR_ACC(w_full, tf);
+  tc_fence_after();
+  const uint32_t b = ring_lo + st * (kTrChunkBytes >> 4);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    if (kb * 4 + kk < nsteps) {
+      const uint32_t ao = (uint32_t)kb * 1024u + (uint32_t)kk * 2u;  // K block: 16 KB; K step: 32 B
+      const uint32_t bk = b + (uint32_t)kk * 2u;
+      if constexpr (J == 0) {
+        umma_f16_lh(I.dc, I.a0 + ao, bk, I.hi, I.idesc, (kb | kk) ? 1u : 0u);
+      } else if constexpr (J == 1) {
+        umma_f16_lh(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
+        umma_f16_lh(I.dc, I.a0 + ao, bk, I.hi, I.idesc, 1u);
+      } else {
+        umma_f16_lh(I.dc, I.a2 + ao, bk, I.hi, I.idesc, 1u);
+        umma_f16_lh(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
+        umma_f16_lh(I.d_main, I.a0 + ao, bk, I.hi, I.idesc, I.g_in ? 1u : 0u);
+        if (++I.g_in == I.gs) {
+          I.g_in = 0;
+          I.d_main += I.n_pad;
+        }
+      }
+    }
+  }
+  umma_commit(b_empty + 8u * st);
+  ++use;
+  return true;
+}
+
 // Tile order shared by the three roles: rounds of two tiles (one per slot);
 // within a round, Matvec by Matvec, slot 0's job then slot 1's.
 struct TrJobs {
   int64_t first, stride;
-  int64_t count[kTrSlots];
+  int64_t c0, c1;  // tiles of slot 0 and slot 1
   __device__ TrJobs(int64_t ntiles, int64_t first_, int64_t stride_) : first(first_), stride(stride_) {
     const int64_t mine = first_ < ntiles ? (ntiles - first_ + stride_ - 1) / stride_ : 0;
-    count[0] = (mine + 1) / 2;
-    count[1] = mine / 2;
+    c0 = (mine + 1) / 2;
+    c1 = mine / 2;
   }
   __device__ int64_t tile(int s, int64_t r) const { return first + (2 * r + s) * stride; }
 };
@@ -347,19 +435,23 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     if (lane == 0) {
       uint32_t use = 0;
       bool ok = true;
-      for (int64_t r = 0; r < jobs.count[0] && ok; ++r)
+      [[maybe_unused]] long long w_empty = 0;
+      (void)w_empty;
+      for (int64_t r = 0; r < jobs.c0 && ok; ++r)
         for (int l = 0; l < nl && ok; ++l)
           for (int s = 0; s < kTrSlots && ok; ++s) {
-            if (r >= jobs.count[s]) continue;
+            if (r >= (s ? jobs.c1 : jobs.c0)) continue;
             const TrLayer& L = p.layers[l];
             const uint32_t bytes = (uint32_t)L.n_pad * 128u;
             for (int c = 0; c < L.kblk * 3; ++c) {
               const uint32_t st = use % kTrStages;
+              TR_T(tw);
               if (use >= (uint32_t)kTrStages &&
                   !wait_phase_abort(b_empty + 8u * st, ((use / kTrStages) - 1) & 1u, abort_flag, kWaitCycles)) {
                 ok = false;
                 break;
               }
+              TR_ACC(w_empty, tw);
               mbar_expect_tx(b_full + 8u * st, bytes);
               bulk_load(s_ring + st * kTrChunkBytes, image + L.w_off + (uint64_t)c * bytes, bytes, b_full + 8u * st);
               ++use;
@@ -373,61 +465,65 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           if (clock64() - t0 > kWaitCycles) break;
       }
       if (!ok) atomicExch(err, 2);
+      TR_FLUSH(3, w_empty);
     }
     __syncwarp();
   } else if (warp == kTrMmaWarp) {
     // --------------------------------------------- MMA issuer ----
     if (lane == 0) {
-      uint32_t use = 0, ep[kTrSlots] = {0, 0};
+      uint32_t use = 0, ep0 = 0, ep1 = 0;
       bool ok = true;
-      for (int64_t r = 0; r < jobs.count[0] && ok; ++r)
-        for (int l = 0; l < nl && ok; ++l)
+      [[maybe_unused]] long long w_epi = 0, w_full = 0;
+      TR_T(t_all);
+      // Descriptors as 32-bit halves: start addresses advance in the low half.
+      const uint32_t hi = (uint32_t)(smem_desc(0, 16, 1024) >> 32);
+      const uint32_t lo_flags = (uint32_t)smem_desc(0, 16, 1024);
+      const uint32_t ring_lo = lo_flags | ((s_ring >> 4) & 0x3FFFu);
+      for (int64_t r = 0; r < jobs.c0 && ok; ++r)
+        for (int l = 0; l < nl && ok; ++l) {
+          const TrLayer& L = p.layers[l];
+          const uint32_t n_pad = (uint32_t)L.n_pad, gs = (uint32_t)L.group_steps, idesc = L.idesc;
+          const int kblk = L.kblk, nsteps = L.nsteps, groups = L.groups;
           for (int s = 0; s < kTrSlots && ok; ++s) {
-            if (r >= jobs.count[s]) continue;
-            const TrLayer& L = p.layers[l];
+            if (r >= (s ? jobs.c1 : jobs.c0)) continue;
             // The slot's operand is written and its accumulators are free.
-            if (!(ok = wait_phase_abort(b_epid + 8u * s, ep[s], abort_flag, kWaitCycles))) break;
-            ep[s] ^= 1u;
+            TR_T(te);
+            if (!(ok = wait_phase_abort(b_epid + 8u * s, s ? ep1 : ep0, abort_flag, kWaitCycles))) break;
+            if (s) ep1 ^= 1u;
+            else ep0 ^= 1u;
+            TR_ACC(w_epi, te);
             tc_fence_after();
-            const uint32_t n_pad = (uint32_t)L.n_pad, gs = (uint32_t)L.group_steps, idesc = L.idesc;
-            const uint32_t d = tmem_base + (uint32_t)s * kTrSlotTmem;
-            const uint32_t dc = d + (uint32_t)(L.groups - 1) * n_pad;
+            TrIssue I;
+            I.d_main = tmem_base + (uint32_t)s * kTrSlotTmem;
+            I.dc = I.d_main + (uint32_t)(groups - 1) * n_pad;
+            I.g_in = 0;
+            I.gs = gs;
+            I.n_pad = n_pad;
+            I.idesc = idesc;
+            I.hi = hi;
             const uint32_t a_base = base + (uint32_t)(s * 3) * kTrPartBytes;
-            const uint64_t a0 = smem_desc(a_base, 16, 1024), a1 = smem_desc(a_base + kTrPartBytes, 16, 1024),
-                           a2 = smem_desc(a_base + 2 * kTrPartBytes, 16, 1024);
-            for (int kb = 0; kb < L.kblk && ok; ++kb)
-              for (int j = 0; j < 3; ++j) {  // weight part 2, 1, 0
-                const uint32_t st = use % kTrStages;
-                if (!(ok = wait_phase_abort(b_full + 8u * st, (use / kTrStages) & 1u, abort_flag, kWaitCycles)))
-                  break;
-                tc_fence_after();
-                const uint64_t b = smem_desc(s_ring + st * kTrChunkBytes, 16, 1024);
-                const int k_end = min(L.nsteps, kb * 4 + 4);
-                for (int k = kb * 4; k < k_end; ++k) {
-                  const uint64_t ao = (uint64_t)(k >> 2) * 1024 + (uint64_t)(k & 3) * 2;
-                  const uint64_t bk = b + (uint64_t)(k & 3) * 2;
-                  if (j == 0) {
-                    umma_f16(dc, a0 + ao, bk, idesc, k > 0 ? 1u : 0u);  // x0 * w2 (first into the correction)
-                  } else if (j == 1) {
-                    umma_f16(dc, a1 + ao, bk, idesc, 1u);  // x1 * w1
-                    umma_f16(dc, a0 + ao, bk, idesc, 1u);  // x0 * w1
-                  } else {
-                    umma_f16(dc, a2 + ao, bk, idesc, 1u);  // x2 * w0
-                    umma_f16(dc, a1 + ao, bk, idesc, 1u);  // x1 * w0
-                    umma_f16(d + ((uint32_t)k / gs) * n_pad, a0 + ao, bk, idesc, ((uint32_t)k % gs) ? 1u : 0u);
-                  }
-                }
-                umma_commit(b_empty + 8u * st);
-                ++use;
-              }
+            I.a0 = lo_flags | ((a_base >> 4) & 0x3FFFu);
+            I.a1 = I.a0 + (kTrPartBytes >> 4);
+            I.a2 = I.a0 + 2 * (kTrPartBytes >> 4);
+            for (int kb = 0; kb < kblk && ok; ++kb) {
+              ok = tr_chunk<0>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full) &&
+                   tr_chunk<1>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full) &&
+                   tr_chunk<2>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full);
+            }
             if (ok) umma_commit(b_accf + 8u * s);
           }
+        }
       // Drain: every MMA issued has completed before TMEM is freed.
       umma_commit(b_drain);
       const long long t0 = clock64();
       while (!mbar_try_wait(b_drain, 0))
         if (clock64() - t0 > kWaitCycles) break;
       if (!ok) atomicExch(err, 3);
+      TR_FLUSH(1, w_epi);
+      TR_FLUSH(2, w_full);
+#ifdef PONNI_B200_TC_PROFILE
+      TR_FLUSH(7, clock64() - t_all);
+#endif
     }
     __syncwarp();
   } else {
@@ -445,16 +541,21 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     const int s = E.s;
     const int k0 = p.layers[0].k_pad;
     uint32_t acc_ph = 0;
-    if (jobs.count[s] > 0) {
+    const int64_t my_tiles = s ? jobs.c1 : jobs.c0;
+    if (my_tiles > 0) {
       tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, 0) * kTcM + E.m, batch, E);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(b_epid + 8u * s);
     }
     bool ok = true;
-    for (int64_t r = 0; r < jobs.count[s] && ok; ++r) {
+    [[maybe_unused]] long long w_acc = 0, c_work = 0;
+    (void)w_acc;
+    (void)c_work;
+    for (int64_t r = 0; r < my_tiles && ok; ++r) {
       const int64_t col = jobs.tile(s, r) * kTcM + E.m;
       for (int l = 0; l < nl; ++l) {
+        TR_T(ta);
         int got = 0;
         if (lane == 0) got = wait_phase_abort(b_accf + 8u * s, acc_ph, abort_flag, kWaitCycles) ? 1 : 0;
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -464,8 +565,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           break;
         }
         acc_ph ^= 1u;
+        TR_ACC(w_acc, ta);
+        TR_T(tw);
         tc_fence_after();
         tr_epilogue(p, l, E, out, out_ld, col, batch);
+        TR_ACC(c_work, tw);
         if (l + 1 < nl) {
           fence_proxy_async();
           tc_fence_before();
@@ -473,7 +577,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           if (lane == 0) mbar_arrive(b_epid + 8u * s);
         }
       }
-      if (ok && r + 1 < jobs.count[s]) {
+      if (ok && r + 1 < my_tiles) {
         // The slot's MMAs are done with its operand and its accumulators are
         // read: stage the next tile.
         tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, r + 1) * kTcM + E.m, batch, E);
@@ -484,6 +588,10 @@ __global__ void __launch_bounds__(kTrThreads, 1)
       }
     }
     if (!ok && tid % kTrGroupThreads == 0) atomicExch(err, 4);
+    if (tid % kTrGroupThreads == 0) {
+      TR_FLUSH(4, w_acc);
+      TR_FLUSH(5, c_work);
+    }
   }
 
   tc_fence_before();
