@@ -51,6 +51,10 @@
 #include "tc_common.cuh"
 #include "tc_resid.h"
 
+#ifndef PONNI_B200_TR_DIAG
+#define PONNI_B200_TR_DIAG 0
+#endif
+
 namespace ponni_b200 {
 namespace {
 using namespace tc;
@@ -170,7 +174,9 @@ __device__ __forceinline__ void tr_ops(const TrOp* ops, int o0, int o1, float (&
         v[4 * q + 3] = __fadd_rn(v[4 * q + 3], b.w);
       }
     } else if (o.kind == TR_ACT) {
+#if !(PONNI_B200_TR_DIAG & 1)  // diagnostic builds: bit 1 skips activations
       act_dispatch(o.arg, v, o.flags, o.s0, o.s1);
+#endif
     } else if (o.kind == TR_ADD) {
       const float4* sv = E.saved + (size_t)o.arg * (kTrMaxN / 4) * 128 + (c0 / 4) * 128 + E.m;
 #pragma unroll
@@ -205,7 +211,14 @@ __device__ __forceinline__ void tr_finish(const float (&v)[32], int c0, bool las
     }
   } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) store_row8<float>(E.a, E.m, c0 + 8 * q, v + 8 * q);
+    for (int q = 0; q < 4; ++q) {
+#if PONNI_B200_TR_DIAG & 4  // diagnostic builds: bit 4 stores part 0 only, unsplit
+      st_shared_v4(E.a[0] + kmajor_chunk(E.m, (uint32_t)(c0 + 8 * q) * 2), __float_as_uint(v[8 * q]),
+                   __float_as_uint(v[8 * q + 2]), __float_as_uint(v[8 * q + 4]), __float_as_uint(v[8 * q + 6]));
+#else
+      store_row8<float>(E.a, E.m, c0 + 8 * q, v + 8 * q);
+#endif
+    }
   }
 }
 
@@ -249,6 +262,14 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
     }
   }
   if (!has_ln) return;
+#if PONNI_B200_TR_DIAG & 2  // diagnostic builds: bit 2 replaces LayerNorm passes 2-3 by a plain store
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    float v[32];
+    tmem_ld32(E.tmem_row + (uint32_t)c0, v);
+    tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
+  }
+  return;
+#endif
   // LayerNorm over the row (src/layers/ponni_LayerNorm.h:77-99): the two
   // column halves exchange partial sums.
   const TrOp ln = p.ops[o_ln];
