@@ -1,17 +1,21 @@
 """Benchmark of the B200 batched-inference hot path (samples/s).
 
-Default workload: the column-physics emulator MLP 30->64->64->64->10 (ReLU,
-fp32), batch 16,777,216 columns per GPU, synthetic inputs N(0,1) generated on
-each device by a counter-based RNG keyed by the global column (weak scaling:
-rank r owns columns [r*B, (r+1)*B)).  A step is one forward_batch_parallel
-over the whole batch; the 2 GB input exceeds the 126 MB L2, so no flush is
-needed between steps (workloads smaller than L2 are timed step by step with
-an L2-flushing write before each step, outside the timed events).
+Default workload: cfg4, the residual MLP 16->128, 4 x [LayerNorm(128) ->
+Dense128 -> GELU -> Dense128 + skip], ->8 (fp32), the largest configuration
+by work (268,288 FLOP per sample), batch 33,554,432 columns per GPU,
+synthetic inputs N(0,1) generated on each device by a counter-based RNG
+keyed by the global column.  A step is one forward_batch_parallel over the
+whole batch; the 2 GB input exceeds the 126 MB L2, so no flush is needed
+between steps (workloads smaller than L2 are timed step by step with an
+L2-flushing write before each step, outside the timed events).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfgX] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfgX] [--scaling weak|strong]
+                  [--impl ours|reference]
 
-Under torchrun (N>1) every rank runs its shard with no collective on the data
-path; timing is CUDA events on each rank's stream, max over ranks.
+Weak scaling: rank r owns columns [r*B, (r+1)*B).  Strong scaling: the
+config's batch B is split into N contiguous column ranges.  Under torchrun
+(N>1) every rank runs its shard with no collective on the data path; timing
+is CUDA events on each rank's stream, max over ranks.
 """
 from __future__ import annotations
 
@@ -26,6 +30,9 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# The CPUs this process may use before any NUMA binding of a GPU rank: the
+# CPU baseline runs on all of them.
+ALL_CPUS = os.sched_getaffinity(0)
 
 
 def parse():
@@ -33,10 +40,12 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--config", default="cfg2")
+    p.add_argument("--config", default="cfg4")
+    p.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                   help="weak: the config's batch on every GPU; strong: the config's batch split across GPUs")
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--batch", type=int, default=0, help="override per-GPU batch (default: the config's)")
-    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--arith", default="", choices=["", "auto", "reference", "tensor"],
                    help="kernel selection (ponni_b200_model_set_arithmetic); default: the config's")
@@ -102,23 +111,39 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def cpu_reference(cfg, target_seconds=10.0, max_cols=1 << 20):
-    """Time the CPU oracle port on a bounded sample: (samples/s, cores, description, seconds)."""
-    from oracle import oracle
-    from ponni_b200 import configs
+def host_cpu():
+    """(physical cores available to this process, CPU model) from lscpu."""
+    model, cores = "unknown", os.cpu_count() or 1
+    try:
+        allowed = ALL_CPUS
+        out = subprocess.run(["lscpu", "-p=CPU,CORE,SOCKET"], capture_output=True, text=True, timeout=10).stdout
+        phys = {(f[2], f[1]) for f in (ln.split(",") for ln in out.splitlines() if ln and ln[0] != "#")
+                if int(f[0]) in allowed}
+        cores = max(1, len(phys))
+        info = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for ln in info.splitlines():
+            if ln.startswith("Model name:"):
+                model = ln.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return cores, model
 
-    cores = os.cpu_count() or 1
-    n = 4096
-    x = configs.host_inputs(cfg, n)
-    t0 = time.perf_counter()
-    oracle.forward(cfg.layers, cfg.dtype, x, nthreads=cores)
-    dt = max(time.perf_counter() - t0, 1e-6)
-    n = int(min(max_cols, max(4096, n * target_seconds / dt / 2)))
-    x = configs.host_inputs(cfg, n)
-    t0 = time.perf_counter()
-    oracle.forward(cfg.layers, cfg.dtype, x, nthreads=cores)
-    dt = time.perf_counter() - t0
-    return n / dt, cores, f"{n} columns of {cfg.name}, one pass, {cores} OpenMP threads", dt
+
+def cpu_reference(cfg_name, seconds=10.0, max_cols=1 << 20):
+    """Time the CPU oracle port of the reference's path (oracle/cpu_bench.py,
+    a child process) with one OpenMP thread per physical core,
+    OMP_PROC_BIND=spread, OMP_PLACES=cores: median samples/s over passes that
+    total at least one second.  Returns (samples/s, cores, description)."""
+    cores, model = host_cpu()
+    env = dict(os.environ, OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="spread", OMP_PLACES="cores")
+    out = subprocess.run([sys.executable, "-m", "oracle.cpu_bench", "--config", cfg_name, "--seconds", str(seconds),
+                          "--max-cols", str(max_cols)], cwd=ROOT, env=env, capture_output=True, text=True,
+                         check=True, preexec_fn=lambda: os.sched_setaffinity(0, ALL_CPUS)).stdout
+    r = json.loads(out.strip().splitlines()[-1])
+    desc = (f"{r['columns']} columns of {cfg_name} per pass, median of {r['passes']} passes "
+            f"({r['seconds']:.1f} s), {cores} OpenMP threads (OMP_PROC_BIND=spread, OMP_PLACES=cores) on "
+            f"{cores} physical cores, {model}")
+    return r["samples_per_s"], cores, desc
 
 
 def run_reference(args, cfg, rank, metric, unit, dtype_name):
@@ -128,14 +153,14 @@ def run_reference(args, cfg, rank, metric, unit, dtype_name):
     steps, info = [], None
     per_step = min(10.0, 120.0 / max(1, args.warmup + args.steps))
     for i in range(args.warmup + args.steps):
-        v, cores, sample, _ = cpu_reference(cfg, target_seconds=per_step)
+        v, cores, sample = cpu_reference(args.config, seconds=per_step)
         if i >= args.warmup:
             steps.append(v)
         info = (cores, sample)
     value = statistics.median(steps)
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": dtype_name, "data": "synthetic",
         "config": {"workload": cfg.name, "batch_per_gpu": cfg.batch, "sample": info[1]},
         "cpu_baseline": {"value": value, "unit": unit, "cores": info[0], "kind": "port", "sample": info[1]},
@@ -199,13 +224,18 @@ def main():
     import torch
     import torch.distributed as dist
     import ponni_b200 as pb
-    from ponni_b200.sharding import job_time, shard_range
+    from ponni_b200.sharding import bind_numa, job_time, shard_range, split_range
 
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    B = cfg.batch
+    if args.scaling == "strong":
+        col0, B = split_range(rank, world, cfg.batch)
+    else:
+        B = cfg.batch
+        col0, _ = shard_range(rank, world, B)
+    numa = bind_numa(local)
     nin, nout = cfg.layers[0].num_inputs, cfg.layers[-1].num_outputs
     arith_name = args.arith or cfg.arith
     arith = {"auto": pb._abi.ARITH_AUTO, "reference": pb._abi.ARITH_REFERENCE,
@@ -225,7 +255,6 @@ def main():
     tdt = model.torch_dtype()
     x = torch.empty((nin, B), dtype=tdt, device=dev)
     y = torch.empty((nout, B), dtype=tdt, device=dev)
-    col0, _ = shard_range(rank, world, B)
     pb.fill_synthetic(x, configs.INPUT_SEED, col0=col0, dist=cfg.input_dist, lo=cfg.lo, hi=cfg.hi)
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
@@ -263,7 +292,8 @@ def main():
         ms = start.elapsed_time(end)
     clk = clocks.stop()
     ms_step = job_time(ms, world, dev) / args.steps
-    value = world * B / (ms_step / 1e3)
+    total_cols = cfg.batch if args.scaling == "strong" else world * B
+    value = total_cols / (ms_step / 1e3)
 
     # Roofline of the fused kernel (one launch per step), algorithmic FLOPs or bytes.
     pk, pk_src = peaks()
@@ -312,8 +342,8 @@ def main():
         e2e_s = (time.perf_counter() - t0) / args.e2e_steps
         e2e_s = job_time(e2e_s, world, dev)
         esz = x.element_size()
-        e2e = {"value": world * B / e2e_s, "unit": unit, "h2d_bytes_per_step": world * nin * B * esz,
-               "d2h_bytes_per_step": world * nout * B * esz,
+        e2e = {"value": total_cols / e2e_s, "unit": unit, "h2d_bytes_per_step": total_cols * nin * esz,
+               "d2h_bytes_per_step": total_cols * nout * esz,
                "host_link_gbs": {"h2d": nin * B * esz / e2e_s / 1e9, "d2h": nout * B * esz / e2e_s / 1e9,
                                  "note": "per GPU; the copies of one step overlap its kernel chunk by chunk"},
                "path": "ponni_b200_forward_host (C ABI), pinned host buffers, chunked copy/compute overlap"}
@@ -321,7 +351,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample, _ = cpu_reference(cfg)
+        v, cores, sample = cpu_reference(args.config)
         cpu = {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": sample}
 
     upd = param_update_latency(model) if rank == 0 else None
@@ -331,10 +361,11 @@ def main():
     if rank == 0:
         print(json.dumps({
             "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": dtype_name, "data": "synthetic",
-            "config": {"workload": cfg.name, "batch_per_gpu": B, "global_batch": world * B, "nin": nin,
-                       "nout": nout, "parallelism": f"column shards x{world}, no collective",
+            "config": {"workload": cfg.name, "batch_per_gpu": B, "global_batch": total_cols, "nin": nin,
+                       "nout": nout, "parallelism": f"column shards x{world} ({args.scaling} scaling), no collective",
+                       "host_numa_node_rank0": numa,
                        "l2": ("L2 flushed (256 MB write) before each step, outside the timed events" if flush
                               else "inputs larger than L2 (no flush)")},
             "kernel": kernel_name, "arithmetic": arith_name, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps, "clocks": clk,

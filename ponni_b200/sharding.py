@@ -18,6 +18,44 @@ def shard_range(rank: int, world: int, per_rank: int) -> tuple[int, int]:
     return rank * per_rank, per_rank
 
 
+def split_range(rank: int, world: int, total: int) -> tuple[int, int]:
+    """First global column and column count of `rank`'s part of a fixed
+    batch of `total` columns split across `world` ranks (strong scaling):
+    contiguous ranges, the first total % world ranks one column longer."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if total < world:
+        raise ValueError(f"a batch of {total} columns cannot give each of {world} ranks a column")
+    base, rem = divmod(total, world)
+    return rank * base + min(rank, rem), base + (1 if rank < rem else 0)
+
+
+def bind_numa(local_rank: int):
+    """Restrict this process to the CPUs of its GPU's NUMA node (best effort),
+    so that pinned host buffers allocated afterwards are placed on that node
+    (first touch).  Returns the node, or None when it cannot be determined."""
+    import os
+    import subprocess
+    try:
+        bus = subprocess.run(["nvidia-smi", "-i", str(local_rank), "--query-gpu=pci.bus_id",
+                              "--format=csv,noheader"], capture_output=True, text=True, timeout=10).stdout.strip()
+        dom, rest = bus.split(":", 1)
+        path = f"/sys/bus/pci/devices/{dom[-4:].lower()}:{rest.lower()}/numa_node"
+        node = int(open(path).read().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in open(f"/sys/devices/system/node/node{node}/cpulist").read().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return node
+    except Exception:
+        return None
+
+
 def job_time(seconds: float, world: int, device=None) -> float:
     """The job's time: the maximum of every rank's `seconds` (all ranks call)."""
     if world <= 1:

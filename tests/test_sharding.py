@@ -65,6 +65,21 @@ def test_shard_range():
     assert sharding.job_time(1.25, 1) == 1.25
 
 
+def test_split_range_strong_scaling():
+    # a fixed batch split into contiguous ranges that tile it exactly
+    for total in (8, 67_108_864, 134_217_728 + 5, 1001):
+        for world in (1, 2, 4, 8):
+            parts = [sharding.split_range(r, world, total) for r in range(world)]
+            assert parts[0][0] == 0
+            assert all(a[0] + a[1] == b[0] for a, b in zip(parts, parts[1:]))
+            assert parts[-1][0] + parts[-1][1] == total
+            assert max(p[1] for p in parts) - min(p[1] for p in parts) <= 1
+    with pytest.raises(ValueError):
+        sharding.split_range(0, 4, 3)
+    with pytest.raises(ValueError):
+        sharding.split_range(4, 4, 100)
+
+
 def test_two_gloo_ranks_match_one_process(oracle_lib):
     world = 2
     ctx = mp.get_context("spawn")
