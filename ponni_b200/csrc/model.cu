@@ -428,6 +428,19 @@ ponni_b200_status pb_ensure_cuda(ponni_b200_model* m) {
   return PONNI_B200_OK;
 }
 
+ponni_b200_status pb_check_device_error(ponni_b200_model* m) {
+  if (!m->err_dev) return PONNI_B200_OK;
+  int flag = 0;
+  // Plain synchronous copies of one word (no allocation).
+  cudaError_t e = cudaMemcpy(&flag, m->err_dev, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(m, e, "error word read");
+  if (!flag) return PONNI_B200_OK;
+  cudaMemset(m->err_dev, 0, sizeof(int));
+  return pb_fail(m, PONNI_B200_ERR_DEVICE,
+                 "a tensor-core kernel's bounded wait gave up (device error code " + std::to_string(flag) +
+                     "); results are invalid");
+}
+
 // Build (or rebuild after a parameter change) the Program, pick the batch
 // tile and where the parameters live, upload the packed parameters.
 ponni_b200_status pb_plan(ponni_b200_model* m) {
@@ -786,9 +799,10 @@ ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, i
 
 void ponni_b200_model_destroy(ponni_b200_model* m) {
   if (!m) return;
+  DeviceGuard guard(m->device);
   if (m->own_stream || m->packed_dev || m->stage_dev || m->tc_image_dev || m->err_dev || m->prog_dev ||
       m->ts_image_dev || m->scratch_dev || m->pmap_dev.recs || m->pmap_dev.staging) {
-    cudaSetDevice(m->device);
+    DeviceGuard guard(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
     if (m->packed_dev) cudaFree(m->packed_dev);
@@ -819,13 +833,17 @@ ponni_b200_dtype ponni_b200_model_dtype(const ponni_b200_model* m) { return m ? 
 
 void* ponni_b200_model_stream(const ponni_b200_model* m) {
   if (!m) return nullptr;
-  if (!m->stream) pb_ensure_cuda(const_cast<ponni_b200_model*>(m));
+  if (!m->stream) {
+    DeviceGuard guard(m->device);
+    pb_ensure_cuda(const_cast<ponni_b200_model*>(m));
+  }
   return (void*)m->stream;
 }
 
 ponni_b200_status ponni_b200_model_set_stream(ponni_b200_model* m, void* stream) {
   if (!m) return PONNI_B200_ERR_INVALID_ARGUMENT;
   if (!stream) {
+    DeviceGuard guard(m->device);
     ponni_b200_status st = pb_ensure_cuda(m);
     if (st) return st;
   }
@@ -835,20 +853,12 @@ ponni_b200_status ponni_b200_model_set_stream(ponni_b200_model* m, void* stream)
 
 ponni_b200_status ponni_b200_model_synchronize(ponni_b200_model* m) {
   if (!m) return PONNI_B200_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(m->device);
   ponni_b200_status st = pb_ensure_cuda(m);
   if (st) return st;
   cudaError_t e = cudaStreamSynchronize(m->stream);
   if (e != cudaSuccess) return cuda_fail(m, e, "cudaStreamSynchronize");
-  if (m->err_dev) {
-    int flag = 0;
-    e = cudaMemcpy(&flag, m->err_dev, sizeof(int), cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(m, e, "error word read");
-    if (flag) {
-      cudaMemset(m->err_dev, 0, sizeof(int));
-      return pb_fail(m, PONNI_B200_ERR_DEVICE, "a tensor-core wait exceeded its bound; results are invalid");
-    }
-  }
-  return PONNI_B200_OK;
+  return pb_check_device_error(m);
 }
 
 ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int64_t in_ld, void* output,
@@ -859,15 +869,13 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
   if (!input || !output) return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "input/output pointer is NULL");
   if (in_ld < batch || out_ld < batch)
     return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "row stride smaller than the batch size");
+  // Launch on the model's device; the caller's current device is restored.
+  DeviceGuard guard(m->device);
   ponni_b200_status st = pb_plan(m);
   if (st) return st;
   // Reference ensure_internal_state_capacity (src/ponni_Inference.h:197-199).
   if (batch > m->capacity) m->capacity = batch;
   cudaStream_t s = stream ? (cudaStream_t)stream : m->stream;
-  // Launch on the model's device; the caller's current device is restored.
-  int cur = -1;
-  cudaGetDevice(&cur);
-  if (cur != m->device) cudaSetDevice(m->device);
   cudaError_t e;
   if (m->kernel == 2) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
@@ -893,7 +901,6 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
     e = launch_tile_forward((int)m->dtype, m->prog, m->packed_dev, input, in_ld, output, out_ld, batch, grid,
                             m->smem_bytes, s);
   }
-  if (cur >= 0 && cur != m->device) cudaSetDevice(cur);
   if (e != cudaSuccess) return cuda_fail(m, e, "kernel launch");
   return PONNI_B200_OK;
 }
@@ -903,7 +910,7 @@ ponni_b200_status ponni_b200_reallocate_internal_state(ponni_b200_model* m, int6
   if (batch < 0)
     return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "Inference internal-state batch size must be nonnegative");
   if (m->stream) {  // reference fences its execution space first
-    cudaSetDevice(m->device);
+    DeviceGuard guard(m->device);
     cudaStreamSynchronize(m->stream);
   }
   m->capacity = batch;
@@ -945,9 +952,9 @@ ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* m, int arith
 ponni_b200_status ponni_b200_model_device_program(ponni_b200_model* m, const void** program, const void** params,
                                                   int* max_width, int* num_buffers) {
   if (!m || !program || !params) return PONNI_B200_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(m->device);
   ponni_b200_status st = pb_plan(m);
   if (st) return st;
-  cudaSetDevice(m->device);
   cudaError_t e = cudaSuccess;
   if (!m->prog_dev) {
     e = cudaMalloc(&m->prog_dev, sizeof(Program));
@@ -967,6 +974,7 @@ ponni_b200_status ponni_b200_model_device_program(ponni_b200_model* m, const voi
 
 int ponni_b200_model_kernel(ponni_b200_model* m) {
   if (!m) return 0;
+  DeviceGuard guard(m->device);
   return pb_plan(m) == PONNI_B200_OK ? m->kernel : 0;
 }
 
@@ -975,7 +983,7 @@ ponni_b200_status ponni_b200_model_diagnostics(ponni_b200_model* m, uint64_t* ou
   for (int i = 0; i < n; ++i) out[i] = 0;
   if (!m->err_dev) return PONNI_B200_OK;
   uint64_t buf[8];
-  cudaSetDevice(m->device);
+  DeviceGuard guard(m->device);
   cudaError_t e = cudaStreamSynchronize(m->stream);
   if (e == cudaSuccess) e = cudaMemcpy(buf, m->err_dev, 64, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(m, e, "diagnostics read");

@@ -93,11 +93,37 @@ struct ponni_b200_model {
   bool host_params_stale = false;
 };
 
+namespace ponni_b200 {
+// Makes `device` current for the lifetime of the guard and restores the
+// caller's current device afterwards: every C-ABI entry point that touches
+// the GPU holds one, so a multi-GPU application's current device never
+// changes under it.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      cudaGetLastError();
+      prev = -1;
+    }
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) cudaGetLastError();
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+}  // namespace ponni_b200
+
 // Helpers shared by the C ABI translation units.
 ponni_b200_status pb_fail(ponni_b200_model* m, ponni_b200_status s, const std::string& msg);
 ponni_b200_status pb_validate(ponni_b200_model* m);
 ponni_b200_status pb_plan(ponni_b200_model* m);
 ponni_b200_status pb_ensure_cuda(ponni_b200_model* m);
+// After the model's stream has been synchronised: PONNI_B200_ERR_DEVICE (and
+// the word cleared) when a kernel recorded a device-side error, else OK.
+ponni_b200_status pb_check_device_error(ponni_b200_model* m);
 std::string pb_schema_fingerprint(const ponni_b200_model* m);
 ponni_b200_status pb_pull_params(ponni_b200_model* m);
 ponni_b200_status pb_update_params_from_host(ponni_b200_model* m, const void* host, int64_t n);

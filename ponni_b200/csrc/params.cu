@@ -30,17 +30,6 @@ using namespace ponni_b200;
 
 namespace {
 
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int d) {
-    cudaGetDevice(&prev);
-    if (prev != d) cudaSetDevice(d);
-  }
-  ~DeviceGuard() {
-    if (prev >= 0) cudaSetDevice(prev);
-  }
-};
-
 ponni_b200_status cfail(ponni_b200_model* m, cudaError_t e, const char* what) {
   return pb_fail(m, PONNI_B200_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -152,6 +141,7 @@ ponni_b200_status upload_map(ponni_b200_model* m) {
 
 // Plan if needed and make the map resident.
 ponni_b200_status prepare(ponni_b200_model* m) {
+  DeviceGuard g(m->device);
   ponni_b200_status st = pb_plan(m);
   if (st) return st;
   return upload_map(m);

@@ -99,6 +99,7 @@ ponni_b200_status ponni_b200_forward_host(ponni_b200_model* m, const void* input
   if (!input || !output) return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "input/output pointer is NULL");
   if (in_ld < batch || out_ld < batch)
     return pb_fail(m, PONNI_B200_ERR_INVALID_ARGUMENT, "row stride smaller than the batch size");
+  DeviceGuard guard(m->device);
   ponni_b200_status st = pb_plan(m);
   if (st) return st;
   cudaError_t e = cudaSuccess;
@@ -152,7 +153,7 @@ ponni_b200_status ponni_b200_forward_host(ponni_b200_model* m, const void* input
   if (st) return st;
   if (e == cudaSuccess) e = e1 != cudaSuccess ? e1 : e2;
   if (e != cudaSuccess) return cuda_status(m, e, "forward_host");
-  return PONNI_B200_OK;
+  return pb_check_device_error(m);
 }
 
 }  // extern "C"
@@ -173,23 +174,52 @@ namespace {
 constexpr size_t kStaticStageBytes = (size_t)64 << 20;  // 64 MiB per GPU
 static __device__ __align__(256) unsigned char g_static_stage[kStaticStageBytes];
 
-// Device address of g_static_stage, looked up once per device.
+// Device address of g_static_stage, looked up at set-up once per device
+// (with that device current) and kept with the CUDA context it belongs to:
+// if the application has since reset the device (a new primary context),
+// the address is looked up again instead of reusing a stale one.
 constexpr int kMaxDevices = 64;
-void* g_static_stage_ptr[kMaxDevices] = {nullptr};
+struct StageAddress {
+  void* ctx = nullptr;
+  void* ptr = nullptr;
+};
+StageAddress g_static_stage_addr[kMaxDevices];
 std::mutex g_static_stage_mutex;
+
+// The current driver context (cuCtxGetCurrent through the runtime's entry
+// point query, so the library needs no link against the driver library).
+void* current_context() {
+  typedef int (*CtxGetCurrent)(void**);
+  static CtxGetCurrent fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      f = nullptr;
+    }
+    return reinterpret_cast<CtxGetCurrent>(f);
+  }();
+  void* ctx = nullptr;
+  if (fn && fn(&ctx) != 0) ctx = nullptr;
+  return ctx;
+}
 
 cudaError_t static_stage_address(int device, void** out) {
   if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_static_stage_mutex);
-  if (!g_static_stage_ptr[device]) {
+  StageAddress& a = g_static_stage_addr[device];
+  void* ctx = current_context();
+  if (!a.ptr || ctx != a.ctx) {
     // In host code g_static_stage is only a stand-in symbol; the device
     // address comes from the runtime, with the device current.
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_static_stage);
     if (e != cudaSuccess) return e;
-    g_static_stage_ptr[device] = p;
+    a.ptr = p;
+    a.ctx = ctx;
   }
-  *out = g_static_stage_ptr[device];
+  *out = a.ptr;
   return cudaSuccess;
 }
 
@@ -219,24 +249,38 @@ extern "C" ponni_b200_status ponni_b200_forward_host_static(ponni_b200_model* m,
                        std::to_string(kStaticStageBytes / ((size_t)(nin + nout) * esz)) +
                        " columns for this model)");
   }
-  cudaError_t e = cudaSetDevice(m->device);
-  if (e != cudaSuccess) return cuda_status(m, e, "cudaSetDevice");
+  DeviceGuard guard(m->device);
   void* stage = nullptr;
-  e = static_stage_address(m->device, &stage);
+  cudaError_t e = static_stage_address(m->device, &stage);
   if (e != cudaSuccess) return cuda_status(m, e, "cudaGetSymbolAddress(static staging)");
+  // Staging row stride: the batch rounded up to 16 bytes when that fits (the
+  // kernels' 16-byte vector paths need aligned rows), else the batch itself.
+  const int64_t per16 = (int64_t)(16 / esz);
+  int64_t ld = (batch + per16 - 1) / per16 * per16;
+  auto layout_fits = [&](int64_t l, size_t* out_off) {
+    const size_t in_bytes = (size_t)nin * (size_t)l * esz;
+    size_t off = (in_bytes + 255) & ~(size_t)255;
+    if (off + (size_t)nout * (size_t)l * esz > kStaticStageBytes) off = in_bytes;
+    *out_off = off;
+    return off + (size_t)nout * (size_t)l * esz <= kStaticStageBytes;
+  };
+  size_t out_off = 0;
+  if (!layout_fits(ld, &out_off)) {
+    ld = batch;
+    layout_fits(ld, &out_off);
+  }
   unsigned char* din = static_cast<unsigned char*>(stage);
-  unsigned char* dout = din + (((size_t)nin * batch * esz + 255) & ~(size_t)255);
-  if ((size_t)(dout - din) + (size_t)nout * batch * esz > kStaticStageBytes) dout = din + (size_t)nin * batch * esz;
+  unsigned char* dout = din + out_off;
   cudaStream_t s = m->stream;
-  e = cudaMemcpy2DAsync(din, (size_t)batch * esz, input, (size_t)in_ld * esz, (size_t)batch * esz, nin,
+  e = cudaMemcpy2DAsync(din, (size_t)ld * esz, input, (size_t)in_ld * esz, (size_t)batch * esz, nin,
                         cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return cuda_status(m, e, "input copy");
-  ponni_b200_status st = ponni_b200_forward(m, din, batch, dout, batch, batch, s);
+  ponni_b200_status st = ponni_b200_forward(m, din, ld, dout, ld, batch, s);
   if (st) return st;
-  e = cudaMemcpy2DAsync(output, (size_t)out_ld * esz, dout, (size_t)batch * esz, (size_t)batch * esz, nout,
+  e = cudaMemcpy2DAsync(output, (size_t)out_ld * esz, dout, (size_t)ld * esz, (size_t)batch * esz, nout,
                         cudaMemcpyDeviceToHost, s);
   if (e != cudaSuccess) return cuda_status(m, e, "output copy");
   e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return cuda_status(m, e, "forward_host_static");
-  return PONNI_B200_OK;
+  return pb_check_device_error(m);
 }

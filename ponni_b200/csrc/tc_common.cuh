@@ -9,6 +9,35 @@
 
 #include "tc_program.h"
 
+// Bound of every spin-wait of the tensor-core kernels, in SM cycles (about
+// one second).  The wait-bound test build (PONNI_B200_WAIT_TEST) shortens it.
+#ifndef PONNI_B200_WAIT_LIMIT
+#ifdef PONNI_B200_WAIT_TEST
+#define PONNI_B200_WAIT_LIMIT (1ll << 20)
+#else
+#define PONNI_B200_WAIT_LIMIT (1ll << 31)
+#endif
+#endif
+
+// Wait-bound test build only (PONNI_B200_WAIT_TEST, never the default
+// library): each tensor-core translation unit holds a flag that the host
+// sets through ponni_b200_debug_skip_arrive_<kernel>(); a launch that sees it
+// leaves out the completion signal of its first job, so that the waiting role
+// runs into its bound and the kernel reports PONNI_B200_ERR_DEVICE.
+#ifdef PONNI_B200_WAIT_TEST
+#define PONNI_B200_SKIP_ARRIVE_FLAG(kernel)                                                     \
+  namespace {                                                                                   \
+  __device__ int g_skip_arrive;                                                                 \
+  }                                                                                             \
+  extern "C" __attribute__((visibility("default"))) int ponni_b200_debug_skip_arrive_##kernel(int on) { \
+    return (int)cudaMemcpyToSymbol(g_skip_arrive, &on, sizeof(int));                            \
+  }
+#define PONNI_B200_SKIP_ARRIVE() (g_skip_arrive != 0)
+#else
+#define PONNI_B200_SKIP_ARRIVE_FLAG(kernel)
+#define PONNI_B200_SKIP_ARRIVE() false
+#endif
+
 namespace ponni_b200 {
 namespace tc {
 
@@ -44,7 +73,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > (1ll << 31)) return false;
+    if (clock64() - t0 > PONNI_B200_WAIT_LIMIT) return false;
   }
   return true;
 }

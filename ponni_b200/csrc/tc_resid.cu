@@ -51,6 +51,8 @@
 #include "tc_common.cuh"
 #include "tc_resid.h"
 
+PONNI_B200_SKIP_ARRIVE_FLAG(tr)
+
 #ifndef PONNI_B200_TR_DIAG
 #define PONNI_B200_TR_DIAG 0
 #endif
@@ -59,7 +61,7 @@ namespace ponni_b200 {
 namespace {
 using namespace tc;
 
-constexpr long long kWaitCycles = 1ll << 31;
+constexpr long long kWaitCycles = PONNI_B200_WAIT_LIMIT;
 
 // Optional phase timing (compiled only with -DPONNI_B200_TC_PROFILE): each
 // role sums the cycles of its phases and adds them once per CTA to the
@@ -494,6 +496,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     if (lane == 0) {
       uint32_t use = 0, ep0 = 0, ep1 = 0;
       bool ok = true;
+      bool skip = PONNI_B200_SKIP_ARRIVE();  // wait-bound test build: drop the first job's signal
       [[maybe_unused]] long long w_epi = 0, w_full = 0;
       TR_T(t_all);
       // Descriptors as 32-bit halves: start addresses advance in the low half.
@@ -531,7 +534,8 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                    tr_chunk<1>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full) &&
                    tr_chunk<2>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full);
             }
-            if (ok) umma_commit(b_accf + 8u * s);
+            if (ok && !skip) umma_commit(b_accf + 8u * s);
+            skip = false;
           }
         }
       // Drain: every MMA issued has completed before TMEM is freed.

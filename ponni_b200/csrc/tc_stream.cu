@@ -42,11 +42,13 @@
 #include "tc_common.cuh"
 #include "tc_stream.h"
 
+PONNI_B200_SKIP_ARRIVE_FLAG(ts)
+
 namespace ponni_b200 {
 namespace {
 using namespace tc;
 
-constexpr long long kWaitCycles = 1ll << 31;
+constexpr long long kWaitCycles = PONNI_B200_WAIT_LIMIT;
 
 // Optional phase timing (compiled only with -DPONNI_B200_TC_PROFILE): each
 // role sums the cycles of its waits locally and adds them once per CTA to
@@ -308,6 +310,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
       uint32_t use = 0, st_ph[kTsSlots] = {0, 0}, k_ph[kTsSlots] = {0, 0};
       bool has_prev[kTsSlots] = {false, false};
       bool ok = true;
+      bool skip = PONNI_B200_SKIP_ARRIVE();  // wait-bound test build: drop the first job's signal
       long long w_epi = 0, w_full = 0;
       (void)w_epi; (void)w_full;
       TS_T(t_all);
@@ -350,7 +353,8 @@ __global__ void __launch_bounds__(kTsThreads, 1)
               umma_commit(b_empty + 8u * st);
               ++use;
             }
-            if (ok) umma_commit(b_accf + 8u * s);
+            if (ok && !skip) umma_commit(b_accf + 8u * s);
+            skip = false;
           }
       // Drain: every MMA issued has completed before TMEM is freed.
       umma_commit(b_drain);

@@ -1,0 +1,96 @@
+"""The tensor-core kernels' bounded waits end with an error status, and the
+context stays usable.
+
+Every spin-wait of the tcgen05 kernels (mbarrier phases between the weight
+producer, the MMA issuer and the epilogue warps) gives up after a bounded
+number of cycles, raises the CTA's abort flag, drains its copies and MMAs,
+frees its TMEM and records an error word that the host maps to
+PONNI_B200_ERR_DEVICE.  To make a wait run out without faulting anything,
+the test library (libponni_b200_waittest.so, built with
+-DPONNI_B200_WAIT_TEST: wait bound 2^20 cycles and a host-settable flag)
+leaves out the completion signal of the first job of a one-CTA launch.  The
+test then checks, in a child process bound to that library:
+  * ponni_b200_model_synchronize returns PONNI_B200_ERR_DEVICE,
+  * the synchronous host-buffer forward returns it too,
+  * the next normal forward on the same context passes the parity gate,
+for the resident (tc), streamed (ts) and LayerNorm/residual (tr) kernels.
+"""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+WAITTEST_LIB = os.path.join(ROOT, "ponni_b200", "libponni_b200_waittest.so")
+
+CHILD = r'''
+import json, sys
+import numpy as np
+import torch
+import ponni_b200 as pb
+from ponni_b200 import configs
+from oracle import oracle
+from tests import kat_models as K
+
+kind = sys.argv[1]
+cfg, arith, kernel = {
+    "tc": (configs.cfg2(batch=100), None, pb._abi.KERNEL_TENSOR),
+    "ts": (configs.cfg5(batch=100), pb._abi.ARITH_TENSOR, pb._abi.KERNEL_TENSOR_STREAM),
+    "tr": (configs.cfg4(batch=100), None, pb._abi.KERNEL_TENSOR_RESID),
+}[kind]
+lib = pb._abi.lib()
+skip = getattr(lib, "ponni_b200_debug_skip_arrive_" + kind)
+m = pb.Inference(cfg.layers, dtype=cfg.dtype, arithmetic=arith)
+assert m.kernel() == kernel
+x = configs.host_inputs(cfg, cfg.batch)
+xd = torch.from_numpy(np.ascontiguousarray(x).view(np.int16) if cfg.dtype == pb.BF16 else x).cuda()
+if cfg.dtype == pb.BF16:
+    xd = xd.view(torch.bfloat16)
+res = {}
+assert skip(1) == 0
+m.forward_batch_parallel(xd)
+res["sync_status"] = lib.ponni_b200_model_synchronize(m._m)
+res["sync_message"] = lib.ponni_b200_last_error(m._m).decode()
+try:
+    m.forward_batch_parallel(np.ascontiguousarray(x))  # host buffers: ponni_b200_forward_host
+    res["host_status"] = 0
+except pb.PonniError as e:
+    res["host_status"] = e.status
+assert skip(0) == 0
+y = m.forward_batch_parallel(xd)
+res["after_status"] = lib.ponni_b200_model_synchronize(m._m)
+torch.cuda.synchronize()
+if cfg.dtype == pb.BF16:
+    yv = K.as_float(y.view(torch.int16).cpu().numpy().view(np.uint16), cfg.dtype)
+    ref = K.as_float(oracle.forward(cfg.layers, cfg.dtype, x, acc32=True), cfg.dtype)
+    res["after_err"] = K.normwise_err(yv, ref)
+    res["tol"] = 1.6e-2
+else:
+    res["after_err"] = K.normwise_err(y.cpu().numpy(), oracle.forward(cfg.layers, cfg.dtype, x))
+    res["tol"] = 1e-5
+yh = m.forward_batch_parallel(np.ascontiguousarray(x))
+res["after_host_ok"] = bool(np.all(np.isfinite(K.as_float(yh, cfg.dtype))))
+print("RESULT " + json.dumps(res))
+'''
+
+
+@pytest.mark.parametrize("kind", ["tc", "ts", "tr"])
+def test_bounded_wait_reports_device_error_and_context_survives(kind):
+    if not os.path.exists(WAITTEST_LIB):
+        pytest.fail("libponni_b200_waittest.so is missing: run __graft_entry__.build()")
+    env = dict(os.environ, PONNI_B200_LIB=WAITTEST_LIB, PYTHONPATH=ROOT)
+    p = subprocess.run([sys.executable, "-c", CHILD, kind], cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=300)
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("RESULT ")]
+    assert p.returncode == 0 and lines, p.stdout[-2000:] + p.stderr[-2000:]
+    r = json.loads(lines[-1][len("RESULT "):])
+    assert r["sync_status"] == 7, r  # PONNI_B200_ERR_DEVICE
+    assert "bounded wait" in r["sync_message"], r
+    assert r["host_status"] == 7, r
+    assert r["after_status"] == 0, r
+    assert r["after_err"] <= r["tol"], r
+    assert r["after_host_ok"], r

@@ -63,3 +63,42 @@ def test_static_forward_rejects_oversize_and_unprepared():
     msg = pb._abi.lib().ponni_b200_last_error(model._m).decode()
     assert st == 1  # PONNI_B200_ERR_INVALID_ARGUMENT
     assert "static staging buffer" in msg
+
+
+def test_static_forward_allocates_nothing(oracle_lib):
+    """A freshly prepared model's first allocation-free calls leave the
+    device's free memory unchanged (no staging buffer is created; the static
+    array itself is loaded with the library's module before the check)."""
+    torch = pytest.importorskip("torch")
+    cfg = configs.cfg2(batch=100_003)
+    warm = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    warm.kernel()
+    x = np.ascontiguousarray(configs.host_inputs(cfg, cfg.batch))
+    assert _static_forward(warm, x, 10)[0] == 0  # loads the module holding the static array
+    model = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    model.kernel()  # prepares (allocates parameters) before the measurement
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(0)[0]
+    for _ in range(2):
+        st, y = _static_forward(model, x, 10)
+        assert st == 0, pb._abi.lib().ponni_b200_last_error(model._m).decode()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(0)[0] == free0
+    ref = oracle_lib.forward(cfg.layers, cfg.dtype, x)
+    check_y = K.normwise_err(y, ref)
+    assert check_y <= 1e-5
+
+
+def test_static_forward_at_the_size_limit(oracle_lib):
+    """A batch within a few bytes of the 64 MiB staging limit: the output is
+    staged right after the input (no alignment padding fits), with the
+    unpadded row stride; the result still matches the oracle, twice."""
+    cfg = configs.cfg1(batch=64 * 1024 * 1024 // 12)  # 2 inputs + 1 output, fp32: 12 bytes per column
+    model = pb.Inference(cfg.layers, dtype=cfg.dtype)
+    model.kernel()
+    x = np.ascontiguousarray(configs.host_inputs(cfg, cfg.batch))
+    ref = oracle_lib.forward(cfg.layers, cfg.dtype, x)
+    for _ in range(2):
+        st, y = _static_forward(model, x, 1)
+        assert st == 0, pb._abi.lib().ponni_b200_last_error(model._m).decode()
+        assert K.normwise_err(y, ref) <= 1e-5
