@@ -270,3 +270,28 @@ def test_narrow_jit_weights_change_reuses_kernel(oracle_lib):
         assert pb.Inference(net).kernel() == pb._abi.KERNEL_NARROW_JIT
         x = pb.to_dtype_bytes(rng.normal(0, 1, (2, 5000)), pb.F32)
         check(run_device(net, pb.F32, x), oracle_lib.forward(net, pb.F32, x), pb.F32, net, x)
+
+
+def test_caller_device_is_restored(oracle_lib):
+    """Every entry point runs on the model's device and leaves the caller's
+    current device as it found it (one-process multi-GPU applications)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    torch.cuda.set_device(0)
+    for cfg in (configs.cfg4(batch=300), configs.cfg1(batch=300)):
+        m = pb.Inference(cfg.layers, dtype=cfg.dtype, device=1)
+        assert m.kernel() > 0
+        assert torch.cuda.current_device() == 0
+        x = configs.host_inputs(cfg, cfg.batch)
+        y = m.forward_batch_parallel(torch.from_numpy(x).to("cuda:1"))
+        m.synchronize()
+        assert torch.cuda.current_device() == 0
+        yh = m.forward_batch_parallel(x)  # host buffers
+        assert torch.cuda.current_device() == 0
+        m.set_trainable_parameters(m.get_trainable_parameters())
+        assert torch.cuda.current_device() == 0
+        ref = oracle_lib.forward(cfg.layers, cfg.dtype, x)
+        check(y.cpu().numpy(), ref, cfg.dtype, cfg.layers, x)
+        check(yh, ref, cfg.dtype, cfg.layers, x)
+        del m
+        assert torch.cuda.current_device() == 0
