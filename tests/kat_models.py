@@ -161,27 +161,53 @@ def normwise_err(y, ref) -> float:
     return float(np.max(num / den))
 
 
+def rel_err_q(y, ref, q) -> float:
+    """q-quantile over elements of |y - ref| / max(|ref|, 1e-3 * rms(ref))."""
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    if ref.size == 0:
+        return 0.0
+    floor = 1e-3 * np.sqrt(np.mean(ref * ref)) + 1e-300
+    return float(np.quantile(np.abs(y - ref) / np.maximum(np.abs(ref), floor), q))
+
+
 def fp_parity(y, ref32, ref64, tol=1e-5):
     """The fp32 parity gate.
 
     * normwise per output feature: max|y - ref| / max|ref| <= tol against the
-      oracle in the model dtype (the reference's own arithmetic order), and
-    * accuracy no worse than the reference's: rms|y - exact| <=
-      2 * rms|ref - exact| + tol * 1e-3 * rms|exact|, where `exact` is the
-      same network in float64 (checked when there are >= 256 outputs, so that
-      the rms is a stable statistic).
-    The GPU contracts a*b+c into one FMA where the reference's CPU build
-    rounds twice, so elementwise agreement is limited by the cancellation in
-    each dot product; both checks are insensitive to that while still catching
-    any wrong index, weight or layer.
-    Returns (normwise error, accuracy ratio or 0 when not checked)."""
+      oracle in the model dtype (the reference's own arithmetic order);
+    * elementwise accuracy comparable to the reference's, on the floored
+      elementwise relative error against the same network in float64
+      (err_i = |y_i - exact_i| / max(|exact_i|, 1e-3 rms(exact))): the
+      99th percentile at most 1.5x the reference's (and tol), the maximum
+      at most 4x the reference's maximum (and tol).  The maximum of a few
+      thousand near-zero outputs is set by a handful of cancellations, so
+      two equally accurate evaluations differ there by a factor of ~2-3 at
+      random (measured: 1.0-2.7 across the GPU kernels), and the 99.9th
+      percentile still by up to 1.45x (the narrow kernels' fused
+      multiply-adds); the 99th percentile is the stable statistic.  With
+      fewer than 1000 outputs only the maximum is used;
+    * rms accuracy no worse than the reference's: rms|y - exact| <=
+      rms|ref - exact| + tol * 1e-3 * rms|exact| (checked when there are
+      >= 256 outputs, so that the rms is a stable statistic).
+    Elementwise agreement with the oracle itself is not a usable gate in fp32:
+    near-zero outputs come out of cancellation, so two correct fp32
+    evaluations in different orders (the GPU fuses a*b+c and sums on tensor
+    cores) differ there by several units of the partial sums -- the
+    reference's own elementwise error against float64 is 5e-4 (cfg2) and
+    7e-4 (cfg4) at this floor.
+    Returns (normwise error, rms accuracy ratio or 0 when not checked,
+    elementwise accuracy ratio: the larger of the two ratios to their bounds)."""
     y, r, e = (np.asarray(a, dtype=np.float64) for a in (y, ref32, ref64))
     nw = normwise_err(y, r)
+    el_ratio = rel_err(y, e) / (4.0 * max(rel_err(r, e), tol))
+    if y.size >= 1000:
+        el_ratio = max(el_ratio, rel_err_q(y, e, 0.99) / (1.5 * max(rel_err_q(r, e, 0.99), tol)))
     if y.size < 256:
-        return nw, 0.0
+        return nw, 0.0, el_ratio
     rms = lambda a: float(np.sqrt(np.mean(a * a)))  # noqa: E731
-    ratio = rms(y - e) / (2 * rms(r - e) + tol * 1e-3 * rms(e) + 1e-300)
-    return nw, ratio
+    ratio = rms(y - e) / (rms(r - e) + tol * 1e-3 * rms(e) + 1e-300)
+    return nw, ratio, el_ratio
 
 
 def as_float(raw, dtype):

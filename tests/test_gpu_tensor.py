@@ -1,14 +1,19 @@
-"""GPU parity of the tensor-core (tcgen05) dense-chain kernel.
+"""GPU parity of the tensor-core (tcgen05) kernels.
 
 fp32 models run on an exact three-way bf16 split of every operand and must
 pass the fp32 gate of the tile kernel (normwise <= 1e-5 against the oracle,
-accuracy no worse than the reference's); fp16/bf16 models accumulate in fp32
-and are checked against the oracle's fp32-accumulation mode with a normwise
-tolerance of four units in the last place of the storage type (fp16: 2e-3,
-bf16: 1.6e-2 -- the tensor core sums in a different order, so a state value
-can land one storage ulp away and carry that through the next layers), and
-must be at least as accurate as the reference's per-operation-rounded
-arithmetic.
+elementwise and rms accuracy no worse than the reference's).  fp16/bf16
+models in the fp32-accumulation mode are checked against the oracle's
+fp32-accumulation mode with a normwise tolerance of two (fp16: 2e-3) or three
+(bf16: 1.2e-2) units in the last place of the storage type (measured at 4099
+columns: cfg3 fp16 5.8e-4, cfg5 bf16 5.2e-3, the odd-width bf16 chain of
+test_ts_odd_widths_all_activations 8.7e-3 -- the tensor core sums in a different
+order, so a state value can land one storage ulp away and carry that through
+the next layers), and must be at least as accurate against float64 as the
+reference's per-operation-rounded half arithmetic (normwise and rms, no
+slack).  The reference's own bf16 arithmetic is about 7e-2 (normwise) from
+the exact result on cfg5, so agreement with it to 2e-3 is not attainable by
+a more accurate evaluation; the accuracy gate replaces it.
 """
 import numpy as np
 import pytest
@@ -37,10 +42,12 @@ def check_acc32(y_raw, layers, dtype, x_raw, oracle_lib):
     a32 = K.as_float(oracle_lib.forward(layers, dtype, x_raw, acc32=True), dtype)
     ref = K.as_float(oracle_lib.forward(layers, dtype, x_raw), dtype)
     exact = oracle_lib.forward(layers, pb.F64, K.as_float(x_raw, dtype))
-    tol = {pb.F16: 2e-3, pb.BF16: 1.6e-2}[dtype]
+    tol = {pb.F16: 2e-3, pb.BF16: 1.2e-2}[dtype]
     nw = K.normwise_err(y, a32)
     assert nw <= tol, f"normwise vs fp32-accumulation oracle {nw:.3e}"
-    assert K.normwise_err(y, exact) <= K.normwise_err(ref, exact) + 2e-3
+    assert K.normwise_err(y, exact) <= K.normwise_err(ref, exact), "normwise accuracy worse than the reference's"
+    rms = lambda a: float(np.sqrt(np.mean(np.asarray(a, np.float64) ** 2)))  # noqa: E731
+    assert rms(y - exact) <= rms(ref - exact), "rms accuracy worse than the reference's"
 
 
 def test_tc_smallest_case(oracle_lib):
