@@ -96,10 +96,14 @@ template <class T, int MAXW, int NBUF = ponni_b200::kMaxBuffers>
 __device__ void infer_one(const Model& m, const T* x, int64_t x_stride, T* y, int64_t y_stride) {
   using namespace ponni_b200;
   using detail::C;
+  using detail::add_rn;
+  using detail::div_rn;
+  using detail::mul_rn;
   using detail::radd;
   using detail::rdiv;
   using detail::rmul;
   using detail::rsub;
+  using detail::sub_rn;
   const Program& p = *m.program;
   const T* params = static_cast<const T*>(m.params);
   C<T> buf[NBUF][MAXW];
@@ -134,6 +138,22 @@ __device__ void infer_one(const Model& m, const T* x, int64_t x_stride, T* y, in
         break;
       case STEP_LAYERNORM: {  // src/layers/ponni_LayerNorm.h:77-99
         const int n = s.nin;
+        if (s.flags & LN_WELFORD) {  // generated LayerNormalization, emitter.py:867-889, :1161-1191
+          C<T> mean = C<T>(0), m2 = C<T>(0);
+          for (int i = 0; i < n; ++i) {
+            const C<T> value = buf[src][i];
+            const C<T> delta = sub_rn(value, mean);
+            mean = add_rn(mean, div_rn(delta, (C<T>)(i + 1)));
+            m2 = add_rn(m2, mul_rn(delta, sub_rn(value, mean)));
+          }
+          const C<T> inv = rnd<T>(div_rn(C<T>(1), m_sqrt(add_rn(div_rn(m2, (C<T>)n), (C<T>)s.s0))));
+          mean = rnd<T>(mean);
+          for (int i = 0; i < n; ++i) {
+            const C<T> v = rmul<T>(rsub<T>(buf[src][i], mean), inv);
+            buf[src][i] = radd<T>(rmul<T>(v, Num<T>::to_c(params[s.w_off + i])), Num<T>::to_c(params[s.b_off + i]));
+          }
+          break;
+        }
         C<T> mean = C<T>(0);
         for (int i = 0; i < n; ++i) mean = radd<T>(mean, buf[src][i]);
         mean = rdiv<T>(mean, (C<T>)n);

@@ -120,6 +120,7 @@ float ponni_oracle_round_bf16(float v) { return round_bf16(v); }
 typedef struct {
   int kind, nin, nout, save_index, aux, flags;
   double s[3];
+  double s_raw[3]; /* the scalars as given (generated 16-bit LayerNorm: epsilon in float) */
   double* pd; /* parameters as double (exact copies of the model-dtype values) */
 } OLayer;
 
@@ -216,6 +217,31 @@ typedef struct {
           for (int f = 0; f < n; ++f) cur[f] = rnd_##SUF(mode, cur[f] + (T)y->pd[f]);                      \
           break;                                                                                           \
         case PONNI_B200_LAYER_NORM: {                                                                      \
+          if (gen) {                                                                                       \
+            /* generated LayerNormalization (emitter.py:867-889; 16-bit: :1161-1191): Welford */          \
+            /* mean / second moment in Scalar (float for 16-bit models, which round the mean */           \
+            /* and 1/stddev to the model type once), then ((x - mean) * inv) * scale + bias */            \
+            const int half = smode == PONNI_B200_F16 || smode == PONNI_B200_BF16;                         \
+            const int wm = half ? -1 : mode;                                                               \
+            T mean = 0, m2 = 0;                                                                            \
+            for (int i = 0; i < n; ++i) {                                                                  \
+              const T value = cur[i];                                                                      \
+              const T delta = rnd_##SUF(wm, value - mean);                                                 \
+              mean = rnd_##SUF(wm, mean + rnd_##SUF(wm, delta / (T)(i + 1)));                             \
+              m2 = rnd_##SUF(wm, m2 + rnd_##SUF(wm, delta * rnd_##SUF(wm, value - mean)));                 \
+            }                                                                                              \
+            const T eps = half ? (T)(float)y->s_raw[0] : (T)y->s[0];                                       \
+            const T var = rnd_##SUF(wm, m2 / (T)n);                                                        \
+            T inv = rnd_##SUF(wm, (T)1 / rnd_##SUF(wm, SQRT(rnd_##SUF(wm, var + eps))));                  \
+            mean = rnd_##SUF(mode, mean);                                                                  \
+            inv = rnd_##SUF(mode, inv);                                                                    \
+            for (int i = 0; i < n; ++i) {                                                                  \
+              T v = rnd_##SUF(mode, rnd_##SUF(mode, cur[i] - mean) * inv);                                 \
+              v = rnd_##SUF(mode, v * (T)y->pd[i]);                                                        \
+              cur[i] = rnd_##SUF(mode, v + (T)y->pd[n + i]);                                               \
+            }                                                                                              \
+            break;                                                                                         \
+          }                                                                                                \
           T mean = 0, var = 0;                                                                             \
           for (int i = 0; i < n; ++i) mean = rnd_##SUF(mode, mean + cur[i]);                               \
           mean = rnd_##SUF(mode, mean / (T)n);                                                             \
@@ -364,7 +390,10 @@ int ponni_oracle_forward_ex(const ponni_b200_layer_desc* layers, int n_layers, i
     L[i].save_index = d->save_index;
     L[i].aux = d->aux;
     L[i].flags = d->flags;
-    for (int k = 0; k < 3; ++k) L[i].s[k] = round_scalar(dtype, d->scalar[k]);
+    for (int k = 0; k < 3; ++k) {
+      L[i].s[k] = round_scalar(dtype, d->scalar[k]);
+      L[i].s_raw[k] = d->scalar[k];
+    }
     size_t np = n_params(d);
     L[i].pd = (double*)malloc(sizeof(double) * (np ? np : 1));
     for (size_t k = 0; k < np; ++k) L[i].pd[k] = load_elem(dtype, d->params, k);

@@ -11,6 +11,7 @@ from .layers import (Layer, Matvec, Bias, Relu, ReLU, LeakyRelu, LeakyReLU, Elu,
                      MinMaxNorm, Softmax, LogSoftmax, Save_State, Binop_Add, Binop_Concatenate,
                      Binop_Projection_Add)
 from .generated import Dense, GeneratedModel
+from .generated import LayerNorm as GeneratedLayerNorm
 from .inference import (Inference, create_inference_model, create_inference_model_single_precision,
                         create_inference_model_double_precision, create_inference_model_half_precision,
                         create_inference_model_bhalf_precision, build_descriptors, to_dtype_bytes,

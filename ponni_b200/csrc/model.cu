@@ -337,6 +337,13 @@ struct Planner {
           s.nin = s.nout = d.num_inputs;
           s.src = cur;
           s.s0 = d.scalar[0];
+          if (m->arithmetic == PONNI_B200_ARITH_GENERATED) {
+            // The generated model's LayerNormalization (emitter.py:867-889):
+            // Welford; 16-bit models run it in float with a float epsilon
+            // (emitter.py:1161-1191).
+            s.flags |= LN_WELFORD;
+            if (m->dtype == PONNI_B200_F16 || m->dtype == PONNI_B200_BF16) s.s0 = (double)(float)Ly.raw_scalar[0];
+          }
           s.w_off = append(Ly.params.data(), d.num_inputs);
           s.b_off = append(Ly.params.data() + (size_t)d.num_inputs * esz, d.num_inputs);
           break;
@@ -776,7 +783,10 @@ ponni_b200_status ponni_b200_model_create(const ponni_b200_layer_desc* layers, i
     Layer L;
     L.d = layers[i];
     L.d.params = nullptr;
-    for (int k = 0; k < 3; ++k) L.d.scalar[k] = round_to_dtype(dtype, layers[i].scalar[k]);
+    for (int k = 0; k < 3; ++k) {
+      L.d.scalar[k] = round_to_dtype(dtype, layers[i].scalar[k]);
+      L.raw_scalar[k] = layers[i].scalar[k];
+    }
     int64_t n = L.num_params();
     if (n < 0 || (n > 0 && (L.d.num_inputs <= 0 || L.d.num_outputs <= 0 ||
                             (L.d.kind == PONNI_B200_BINOP_PROJECTION_ADD && L.d.aux <= 0))))

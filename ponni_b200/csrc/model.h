@@ -18,6 +18,7 @@ namespace ponni_b200 {
 
 struct Layer {
   ponni_b200_layer_desc d;            // params pointer cleared; data lives in `params`
+  double raw_scalar[3] = {0, 0, 0};   // the scalars as given (d.scalar is rounded to the model dtype)
   std::vector<unsigned char> params;  // canonical parameters, model dtype
   int64_t num_params() const;         // all parameters the layer owns (elements)
   int64_t num_trainable() const;      // reference get_num_trainable_parameters()

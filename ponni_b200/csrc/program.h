@@ -42,6 +42,7 @@ constexpr int32_t DENSE_TO_GLOBAL = 0x4;    // final block: write the caller's o
 constexpr int32_t DENSE_FAST_EPI = 0x8;     // epilogue is [Bias?][activation?]: fast path
 constexpr int32_t DENSE_HALF_FMA = 0x10;    // 16-bit: one fused multiply-add per product (generated arithmetic)
 constexpr int32_t CONCAT_AFTER = 0x4;
+constexpr int32_t LN_WELFORD = 0x20;        // LayerNorm of the generated model (Welford; 16-bit: in float)
 
 struct EpiDesc {
   int32_t kind;

@@ -377,6 +377,30 @@ __device__ void layernorm_step(const StepDesc& s, int bt, const T* params, T* x)
   const C eps = (C)s.s0;
   const T* gamma = params + s.w_off;
   const T* beta = params + s.b_off;
+  if (s.flags & LN_WELFORD) {
+    // Generated LayerNormalization (src/generator/kokkos_nn/emitter.py:867-889):
+    // one Welford pass in Scalar (16-bit models: in float, emitter.py:1161-1191,
+    // the mean and 1/stddev rounded once to the model type), then
+    // ((x - mean) * inv) * scale + bias with every operation rounded.
+    for (int c = threadIdx.x; c < bt; c += kThreads) {
+      C mean = C(0), m2 = C(0);
+      for (int i = 0; i < n; ++i) {
+        const C value = Num<T>::to_c(x[i * bt + c]);
+        const C delta = sub_rn(value, mean);
+        mean = add_rn(mean, div_rn(delta, (C)(i + 1)));
+        m2 = add_rn(m2, mul_rn(delta, sub_rn(value, mean)));
+      }
+      const C var = div_rn(m2, (C)n);
+      const C inv = rnd<T>(div_rn(C(1), m_sqrt(add_rn(var, eps))));
+      mean = rnd<T>(mean);
+      for (int i = 0; i < n; ++i) {
+        C v = rmul<T>(rsub<T>(Num<T>::to_c(x[i * bt + c]), mean), inv);
+        v = radd<T>(rmul<T>(v, Num<T>::to_c(gamma[i])), Num<T>::to_c(beta[i]));
+        x[i * bt + c] = Num<T>::from_c(v);
+      }
+    }
+    return;
+  }
   for (int c = threadIdx.x; c < bt; c += kThreads) {
     C mean = C(0);
     for (int i = 0; i < n; ++i) mean = radd<T>(mean, Num<T>::to_c(x[i * bt + c]));

@@ -13,10 +13,18 @@ ARITH_GENERATED:
   and accumulates with one fused multiply-add per product
   (TwoHalf::fma, emitter.py:975-983).
 
+* LayerNormalization nodes run one Welford pass for the mean and second
+  moment (emitter.py:867-889; the half2 path in float, :1161-1191) and
+  output ((x - mean) * inv_stddev) * scale + bias.
+
 The ONNX import and graph compiler of the generator are not rebuilt: a model
-is given as a list of ``Dense`` layers (the fused DenseBiasActivation nodes
-the generator produces for MLPs).  Named weights load from a .ponni file as
-``<name>.weight`` [out, in] and ``<name>.bias`` [out].
+is given as the list of nodes the generator's passes produce for MLPs and
+residual MLPs: ``Dense`` (Dense / DenseBiasActivation, and
+DenseResidualActivation when it names a ``residual`` tensor: activation(W x +
+b + residual), emitter.py:726-729) and ``LayerNorm`` (LayerNormalization).
+A residual names an earlier node's output, or "input".  Named weights load
+from a .ponni file as ``<name>.weight`` [out, in] and ``<name>.bias`` [out]
+(LayerNorm: ``<name>.scale`` and ``<name>.bias``).
 """
 from __future__ import annotations
 
@@ -48,12 +56,27 @@ _ACT = {
 
 @dataclass
 class Dense:
-    """One fused dense node: y = activation(bias + W x), W[out, in]."""
+    """One fused dense node: y = activation(bias + W x [+ residual]), W[out, in]."""
     name: str
     weight: np.ndarray
     bias: np.ndarray | None = None
     activation: str | None = None
     alpha: float = 0.01  # LeakyReLU slope / ELU alpha
+    residual: str | None = None  # DenseResidualActivation: name of an earlier node, or "input"
+
+    @property
+    def width_in(self) -> int:
+        return self.weight.shape[1]
+
+    @property
+    def width_out(self) -> int:
+        return self.weight.shape[0]
+
+    def tensors(self):
+        out = [("weight", self.weight)]
+        if self.bias is not None:
+            out.append(("bias", self.bias))
+        return out
 
     def __post_init__(self):
         self.weight = np.asarray(self.weight, dtype=np.float64)
@@ -65,6 +88,32 @@ class Dense:
                 raise ValueError(f"{self.name}: bias size differs from the output width")
         if self.activation not in _ACT:
             raise ValueError(f"{self.name}: unsupported activation {self.activation!r}")
+
+
+@dataclass
+class LayerNorm:
+    """One LayerNormalization node over the feature vector: scale and bias [n]."""
+    name: str
+    scale: np.ndarray
+    bias: np.ndarray
+    epsilon: float = 1e-5
+
+    def __post_init__(self):
+        self.scale = np.asarray(self.scale, dtype=np.float64).reshape(-1)
+        self.bias = np.asarray(self.bias, dtype=np.float64).reshape(-1)
+        if self.scale.size != self.bias.size:
+            raise ValueError(f"{self.name}: scale and bias sizes differ")
+
+    @property
+    def width_in(self) -> int:
+        return self.scale.size
+
+    @property
+    def width_out(self) -> int:
+        return self.scale.size
+
+    def tensors(self):
+        return [("scale", self.scale), ("bias", self.bias)]
 
 
 def _read_tensor(path: str, name: str) -> np.ndarray:
@@ -87,39 +136,71 @@ def _read_tensor(path: str, name: str) -> np.ndarray:
 class GeneratedModel:
     """Mirror of the generated model struct (``Scalar`` = float or double)."""
 
-    def __init__(self, dense: list[Dense], scalar=np.float32, device: int = 0):
+    def __init__(self, dense: list, scalar=np.float32, device: int = 0):
         if not dense:
-            raise ValueError("a generated model needs at least one dense layer")
+            raise ValueError("a generated model needs at least one node")
+        names = {"input"}
         for a, b in zip(dense, dense[1:]):
-            if a.weight.shape[0] != b.weight.shape[1]:
+            if a.width_out != b.width_in:
                 raise ValueError(f"{a.name} -> {b.name}: width mismatch")
-        self.dense = list(dense)
+        widths = {"input": dense[0].width_in}
+        for n in dense:
+            if n.name in names:
+                raise ValueError(f"node name {n.name!r} used twice")
+            if isinstance(n, Dense) and n.residual is not None:
+                if n.residual not in names:
+                    raise ValueError(f"{n.name}: residual {n.residual!r} is not an earlier node or the input")
+                if widths[n.residual] != n.width_out:
+                    raise ValueError(f"{n.name}: residual {n.residual!r} has width {widths[n.residual]}, "
+                                     f"the node {n.width_out}")
+            names.add(n.name)
+            widths[n.name] = n.width_out
+        self.dense = list(dense)  # the nodes, in order (Dense and LayerNorm)
         self.scalar = np.dtype(scalar)
         if self.scalar not in (np.dtype(np.float32), np.dtype(np.float64)):
             raise ValueError("GeneratedModel Scalar must be float or double")
         self.device = device
-        self.num_inputs = self.dense[0].weight.shape[1]
-        self.num_outputs = self.dense[-1].weight.shape[0]
+        self.num_inputs = self.dense[0].width_in
+        self.num_outputs = self.dense[-1].width_out
         self._models: dict[int, Inference] = {}
 
     # -- parameters (emitter.py:1724-1895) --
     @staticmethod
     def _layer_list(dense, rnd=lambda a: a):
+        """Lower the nodes to the template layer tuple: residual sources are
+        saved (Save_State) where they are produced and added (Binop_Add)
+        after the bias, before the activation."""
+        sources = [n.residual for n in dense if isinstance(n, Dense) and n.residual is not None]
+        slot = {name: i for i, name in enumerate(dict.fromkeys(sources))}
         out = []
+        if "input" in slot:
+            out.append(L.Save_State(dense[0].width_in, slot["input"]))
         for d in dense:
-            out.append(L.Matvec(rnd(d.weight).T))
-            if d.bias is not None:
-                out.append(L.Bias(rnd(d.bias)))
-            if d.activation is not None:
-                out.append(_ACT[d.activation](d.weight.shape[0], d.alpha))
+            if isinstance(d, LayerNorm):
+                out.append(L.LayerNorm(rnd(d.scale), rnd(d.bias), d.epsilon))
+            else:
+                out.append(L.Matvec(rnd(d.weight).T))
+                if d.bias is not None:
+                    out.append(L.Bias(rnd(d.bias)))
+                if d.residual is not None:
+                    out.append(L.Binop_Add(d.width_out, slot[d.residual]))
+                if d.activation is not None:
+                    out.append(_ACT[d.activation](d.weight.shape[0], d.alpha))
+            if d.name in slot:
+                out.append(L.Save_State(d.width_out, slot[d.name]))
         return out
 
     def _trainable_order(self) -> np.ndarray:
         """Index of each trainable value (Inference tuple order: Matvec W[in][out],
-        then the bias) in the generated order (W[out, in], then the bias)."""
+        then the bias; LayerNorm gamma then beta) in the generated order
+        (W[out, in], then the bias; scale then bias)."""
         if getattr(self, "_perm", None) is None:
             parts, g = [], 0
             for d in self.dense:
+                if isinstance(d, LayerNorm):
+                    parts.append(g + np.arange(2 * d.scale.size, dtype=np.int64))
+                    g += 2 * d.scale.size
+                    continue
                 o, i = d.weight.shape
                 parts.append(g + np.arange(o * i, dtype=np.int64).reshape(o, i).T.reshape(-1))
                 g += o * i
@@ -130,17 +211,13 @@ class GeneratedModel:
         return self._perm
 
     def get_num_parameters(self) -> int:
-        return int(sum(d.weight.size + (d.bias.size if d.bias is not None else 0) for d in self.dense))
+        return int(sum(t.size for d in self.dense for _, t in d.tensors()))
 
     def get_parameters(self) -> np.ndarray:
-        """Learned parameters in layer order: W[out, in] row-major, then the bias."""
+        """Learned parameters in node order: W[out, in] row-major, then the
+        bias (LayerNorm: scale, then bias)."""
         self._pull_dense()
-        parts = []
-        for d in self.dense:
-            parts.append(d.weight.reshape(-1))
-            if d.bias is not None:
-                parts.append(d.bias)
-        return np.concatenate(parts).astype(self.scalar)
+        return np.concatenate([t.reshape(-1) for d in self.dense for _, t in d.tensors()]).astype(self.scalar)
 
     def set_parameters(self, values) -> None:
         v = np.asarray(values, dtype=np.float64).reshape(-1)
@@ -168,12 +245,9 @@ class GeneratedModel:
     def _set_dense(self, v):
         off = 0
         for d in self.dense:
-            n = d.weight.size
-            d.weight = v[off:off + n].reshape(d.weight.shape).copy()
-            off += n
-            if d.bias is not None:
-                d.bias = v[off:off + d.bias.size].copy()
-                off += d.bias.size
+            for attr, t in d.tensors():
+                setattr(d, attr, v[off:off + t.size].reshape(t.shape).copy())
+                off += t.size
 
     def _scalar_dtype(self) -> int:
         return _abi.F32 if self.scalar == np.float32 else _abi.F64
@@ -242,14 +316,14 @@ class GeneratedModel:
                                 scalar.get_trainable_parameters_device(torch.float16)))
 
     def load_weights(self, path: str) -> None:
-        """Named tensors <name>.weight [out, in] and <name>.bias of a .ponni file."""
+        """Named tensors <name>.weight [out, in] and <name>.bias (LayerNorm:
+        <name>.scale and <name>.bias) of a .ponni file."""
         for d in self.dense:
-            w = _read_tensor(path, f"{d.name}.weight").astype(np.float64)
-            if w.shape != d.weight.shape:
-                raise _abi.PonniError(2, f"{d.name}.weight has shape {w.shape}, expected {d.weight.shape}")
-            d.weight = w
-            if d.bias is not None:
-                d.bias = _read_tensor(path, f"{d.name}.bias").astype(np.float64).reshape(-1)
+            for attr, t in d.tensors():
+                v = _read_tensor(path, f"{d.name}.{attr}").astype(np.float64)
+                if v.size != t.size or (attr == "weight" and v.shape != t.shape):
+                    raise _abi.PonniError(2, f"{d.name}.{attr} has shape {v.shape}, expected {t.shape}")
+                setattr(d, attr, v.reshape(t.shape))
         self._dense_stale = False
         self._push_host()
 

@@ -31,8 +31,8 @@ def embedded():
     return f
 
 
-def run_embedded(fn, layers, dtype, x_raw):
-    m = pb.Inference(layers, dtype=dtype)
+def run_embedded(fn, layers, dtype, x_raw, arithmetic=None):
+    m = pb.Inference(layers, dtype=dtype, arithmetic=arithmetic)
     x = to_torch(x_raw, dtype).cuda()
     y = torch.empty((m.get_num_outputs(), x.shape[1]), dtype=x.dtype, device="cuda")
     rc = fn(m._m, x.data_ptr(), x.stride(0), y.data_ptr(), y.stride(0), x.shape[1])
@@ -85,6 +85,24 @@ def test_embedded_matches_oracle(net, dtype, embedded, oracle_lib, monkeypatch):
     if dtype in (pb.F32, pb.F64):
         t = tile_forward(layers, dtype, x, monkeypatch)
         assert K.normwise_err(y, t) <= (1e-6 if dtype == pb.F32 else 1e-14)
+
+
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F64, pb.F16])
+@pytest.mark.parametrize("name", ["layernorm", "residual"])
+def test_embedded_generated_arithmetic(name, dtype, embedded, oracle_lib):
+    """A generated model (Welford LayerNorm, residual before the activation,
+    bias-first sums) through the device API, against the oracle's generated
+    arithmetic and the reference interpreter's fixture."""
+    from tests.test_generated import load_fixture
+    nodes, x, y64, _ = load_fixture(name)
+    g = pb.GeneratedModel(nodes, np.float64 if dtype == pb.F64 else np.float32)
+    layers = g._layer_list(g.dense, g._mirror_values if dtype == pb.F16 else (lambda a: a))
+    xr = pb.to_dtype_bytes(x, dtype)
+    y = K.as_float(run_embedded(embedded, layers, dtype, xr, pb._abi.ARITH_GENERATED), dtype)
+    ref = K.as_float(oracle_lib.forward(layers, dtype, xr, generated=True), dtype)
+    tol = {pb.F32: 1e-5, pb.F64: 1e-12, pb.F16: 2e-3}[dtype]
+    assert K.normwise_err(y, ref) <= tol
+    assert K.normwise_err(y, y64) <= {pb.F32: 1e-5, pb.F64: 1e-12, pb.F16: 3e-2}[dtype]
 
 
 def test_embedded_golden_fixture(embedded):

@@ -150,3 +150,83 @@ def test_gpu_generated_model_api():
     refh = pb.from_dtype_bytes(oracle.forward(layers, pb.F16, pb.to_dtype_bytes(x, pb.F16), generated=True), pb.F16)
     assert yh.dtype == np.float32 and K.normwise_err(yh, refh) <= 2e-3
     assert np.allclose(g.infer_one(x[:, 7]), y[:, 7], rtol=1e-6, atol=1e-7)
+
+
+# ---- pinned to the reference's own graph interpreter -------------------------
+# tests/golden/generated_*.npz come from tests/golden/make_generated_golden.py:
+# canonical graphs of the reference generator's IR (DenseBiasActivation, Dense,
+# DenseResidualActivation, LayerNormalization) evaluated by the reference's
+# kokkos_nn.interpreter.run_graph in float64 and float32.
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+FIXTURES = ["dense_silu", "layernorm", "residual", "residual_input"]
+
+
+def load_fixture(name):
+    import json
+    z = np.load(os.path.join(GOLDEN, f"generated_{name}.npz"))
+    spec = json.loads(str(z["spec"]))
+    p = {k[len("param:"):]: z[k] for k in z.files if k.startswith("param:")}
+    nodes = []
+    for n in spec:
+        if n["op"] == "LayerNormalization":
+            nodes.append(pb.GeneratedLayerNorm(n["name"], p[n["name"] + ".scale"], p[n["name"] + ".bias"], 1e-5))
+        else:
+            act = n["activation"].lower() if n["activation"] else None
+            nodes.append(pb.Dense(n["name"], p[n["name"] + ".weight"], p[n["name"] + ".bias"], act,
+                                  residual=n["residual"]))
+    return nodes, z["x"], z["y64"], z["y32"]
+
+
+@pytest.mark.parametrize("name", FIXTURES)
+def test_oracle_generated_matches_reference_interpreter(name):
+    """The oracle's generated arithmetic (Welford LayerNorm, bias-first sums,
+    residual before the activation) reproduces the reference interpreter."""
+    nodes, x, y64, y32 = load_fixture(name)
+    layers = pb.GeneratedModel(nodes, np.float64)._layer_list(nodes)
+    o64 = oracle.forward(layers, pb.F64, x, generated=True)
+    assert K.normwise_err(o64, y64) <= 1e-12
+    o32 = oracle.forward(layers, pb.F32, x.astype(np.float32), generated=True)
+    assert K.normwise_err(o32, y64) <= 1e-5
+    assert K.normwise_err(o32, y32) <= 1e-5
+
+
+def test_generated_model_structure_checks():
+    rng = np.random.default_rng(9)
+    a = pb.Dense("a", rng.normal(0, 1, (8, 4)), np.zeros(8), "relu")
+    with pytest.raises(ValueError):  # residual of another width
+        pb.GeneratedModel([a, pb.Dense("b", rng.normal(0, 1, (8, 8)), None, None, residual="input")])
+    with pytest.raises(ValueError):  # residual that is not earlier
+        pb.GeneratedModel([a, pb.Dense("b", rng.normal(0, 1, (8, 8)), None, None, residual="c")])
+    g = pb.GeneratedModel([a, pb.GeneratedLayerNorm("ln", np.ones(8), np.zeros(8)),
+                           pb.Dense("b", rng.normal(0, 1, (8, 8)), np.zeros(8), "tanh", residual="a")])
+    assert g.get_num_parameters() == 8 * 4 + 8 + 16 + 64 + 8
+    kinds = [type(l).__name__ for l in g._layer_list(g.dense)]
+    assert kinds == ["Matvec", "Bias", "Relu", "Save_State", "LayerNorm", "Matvec", "Bias", "Binop_Add", "Tanh"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", FIXTURES)
+def test_generated_model_gpu_matches_reference_interpreter(name):
+    """GeneratedModel.infer_batch (float and double) and infer_batch_half2 on
+    the GPU against the reference interpreter's outputs and the oracle's
+    generated arithmetic."""
+    nodes, x, y64, y32 = load_fixture(name)
+    g64 = pb.GeneratedModel([_copy(n) for n in nodes], np.float64)
+    layers = g64._layer_list(g64.dense)
+    assert K.normwise_err(g64.infer_batch(x), oracle.forward(layers, pb.F64, x, generated=True)) <= 1e-12
+    assert K.normwise_err(g64.infer_batch(x), y64) <= 1e-12
+    g32 = pb.GeneratedModel([_copy(n) for n in nodes], np.float32)
+    y = g32.infer_batch(x.astype(np.float32))
+    assert K.normwise_err(y, oracle.forward(layers, pb.F32, x.astype(np.float32), generated=True)) <= 1e-5
+    assert K.normwise_err(y, y64) <= 1e-5
+    yh = g32.infer_batch_half2(x.astype(np.float32))
+    half_layers = g32._layer_list(g32.dense, g32._mirror_values)
+    oh = pb.from_dtype_bytes(oracle.forward(half_layers, pb.F16, pb.to_dtype_bytes(x, pb.F16), generated=True), pb.F16)
+    assert K.normwise_err(yh, oh) <= 2e-3
+    assert K.normwise_err(yh, y64) <= 3e-2  # fp16 storage and fp16 accumulation
+
+
+def _copy(n):
+    import copy
+    return copy.deepcopy(n)
