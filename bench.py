@@ -130,20 +130,22 @@ def host_cpu():
 
 
 def cpu_reference(cfg_name, seconds=10.0, max_cols=1 << 20):
-    """Time the CPU oracle port of the reference's path (oracle/cpu_bench.py,
-    a child process) with one OpenMP thread per physical core,
+    """Time the reference's path on the host cores (oracle/cpu_bench.py, a
+    child process): the reference's own template code compiled against the
+    host Kokkos shim (oracle/_ref, kind "reference") where it was built, else
+    the C port (kind "port"), with one OpenMP thread per physical core,
     OMP_PROC_BIND=spread, OMP_PLACES=cores: median samples/s over passes that
-    total at least one second.  Returns (samples/s, cores, description)."""
+    total at least one second.  Returns (samples/s, cores, description, kind)."""
     cores, model = host_cpu()
     env = dict(os.environ, OMP_NUM_THREADS=str(cores), OMP_PROC_BIND="spread", OMP_PLACES="cores")
     out = subprocess.run([sys.executable, "-m", "oracle.cpu_bench", "--config", cfg_name, "--seconds", str(seconds),
                           "--max-cols", str(max_cols)], cwd=ROOT, env=env, capture_output=True, text=True,
                          check=True, preexec_fn=lambda: os.sched_setaffinity(0, ALL_CPUS)).stdout
     r = json.loads(out.strip().splitlines()[-1])
-    desc = (f"{r['columns']} columns of {cfg_name} per pass, median of {r['passes']} passes "
+    desc = (f"{r['kind']}: {r['columns']} columns of {cfg_name} per pass, median of {r['passes']} passes "
             f"({r['seconds']:.1f} s), {cores} OpenMP threads (OMP_PROC_BIND=spread, OMP_PLACES=cores) on "
             f"{cores} physical cores, {model}")
-    return r["samples_per_s"], cores, desc
+    return r["samples_per_s"], cores, desc, r["kind"]
 
 
 def run_reference(args, cfg, rank, metric, unit, dtype_name):
@@ -153,17 +155,17 @@ def run_reference(args, cfg, rank, metric, unit, dtype_name):
     steps, info = [], None
     per_step = min(10.0, 120.0 / max(1, args.warmup + args.steps))
     for i in range(args.warmup + args.steps):
-        v, cores, sample = cpu_reference(args.config, seconds=per_step)
+        v, cores, sample, kind = cpu_reference(args.config, seconds=per_step)
         if i >= args.warmup:
             steps.append(v)
-        info = (cores, sample)
+        info = (cores, sample, kind)
     value = statistics.median(steps)
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": dtype_name, "data": "synthetic",
         "config": {"workload": cfg.name, "batch_per_gpu": cfg.batch, "sample": info[1]},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": info[0], "kind": "port", "sample": info[1]},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": info[0], "kind": info[2], "sample": info[1]},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -351,8 +353,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_reference(args.config)
-        cpu = {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": sample}
+        v, cores, sample, kind = cpu_reference(args.config)
+        cpu = {"value": v, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
 
     upd = param_update_latency(model) if rank == 0 else None
 

@@ -84,6 +84,9 @@ __device__ __forceinline__ C<T> epilogue(const ponni_b200::Program& p, int first
   for (int e = first; e < first + n; ++e) {
     const ponni_b200::EpiDesc& d = p.epi[e];
     if (d.kind == ponni_b200::EPI_BIAS) v = v + Num<T>::to_c(params[d.p_off + f]);
+    else if (sizeof(T) == 2 && (d.flags & ponni_b200::EPI_FLAG_REF16))
+      v = ponni_b200::activation16(d.kind, d.flags, (float)v, (float)d.s0, (float)d.s1,
+                                   [](float x) { return (float)rnd<T>(x); });
     else v = ponni_b200::activation<C<T>>(d.kind, d.flags, v, (C<T>)d.s0, (C<T>)d.s1);
     v = rnd<T>(v);
   }
@@ -163,7 +166,7 @@ __device__ void infer_one(const Model& m, const T* x, int64_t x_stride, T* y, in
           var = radd<T>(var, rmul<T>(d, d));
         }
         var = rdiv<T>(var, (C<T>)n);
-        const C<T> inv_std = rdiv<T>(C<T>(1), rnd<T>(m_sqrt(radd<T>(var, (C<T>)s.s0))));
+        const C<T> inv_std = rdiv<T>(C<T>(1), m_sqrt(radd<T>(var, (C<T>)s.s0)));  // sqrt in float (16-bit)
         for (int i = 0; i < n; ++i) {
           const C<T> xhat = rmul<T>(rsub<T>(buf[src][i], mean), inv_std);
           buf[src][i] = radd<T>(rmul<T>(Num<T>::to_c(params[s.w_off + i]), xhat), Num<T>::to_c(params[s.b_off + i]));
@@ -188,12 +191,12 @@ __device__ void infer_one(const Model& m, const T* x, int64_t x_stride, T* y, in
         C<T> mx = buf[src][0];
         for (int i = 1; i < n; ++i) mx = buf[src][i] > mx ? buf[src][i] : mx;
         C<T> sum = C<T>(0);
-        for (int i = 0; i < n; ++i) sum = radd<T>(sum, rnd<T>(m_exp(rsub<T>(buf[src][i], mx))));
+        for (int i = 0; i < n; ++i) sum = radd<T>(sum, m_exp(rsub<T>(buf[src][i], mx)));
         if (s.kind == STEP_LOGSOFTMAX) {
-          const C<T> lse = radd<T>(rnd<T>(m_log(sum)), mx);
+          const C<T> lse = radd<T>(m_log(sum), mx);
           for (int i = 0; i < n; ++i) buf[src][i] = rsub<T>(buf[src][i], lse);
         } else {
-          for (int i = 0; i < n; ++i) buf[src][i] = rdiv<T>(rnd<T>(m_exp(rsub<T>(buf[src][i], mx))), sum);
+          for (int i = 0; i < n; ++i) buf[src][i] = rdiv<T>(m_exp(rsub<T>(buf[src][i], mx)), sum);
         }
         break;
       }

@@ -182,6 +182,67 @@ typedef struct {
     }                                                                                                      \
     return x;                                                                                              \
   }                                                                                                        \
+  /* 16-bit models: the activation with the reference's own rounding points */                           \
+  /* (an operation between two `real` values rounds to the type; std::      */                           \
+  /* functions and mixed operations with float run in float; a float result */                           \
+  /* rounds where the reference stores it in a `real`): the apply() of     */                            \
+  /* each src/layers/ponni_<Layer>.h instantiated with half_t / bhalf_t.    */                           \
+  static T act16_##SUF(int md, int kind, int flags, T x, T s0, T s1) {                                     \
+    _Pragma("GCC diagnostic push") _Pragma("GCC diagnostic ignored \"-Wunused-parameter\"")                \
+    switch (kind) {                                                                                        \
+      case PONNI_B200_RELU: return x > 0 ? x : 0;                                                          \
+      case PONNI_B200_LEAKY_RELU: return x > 0 ? x : rnd_##SUF(md, s0 * x);                                \
+      case PONNI_B200_ELU: return x > 0 ? x : rnd_##SUF(md, s0 * (EXP(x) - 1));                            \
+      case PONNI_B200_SELU: {                                                                              \
+        const T a = rnd_##SUF(md, (T)1.6732632423543772848), sc = rnd_##SUF(md, (T)1.0507009873554804934); \
+        return x > 0 ? rnd_##SUF(md, sc * x) : rnd_##SUF(md, rnd_##SUF(md, sc * a) * (EXP(x) - 1));         \
+      }                                                                                                    \
+      case PONNI_B200_GELU:                                                                                \
+        if (flags & PONNI_B200_FLAG_APPROXIMATE) {                                                         \
+          const T k = rnd_##SUF(md, (T)0.79788456080286535588), c = rnd_##SUF(md, (T)0.044715);           \
+          const T x3 = rnd_##SUF(md, rnd_##SUF(md, x * x) * x);                                            \
+          const T t = TANH(rnd_##SUF(md, k * rnd_##SUF(md, x + rnd_##SUF(md, c * x3))));                   \
+          return rnd_##SUF(md, rnd_##SUF(md, (T)0.5 * x) * (1 + t));                                       \
+        }                                                                                                  \
+        return rnd_##SUF(md, rnd_##SUF(md, (T)0.5 * x) *                                                   \
+                                 (1 + ERF(rnd_##SUF(md, x / rnd_##SUF(md, (T)1.4142135623730950488)))));   \
+      case PONNI_B200_SILU:                                                                                \
+        if (x >= 0) return rnd_##SUF(md, x / (1 + EXP(-x)));                                               \
+        {                                                                                                  \
+          const T e = rnd_##SUF(md, EXP(x));                                                               \
+          return rnd_##SUF(md, rnd_##SUF(md, x * e) / rnd_##SUF(md, 1 + e));                               \
+        }                                                                                                  \
+      case PONNI_B200_SIGMOID:                                                                             \
+        if (x >= 0) return rnd_##SUF(md, 1 / (1 + EXP(-x)));                                               \
+        {                                                                                                  \
+          const T e = rnd_##SUF(md, EXP(x));                                                               \
+          return rnd_##SUF(md, e / rnd_##SUF(md, 1 + e));                                                  \
+        }                                                                                                  \
+      case PONNI_B200_TANH: return rnd_##SUF(md, TANH(x));                                                 \
+      case PONNI_B200_SOFTPLUS: {                                                                          \
+        const T sx = rnd_##SUF(md, s0 * x);                                                                \
+        if (sx > 0) return rnd_##SUF(md, (sx + LOG(1 + EXP(-sx))) / s0);                                   \
+        return rnd_##SUF(md, LOG(1 + EXP(sx)) / s0);                                                       \
+      }                                                                                                    \
+      case PONNI_B200_HARD_SIGMOID: {                                                                      \
+        T v = rnd_##SUF(md, rnd_##SUF(md, s0 * x) + s1);                                                   \
+        v = v < 0 ? 0 : v;                                                                                 \
+        return v > 1 ? 1 : v;                                                                              \
+      }                                                                                                    \
+      case PONNI_B200_HARD_SWISH: {                                                                        \
+        T r6 = rnd_##SUF(md, x + 3);                                                                       \
+        r6 = r6 < 0 ? 0 : r6;                                                                              \
+        r6 = r6 > 6 ? 6 : r6;                                                                              \
+        return rnd_##SUF(md, rnd_##SUF(md, x * r6) / 6);                                                   \
+      }                                                                                                    \
+      case PONNI_B200_MISH: {                                                                              \
+        const T sp = x > 0 ? rnd_##SUF(md, x + LOG(1 + EXP(-x))) : rnd_##SUF(md, LOG(1 + EXP(x)));         \
+        return rnd_##SUF(md, x * TANH(sp));                                                                \
+      }                                                                                                    \
+      default: return rnd_##SUF(md, x);                                                                    \
+    }                                                                                                      \
+    _Pragma("GCC diagnostic pop")                                                                          \
+  }                                                                                                        \
   /* Run one sample: bufa holds the input; *res points at the result. */                                   \
   static void sample_##SUF(const OLayer* L, int nl, int smode, int mflags, T* bufa, T* bufb, T** saved,     \
                             T** res) {                                                                     \
@@ -250,7 +311,8 @@ typedef struct {
             var = rnd_##SUF(mode, var + rnd_##SUF(mode, d * d));                                           \
           }                                                                                                \
           var = rnd_##SUF(mode, var / (T)n);                                                               \
-          T inv = rnd_##SUF(mode, (T)1 / rnd_##SUF(mode, SQRT(rnd_##SUF(mode, var + (T)y->s[0]))));         \
+          /* 1 / std::sqrt(real): the square root is a float, rounded once with the quotient */           \
+          T inv = rnd_##SUF(mode, (T)1 / SQRT(rnd_##SUF(mode, var + (T)y->s[0])));                        \
           for (int i = 0; i < n; ++i) {                                                                    \
             T xh = rnd_##SUF(mode, rnd_##SUF(mode, cur[i] - mean) * inv);                                  \
             cur[i] = rnd_##SUF(mode, rnd_##SUF(mode, (T)y->pd[i] * xh) + (T)y->pd[n + i]);                 \
@@ -274,13 +336,13 @@ typedef struct {
           T mx = cur[0], sum = 0;                                                                          \
           for (int i = 1; i < n; ++i) mx = cur[i] > mx ? cur[i] : mx;                                      \
           for (int i = 0; i < n; ++i)                                                                      \
-            sum = rnd_##SUF(mode, sum + rnd_##SUF(mode, EXP(rnd_##SUF(mode, cur[i] - mx))));               \
+            sum = rnd_##SUF(mode, sum + EXP(rnd_##SUF(mode, cur[i] - mx)));                                \
           if (y->kind == PONNI_B200_LOG_SOFTMAX) {                                                         \
-            T lse = rnd_##SUF(mode, rnd_##SUF(mode, LOG(sum)) + mx);                                       \
+            T lse = rnd_##SUF(mode, LOG(sum) + mx);                                                        \
             for (int i = 0; i < n; ++i) cur[i] = rnd_##SUF(mode, cur[i] - lse);                            \
           } else {                                                                                         \
             for (int i = 0; i < n; ++i)                                                                    \
-              cur[i] = rnd_##SUF(mode, rnd_##SUF(mode, EXP(rnd_##SUF(mode, cur[i] - mx))) / sum);          \
+              cur[i] = rnd_##SUF(mode, EXP(rnd_##SUF(mode, cur[i] - mx)) / sum);                           \
           }                                                                                                \
           break;                                                                                           \
         }                                                                                                  \
@@ -313,7 +375,9 @@ typedef struct {
         }                                                                                                  \
         default:                                                                                           \
           for (int f = 0; f < n; ++f)                                                                      \
-            cur[f] = rnd_##SUF(mode, act_##SUF(y->kind, y->flags, cur[f], (T)y->s[0], (T)y->s[1]));        \
+            cur[f] = (!gen && (mode == PONNI_B200_F16 || mode == PONNI_B200_BF16))                        \
+                         ? act16_##SUF(mode, y->kind, y->flags, cur[f], (T)y->s[0], (T)y->s[1])            \
+                         : rnd_##SUF(mode, act_##SUF(y->kind, y->flags, cur[f], (T)y->s[0], (T)y->s[1]));  \
           break;                                                                                           \
       }                                                                                                    \
       /* acc32: the state is stored (rounded to the model type) where a fused  */                          \

@@ -12,4 +12,9 @@ enum EpiKind : int {
   EPI_HARD_SWISH = 12, EPI_MISH = 13,
 };
 
+// Epilogue-entry flag: a 16-bit model evaluates this activation with the
+// reference's own rounding points (activation16), not in float with one
+// rounding (the generated model's half2 arithmetic).
+constexpr int EPI_FLAG_REF16 = 0x100;
+
 }  // namespace ponni_b200

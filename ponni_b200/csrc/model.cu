@@ -240,6 +240,9 @@ struct Planner {
       memset(&e, 0, sizeof(e));
       e.kind = L.d.kind;
       e.flags = L.d.flags;
+      if ((m->dtype == PONNI_B200_F16 || m->dtype == PONNI_B200_BF16) && m->arithmetic != PONNI_B200_ARITH_GENERATED &&
+          L.d.kind != PONNI_B200_BIAS)
+        e.flags |= EPI_FLAG_REF16;
       e.s0 = L.d.scalar[0];
       e.s1 = L.d.scalar[1];
       e.s2 = L.d.scalar[2];

@@ -110,6 +110,9 @@ __device__ __forceinline__ void epi_staged(const Tables<T>& t, int first, int n,
       for (int j = 0; j < V; ++j) {
         C& v = t.stage[(f * V + j) * kNarrowThreads + threadIdx.x];
         if (d.kind == EPI_BIAS) v = rnd<T>(v + b);
+        else if (sizeof(T) == 2 && (d.flags & EPI_FLAG_REF16))
+          v = rnd<T>(activation16(d.kind, d.flags, (float)v, (float)d.s0, (float)d.s1,
+                                  [](float x) { return (float)rnd<T>(x); }));
         else v = rnd<T>(activation<C>(d.kind, d.flags, v, d.s0, d.s1));
       }
     }

@@ -74,6 +74,17 @@ __device__ __forceinline__ void load_input_tile(T* dst, const T* __restrict__ in
   }
 }
 
+// One activation: 16-bit models with the reference's rounding points when
+// the entry asks for them, else in the compute type.
+template <class T>
+__device__ __forceinline__ typename Num<T>::C act_value(int kind, int flags, typename Num<T>::C v,
+                                                         typename Num<T>::C s0, typename Num<T>::C s1) {
+  if constexpr (sizeof(T) == 2) {
+    if (flags & EPI_FLAG_REF16) return activation16(kind, flags, v, s0, s1, [](float x) { return rnd<T>(x); });
+  }
+  return activation<typename Num<T>::C>(kind, flags, v, s0, s1);
+}
+
 // Apply the pointwise epilogue list of a step to one value of feature f.
 template <class T>
 __device__ __forceinline__ typename Num<T>::C apply_epilogue(const Program& p, int first, int n, int f,
@@ -84,7 +95,7 @@ __device__ __forceinline__ typename Num<T>::C apply_epilogue(const Program& p, i
     if (d.kind == EPI_BIAS) {
       v = v + Num<T>::to_c(params[d.p_off + f]);
     } else {
-      v = activation<C>(d.kind, d.flags, v, (C)d.s0, (C)d.s1);
+      v = act_value<T>(d.kind, d.flags, v, (C)d.s0, (C)d.s1);
     }
     v = rnd<T>(v);
   }
@@ -175,7 +186,7 @@ __device__ __forceinline__ void dense_epilogue(const Program& p, const StepDesc&
       if (s.flags & DENSE_ADD_RESIDUAL) a = rnd<T>(Num<T>::to_c(res[o * bt + c0 + j]) + a);
       if (ACT >= 0) {
         if (s.fast_bias_off >= 0) a = rnd<T>(a + b);
-        if (ACT != EPI_NONE) a = rnd<T>(activation<C>(ACT, s.fast_act_flags, a, (C)s.s0, (C)s.s1));
+        if (ACT != EPI_NONE) a = rnd<T>(act_value<T>(ACT, s.fast_act_flags, a, (C)s.s0, (C)s.s1));
         v[j] = a;
       } else {
         v[j] = apply_epilogue<T>(p, s.epi_first, s.n_epi, o, a, params);
@@ -411,7 +422,9 @@ __device__ void layernorm_step(const StepDesc& s, int bt, const T* params, T* x)
       var = radd<T>(var, rmul<T>(d, d));
     }
     var = rdiv<T>(var, (C)n);
-    const C inv_std = rdiv<T>(C(1), rnd<T>(m_sqrt(radd<T>(var, eps))));
+    // 1 / std::sqrt(real): for 16-bit models the square root is a float and
+    // only the quotient is rounded
+    const C inv_std = rdiv<T>(C(1), m_sqrt(radd<T>(var, eps)));
     for (int i = 0; i < n; ++i) {
       C xhat = rmul<T>(rsub<T>(Num<T>::to_c(x[i * bt + c]), mean), inv_std);
       C v = radd<T>(rmul<T>(Num<T>::to_c(gamma[i]), xhat), Num<T>::to_c(beta[i]));
@@ -453,16 +466,18 @@ __device__ void softmax_step(const StepDesc& s, int bt, T* x) {
       C v = Num<T>::to_c(x[i * bt + c]);
       mx = v > mx ? v : mx;
     }
+    // std::exp / std::log of a 16-bit `real` are floats, rounded only where
+    // the reference stores them (src/layers/ponni_Softmax.h:46-57)
     C sum = C(0);
     for (int i = 0; i < n; ++i)
-      sum = radd<T>(sum, rnd<T>(m_exp(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx))));
+      sum = radd<T>(sum, m_exp(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx)));
     if (LOG) {
-      const C lse = radd<T>(rnd<T>(m_log(sum)), mx);
+      const C lse = radd<T>(m_log(sum), mx);
       for (int i = 0; i < n; ++i)
         x[i * bt + c] = Num<T>::from_c(rsub<T>(Num<T>::to_c(x[i * bt + c]), lse));
     } else {
       for (int i = 0; i < n; ++i) {
-        C e = rnd<T>(m_exp(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx)));
+        const C e = m_exp(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx));
         x[i * bt + c] = Num<T>::from_c(rdiv<T>(e, sum));
       }
     }

@@ -8,6 +8,10 @@ pytorch_resnet.ponni: the reference's own fixture generator
 unit/pytorch_resnet/generate_pytorch_resnet_data.py (TinyResNet 12->5 SiLU x4
 residual ->4, seed 9012, one test sample; torch computes test.output), run
 unmodified with the reference's generator package on PYTHONPATH.
+
+projection_skip.ponni: the reference's unit/projection_skip/
+generate_projection_skip_data.py (main and skip Linear 2->3 with fixed
+weights and the expected outputs of its test), run the same way.
 """
 import os
 import subprocess
@@ -23,6 +27,8 @@ def main():
     env = dict(os.environ, PYTHONPATH=os.path.join(ref, "src", "generator"), CUDA_VISIBLE_DEVICES="")
     subprocess.run([sys.executable, os.path.join(ref, "unit", "pytorch_resnet", "generate_pytorch_resnet_data.py"),
                     os.path.join(HERE, "pytorch_resnet.ponni")], check=True, env=env)
+    subprocess.run([sys.executable, os.path.join(ref, "unit", "projection_skip", "generate_projection_skip_data.py"),
+                    os.path.join(HERE, "projection_skip.ponni")], check=True, env=env)
 
 
 if __name__ == "__main__":
