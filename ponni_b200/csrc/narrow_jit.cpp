@@ -129,7 +129,7 @@ void emit_epi(std::ostringstream& o, int dtype, const EpiDesc& d, const char* f)
     case EPI_RELU: o << "        acc = acc > C(0) ? acc : C(0);\n"; break;
     case EPI_LEAKY_RELU: o << "        acc = R(acc > C(0) ? acc : " << lit(dtype, d.s0) << " * acc);\n"; break;
     default:
-      if ((dtype == PONNI_B200_F16 || dtype == PONNI_B200_BF16) && (d.flags & EPI_FLAG_REF16))
+      if ((dtype == 2 || dtype == 3) && (d.flags & EPI_FLAG_REF16))  // fp16 / bf16
         o << "        acc = R(ponni_b200::activation16(" << d.kind << ", " << d.flags << ", acc, " << lit(dtype, d.s0)
           << ", " << lit(dtype, d.s1) << ", [](float x) { return R(x); }));\n";
       else
