@@ -311,3 +311,29 @@ def test_caller_device_is_restored(oracle_lib):
         check(yh, ref, cfg.dtype, cfg.layers, x)
         del m
         assert torch.cuda.current_device() == 0
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+@pytest.mark.parametrize("dtype", [pb.F32, pb.F16, pb.BF16])
+def test_configs_vs_reference_itself(name, dtype):
+    """Each config on the GPU against the reference's own code (its template
+    headers compiled against the host Kokkos shim, oracle/_ref): fp32 through
+    the default kernels with the fp32 gate, 16-bit with the reference's
+    arithmetic (tile / narrow kernels): bit for bit where the network has no
+    transcendental function (cfg1-cfg3), else normwise <= 2e-3 against the
+    reference's half path (CUDA's and the host C library's expf / erff differ
+    by a unit in the last place, which can move a 16-bit rounding)."""
+    from oracle import ref
+    if not ref.available():
+        pytest.skip("oracle/_ref not built")
+    cfg = configs.ALL[name](batch=3001)
+    x = pb.to_dtype_bytes(K.as_float(configs.host_inputs(cfg, cfg.batch), cfg.dtype), dtype)
+    arith = None if dtype == pb.F32 else pb._abi.ARITH_REFERENCE
+    y = run_device(cfg.layers, dtype, x, arith)
+    r = ref.forward(cfg.layers, dtype, x)
+    if dtype == pb.F32:
+        check(y, r, dtype, cfg.layers, x)
+    elif name in ("cfg1", "cfg2", "cfg3"):
+        assert np.array_equal(y.view(np.uint16), r.view(np.uint16))
+    else:
+        assert K.normwise_err(K.as_float(y, dtype), K.as_float(r, dtype)) <= 2e-3
