@@ -404,11 +404,6 @@ bool tr_plan(const ponni_b200_model* m, TrProgram& p, std::vector<unsigned char>
           why = "two LayerNorms between Matvecs";
           return false;
         }
-        if (L.n_pad % 32 != 0) {
-          // The row is parked in the layer's first accumulator (32-column chunks).
-          why = "LayerNorm width not a multiple of 32 after a Matvec";
-          return false;
-        }
         o.kind = TR_LN;
         L.ln = nops - L.op_first;
         vec_ops.push_back({nops, &Ls[i]});

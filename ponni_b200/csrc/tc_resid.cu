@@ -14,10 +14,11 @@
 //     products into a correction accumulator (the tensor core's fp32
 //     accumulation truncates; keeping the small products apart keeps the
 //     result fp32-accurate);
-//   epilogue (warps 0-15: two groups of 8, one per tile slot, each 4 TMEM
-//     lane quarters x 2 column halves; thread = one batch column = one row of
-//     the tile): sums the accumulators and runs the job's epilogue
-//     operations in tuple order (reference src/ponni_Inference.h:416-555):
+//   epilogue (warps 0-15, 4 TMEM lane quarters x 4 column quarters; a
+//     thread holds one 32-column chunk of one row = one batch column): all
+//     16 warps take the jobs one at a time in the issuer's order; per job
+//     they sum the accumulators and run the job's epilogue operations in
+//     tuple order (reference src/ponni_Inference.h:416-555):
 //       Bias                    v += b                (ponni_Bias.h:66-68)
 //       activations             v = f(v)              (activation.cuh)
 //       Binop_Add<I>            v += saved[I]         (ponni_Binop_Add.h:58-68)
@@ -25,15 +26,14 @@
 //       LayerNorm               two-pass mean / biased variance,
 //                               gamma * (v - mean) / sqrt(var + eps) + beta
 //                               (ponni_LayerNorm.h:77-99)
-//     then splits the result into the three bf16 parts of the next job's A
-//     operand (shared memory, K-major SW128) or writes the caller's output.
-//     LayerNorm parks the row's values in the (already read) main
-//     accumulator columns and exchanges the two column halves' partial sums
-//     through shared memory.  Saved states live in a per-CTA, per-slot
-//     global scratch area (64 KB per slot and state; L2-resident), written
-//     and read back by the same thread.
-// Two tiles are in flight and their jobs alternate Matvec by Matvec, so one
-// tile's epilogue overlaps the other's MMAs.
+//     then split the result into the three bf16 parts of the next job's A
+//     operand (shared memory, K-major SW128) or write the caller's output.
+//     LayerNorm keeps the row's values in registers and exchanges the four
+//     column quarters' partial sums through shared memory.  Saved states
+//     live in a per-CTA, per-slot global scratch area (64 KB per slot and
+//     state; L2-resident), written and read back by the same thread.
+// Two tiles are in flight and their jobs alternate Matvec by Matvec, so the
+// epilogue of one tile's job overlaps the MMAs of the other tile's job.
 //
 // Arithmetic: fp32 model values; each operand x = x0 + x1 + x2 exactly
 // (bf16 truncation parts); products of order <= 2 are kept (the dropped ones
@@ -42,8 +42,8 @@
 //
 // Every wait is bounded: a role that gives up raises the CTA's abort flag,
 // records an error code and the CTA drains its copies and MMAs before it
-// frees TMEM; the epilogue warps of a slot decide to leave together (a
-// barrier reduction), so none is left waiting at a named barrier.
+// frees TMEM; the epilogue warps decide to leave together (a barrier
+// reduction), so none is left waiting at a named barrier.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -78,44 +78,6 @@ constexpr long long kWaitCycles = PONNI_B200_WAIT_LIMIT;
 #define TR_ACC(acc, t0)
 #define TR_FLUSH(idx, acc)
 #endif
-
-// 32 fp32 values into 32 consecutive TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-      : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
-
-// Named barrier over one slot's epilogue warps (ids 1, 2; 0 is __syncthreads).
-__device__ __forceinline__ void slot_sync(int s) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(s + 1), "r"(kTrGroupThreads) : "memory");
-}
-__device__ __forceinline__ int slot_sync_or(int s, int pred) {
-  int r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.b32 p, %2, 0;\n\t"
-      "bar.red.or.pred q, %1, %3, p;\n\t"
-      "selp.b32 %0, 1, 0, q;\n\t}\n"
-      : "=r"(r)
-      : "r"(s + 1), "r"(pred), "r"(kTrGroupThreads)
-      : "memory");
-  return r;
-}
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float r;
@@ -171,15 +133,38 @@ __device__ __forceinline__ void act_dispatch(int kind, float (&v)[32], int flags
   }
 }
 
-// Per-thread context of the epilogue.
+// Per-thread context of the epilogue.  All 16 epilogue warps work on one
+// job at a time: warp w reads TMEM lane quarter w % 4 (rows 32 (w % 4) ..)
+// and handles accumulator columns 32 (w / 4) .. + 31, so each thread holds
+// one 32-column chunk of one row in registers.
 struct TrEpi {
   const unsigned char* image;
-  float4* saved;      // this CTA's and slot's saved states: [state][f / 4][128 rows] float4
+  float4* saved_cta;  // this CTA's saved states: [slot][state][f / 4][128 rows] float4
+  int n_saved;
+  float* xch;         // LayerNorm exchange [4 column quarters][128 rows]
+  int cq, m;          // column quarter, row
+  // the job's slot
+  float4* saved;      // the slot's saved states
   uint32_t a[3];      // the slot's A operand parts
-  uint32_t tmem_row;  // slot accumulator base + this warp's lane quarter
-  float* xch;         // the slot's LayerNorm exchange [2 halves][128 rows]
-  int s, h, m;        // slot, column half, row
+  uint32_t tmem_row;  // the slot's accumulators + this warp's lane quarter
 };
+
+// Named barrier over the 16 epilogue warps (id 1; 0 is __syncthreads).
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;\n" ::"r"(kTrEpiWarps * 32) : "memory");
+}
+__device__ __forceinline__ int epi_sync_or(int pred) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(pred), "r"(kTrEpiWarps * 32)
+      : "memory");
+  return r;
+}
 
 // Element-wise operations [o0, o1) on the 32 columns c0.. of this row.
 __device__ __forceinline__ void tr_ops(const TrOp* ops, int o0, int o1, float (&v)[32], int c0, const TrEpi& E) {
@@ -244,21 +229,22 @@ __device__ __forceinline__ void tr_finish(const float (&v)[32], int c0, bool las
   }
 }
 
-// Epilogue of job (layer l) for this thread's row and column half.
-__device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrEpi& E, float* __restrict__ out, int64_t out_ld,
-                            int64_t col, int64_t batch) {
+// Epilogue of job (layer l) for this thread's row and 32-column chunk.
+__device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrEpi& E, float* __restrict__ out,
+                                            int64_t out_ld, int64_t col, int64_t batch) {
   const TrLayer& L = p.layers[l];
   const int n_pad = L.n_pad, nout = L.nout, groups = L.groups;
   const bool last = l == p.n_layers - 1;
   const int o0 = L.op_first, o_end = o0 + L.n_ops;
   const bool has_ln = L.ln >= 0;
   const int o_ln = has_ln ? o0 + L.ln : o_end;
-  const int cb = E.h * kTrHalfCols, ce = min(cb + kTrHalfCols, n_pad);
-  const uint32_t corr = E.tmem_row + (uint32_t)((groups - 1) * n_pad);
-  float psum = 0.f;
-#pragma unroll 1
-  for (int c0 = cb; c0 < ce; c0 += 32) {
-    float v[32], w[32];
+  const int c0 = E.cq * 32;
+  const bool active = c0 < n_pad;  // warp-uniform
+  const int nv = min(32, nout - c0);  // valid columns of the chunk
+  float v[32];
+  if (active) {
+    float w[32];
+    const uint32_t corr = E.tmem_row + (uint32_t)((groups - 1) * n_pad);
     tmem_ld32x2(corr + (uint32_t)c0, E.tmem_row + (uint32_t)c0, v, w);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] += w[j];
@@ -269,91 +255,79 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
       for (int j = 0; j < 32; ++j) v[j] += w[j];
     }
     tr_ops(p.ops, o0, o_ln, v, c0, E);
-    if (has_ln) {
-      if (nout - c0 >= 32) {
+  }
+  if (has_ln) {
+    // LayerNorm over the row (src/layers/ponni_LayerNorm.h:77-99): the four
+    // column quarters of a row exchange partial sums.
+    float psum = 0.f;
+    if (active) {
+      if (nv >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) psum = __fadd_rn(psum, v[j]);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (c0 + j < nout) psum = __fadd_rn(psum, v[j]);
+          if (j < nv) psum = __fadd_rn(psum, v[j]);
       }
-      tmem_st32(E.tmem_row + (uint32_t)c0, v);  // park the row in the read main accumulator
-    } else {
-      tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
     }
-  }
-  if (!has_ln) return;
-#if PONNI_B200_TR_DIAG & 2  // diagnostic builds: bit 2 replaces LayerNorm passes 2-3 by a plain store
-  for (int c0 = cb; c0 < ce; c0 += 32) {
-    float v[32];
-    tmem_ld32(E.tmem_row + (uint32_t)c0, v);
-    tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
-  }
-  return;
-#endif
-  // LayerNorm over the row (src/layers/ponni_LayerNorm.h:77-99): the two
-  // column halves exchange partial sums.
-  const TrOp ln = p.ops[o_ln];
-  const float n = (float)nout;
-  tmem_wait_st();
-  E.xch[E.h * 128 + E.m] = psum;
-  slot_sync(E.s);
-  const float mean = __fdiv_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), n);
-  slot_sync(E.s);
-  float pvar = 0.f;
-#pragma unroll 1
-  for (int c0 = cb; c0 < ce; c0 += 32) {
-    float v[32];
-    tmem_ld32(E.tmem_row + (uint32_t)c0, v);
-    if (nout - c0 >= 32) {
+    const float n = (float)nout;
+    E.xch[E.cq * 128 + E.m] = psum;
+    epi_sync();
+    const float mean =
+        __fdiv_rn(__fadd_rn(__fadd_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), E.xch[256 + E.m]), E.xch[384 + E.m]), n);
+    epi_sync();
+    float pvar = 0.f;
+    if (active) {
+      if (nv >= 32) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float d = __fsub_rn(v[j], mean);
-        pvar = __fadd_rn(pvar, __fmul_rn(d, d));
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < nout) {
+        for (int j = 0; j < 32; ++j) {
           const float d = __fsub_rn(v[j], mean);
           pvar = __fadd_rn(pvar, __fmul_rn(d, d));
         }
-    }
-  }
-  E.xch[E.h * 128 + E.m] = pvar;
-  slot_sync(E.s);
-  const float var = __fdiv_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), n);
-  const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, ln.s0)));
-  const float4* g4 = reinterpret_cast<const float4*>(E.image + ln.off);
-  const float4* b4 = g4 + 32;
-#pragma unroll 1
-  for (int c0 = cb; c0 < ce; c0 += 32) {
-    float v[32];
-    tmem_ld32(E.tmem_row + (uint32_t)c0, v);
+      } else {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 g = __ldg(g4 + c0 / 4 + q), b = __ldg(b4 + c0 / 4 + q);
-      const float gg[4] = {g.x, g.y, g.z, g.w}, bb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float xhat = __fmul_rn(__fsub_rn(v[4 * q + e], mean), inv_std);
-        v[4 * q + e] = __fadd_rn(__fmul_rn(gg[e], xhat), bb[e]);
+        for (int j = 0; j < 32; ++j)
+          if (j < nv) {
+            const float d = __fsub_rn(v[j], mean);
+            pvar = __fadd_rn(pvar, __fmul_rn(d, d));
+          }
       }
     }
-    tr_ops(p.ops, o_ln + 1, o_end, v, c0, E);
-    tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
+    E.xch[E.cq * 128 + E.m] = pvar;
+    epi_sync();
+    const float var =
+        __fdiv_rn(__fadd_rn(__fadd_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), E.xch[256 + E.m]), E.xch[384 + E.m]), n);
+    if (active) {
+      const TrOp ln = p.ops[o_ln];
+      const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, ln.s0)));
+      const float4* g4 = reinterpret_cast<const float4*>(E.image + ln.off) + c0 / 4;
+      const float4* b4 = g4 + 32;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 g = __ldg(g4 + q), b = __ldg(b4 + q);
+        const float gg[4] = {g.x, g.y, g.z, g.w}, bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float xhat = __fmul_rn(__fsub_rn(v[4 * q + e], mean), inv_std);
+          v[4 * q + e] = __fadd_rn(__fmul_rn(gg[e], xhat), bb[e]);
+        }
+      }
+      tr_ops(p.ops, o_ln + 1, o_end, v, c0, E);
+    }
+    // (the exchange buffer is rewritten only by a later job, which starts
+    // after every epilogue warp has arrived for this one)
   }
+  if (active) tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
 }
 
 // Stage this row's input column as layer 0's A operand (three bf16 parts);
-// column half h takes the 8-feature groups h, h + 2, ...
+// column quarter cq takes the 8-feature groups cq, cq + 4, ...
 __device__ __forceinline__ void tr_stage_input(const float* __restrict__ in, int64_t in_ld, int nin, int k_pad,
                                                int64_t col, int64_t batch, const TrEpi& E) {
   const bool live = col < batch;
   const float* src = in + col;
 #pragma unroll 1
-  for (int g = E.h; g < k_pad / 8; g += 2) {
+  for (int g = E.cq; g < k_pad / 8; g += 4) {
     float v[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -462,7 +436,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     }
     for (int s = 0; s < kTrSlots; ++s) {
       mbar_init(b_accf + 8u * s, 1);
-      mbar_init(b_epid + 8u * s, kTrGroupWarps);
+      mbar_init(b_epid + 8u * s, kTrEpiWarps);
     }
     mbar_init(b_drain, 1);
     *abort_flag = 0;
@@ -573,82 +547,71 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     __syncwarp();
   } else {
     // ----------------------------------------------- epilogue ----
+    // All 16 warps take the jobs in the MMA issuer's order, one job at a
+    // time, so that one job's epilogue runs while the tensor core works on
+    // the other slot's job.
     TrEpi E;
-    E.s = warp / kTrGroupWarps;
-    E.h = (warp >> 2) & 1;
+    E.cq = warp >> 2;
     E.m = (warp & 3) * 32 + lane;
     E.image = image;
-    E.saved = reinterpret_cast<float4*>(scratch + (size_t)blockIdx.x * (p.scratch_per_cta / 4)) +
-              (size_t)E.s * p.n_saved * (kTrMaxN / 4) * 128;
-    for (int q = 0; q < 3; ++q) E.a[q] = base + (uint32_t)(E.s * 3 + q) * kTrPartBytes;
-    E.tmem_row = tmem_base + (uint32_t)E.s * kTrSlotTmem + ((uint32_t)((warp & 3) * 32) << 16);
-    E.xch = reinterpret_cast<float*>(smem_raw + (s_xch - base)) + E.s * 256;
-    const int s = E.s;
+    E.n_saved = p.n_saved;
+    E.saved_cta = reinterpret_cast<float4*>(scratch + (size_t)blockIdx.x * (p.scratch_per_cta / 4));
+    E.xch = reinterpret_cast<float*>(smem_raw + (s_xch - base));
+    auto select_slot = [&](int s) {
+      E.saved = E.saved_cta + (size_t)s * p.n_saved * (kTrMaxN / 4) * 128;
+      for (int q = 0; q < 3; ++q) E.a[q] = base + (uint32_t)(s * 3 + q) * kTrPartBytes;
+      E.tmem_row = tmem_base + (uint32_t)s * kTrSlotTmem + ((uint32_t)((warp & 3) * 32) << 16);
+    };
     const int k0 = p.layers[0].k_pad;
-    uint32_t acc_ph = 0;
-    const int64_t my_tiles = s ? jobs.c1 : jobs.c0;
-    if (my_tiles > 0) {
-      tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, 0) * kTcM + E.m, batch, E);
+    // Operand written and accumulators read: hand the slot to the MMA issuer.
+    auto release = [&](int s) {
       fence_proxy_async();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(b_epid + 8u * s);
-    }
+    };
+    for (int s = 0; s < kTrSlots; ++s)
+      if ((s ? jobs.c1 : jobs.c0) > 0) {
+        select_slot(s);
+        tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, 0) * kTcM + E.m, batch, E);
+        release(s);
+      }
     bool ok = true;
+    uint32_t ph0 = 0, ph1 = 0;
     [[maybe_unused]] long long w_acc = 0, c_work = 0;
-    (void)w_acc;
-    (void)c_work;
-    for (int64_t r = 0; r < my_tiles && ok; ++r) {
-      const int64_t col = jobs.tile(s, r) * kTcM + E.m;
-      for (int l = 0; l < nl; ++l) {
-        TR_T(ta);
-        int got = 0;
-#if PONNI_B200_TR_DIAG & 16  // diagnostic builds: bit 16 backs the epilogue's waits off with nanosleep
-        if (lane == 0) {
-          const long long t0 = clock64();
-          got = 1;
-          while (!mbar_try_wait(b_accf + 8u * s, acc_ph)) {
-            if (*abort_flag || clock64() - t0 > kWaitCycles) {
-              *abort_flag = 1;
-              got = 0;
-              break;
-            }
-            __nanosleep(64);
+    for (int64_t r = 0; r < jobs.c0 && ok; ++r)
+      for (int l = 0; l < nl && ok; ++l)
+        for (int s = 0; s < kTrSlots; ++s) {
+          const int64_t tiles = s ? jobs.c1 : jobs.c0;
+          if (r >= tiles) continue;
+          TR_T(ta);
+          int got = 0;
+          if (lane == 0) got = wait_phase_abort(b_accf + 8u * s, s ? ph1 : ph0, abort_flag, kWaitCycles) ? 1 : 0;
+          got = __shfl_sync(0xffffffffu, got, 0);
+          // The epilogue warps leave together (none is left at a named barrier).
+          if (epi_sync_or(!got)) {
+            ok = false;
+            break;
+          }
+          if (s) ph1 ^= 1u;
+          else ph0 ^= 1u;
+          TR_ACC(w_acc, ta);
+          TR_T(tw);
+          tc_fence_after();
+          select_slot(s);
+          tr_epilogue(p, l, E, out, out_ld, jobs.tile(s, r) * kTcM + E.m, batch);
+          TR_ACC(c_work, tw);
+          if (l + 1 < nl) {
+            release(s);
+          } else if (r + 1 < tiles) {
+            // The slot's MMAs are done with its operand and its accumulators
+            // are read: stage its next tile.
+            tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, r + 1) * kTcM + E.m, batch, E);
+            release(s);
           }
         }
-#else
-        if (lane == 0) got = wait_phase_abort(b_accf + 8u * s, acc_ph, abort_flag, kWaitCycles) ? 1 : 0;
-#endif
-        got = __shfl_sync(0xffffffffu, got, 0);
-        // The slot's warps leave together (none is left at a named barrier).
-        if (slot_sync_or(s, !got)) {
-          ok = false;
-          break;
-        }
-        acc_ph ^= 1u;
-        TR_ACC(w_acc, ta);
-        TR_T(tw);
-        tc_fence_after();
-        tr_epilogue(p, l, E, out, out_ld, col, batch);
-        TR_ACC(c_work, tw);
-        if (l + 1 < nl) {
-          fence_proxy_async();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(b_epid + 8u * s);
-        }
-      }
-      if (ok && r + 1 < my_tiles) {
-        // The slot's MMAs are done with its operand and its accumulators are
-        // read: stage the next tile.
-        tr_stage_input(in, in_ld, p.nin, k0, jobs.tile(s, r + 1) * kTcM + E.m, batch, E);
-        fence_proxy_async();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(b_epid + 8u * s);
-      }
-    }
-    if (!ok && tid % kTrGroupThreads == 0) atomicExch(err, 4);
-    if (tid % kTrGroupThreads == 0) {
+    if (!ok && tid == 0) atomicExch(err, 4);
+    if (tid == 0) {
       TR_FLUSH(4, w_acc);
       TR_FLUSH(5, c_work);
     }

@@ -9,7 +9,8 @@
 // whose epilogue runs every layer up to the next Matvec, in tuple order:
 // element-wise operations (Bias, activations, Binop_Add of a saved state,
 // Save_State) on 32-column chunks of the accumulator, and at most one
-// LayerNorm, a whole-row operation over the row's values parked in TMEM.
+// LayerNorm, a whole-row operation whose four 32-column chunks exchange
+// partial sums.
 // Batch columns sit on the TMEM lanes, so one row of a tile is one sample.
 //
 // Work unit ("job"): one Matvec for one tile of 128 batch columns,
@@ -39,13 +40,10 @@ constexpr int kTrMaxSaved = 2;                  // distinct Save_State indices
 constexpr int kTrChunkBytes = kTrMaxN * 128;    // ring stage: up to 128 rows x 128 B
 constexpr int kTrStages = 2;
 constexpr int kTrSlots = 2;                     // tiles in flight per CTA
-constexpr int kTrGroupWarps = 8;                // epilogue warps of a slot: 4 TMEM lane quarters x 2 column halves
-constexpr int kTrGroupThreads = kTrGroupWarps * 32;
-constexpr int kTrEpiWarps = kTrSlots * kTrGroupWarps;
+constexpr int kTrEpiWarps = 16;                 // epilogue warps: 4 TMEM lane quarters x 4 column quarters
 constexpr int kTrProducerWarp = kTrEpiWarps;
 constexpr int kTrMmaWarp = kTrEpiWarps + 1;
 constexpr int kTrThreads = (kTrEpiWarps + 2) * 32;
-constexpr int kTrHalfCols = kTrMaxN / 2;        // accumulator columns per column half
 constexpr uint32_t kTrSlotTmem = 256;           // TMEM columns per slot: main + correction accumulators
 constexpr uint32_t kTrPartBytes = 2 * 128 * 128;  // one operand part: 2 K blocks x 128 rows x 128 B
 constexpr int kTrMaxParts = 3;

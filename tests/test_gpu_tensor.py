@@ -235,7 +235,7 @@ def test_tr_cfg4_many_tiles_per_cta(grid, batch, oracle_lib, monkeypatch):
 
 def resid_model(rng, widths=(24, 64, 96, 128, 40, 32), n_out=7):
     """Residual chain with every fused operation: LayerNorm with non-trivial
-    gamma/beta at several widths, two saved states, Binop_Add before and after
+    gamma/beta at several widths (one not a multiple of 32), two saved states, Binop_Add before and after
     activations and LayerNorm, all activations, widths that are not multiples
     of 16."""
     acts = [pb.Relu, pb.Gelu, lambda n: pb.Gelu(n, True), pb.Silu, pb.Tanh, pb.Sigmoid, pb.Elu, pb.Selu,
@@ -254,7 +254,7 @@ def resid_model(rng, widths=(24, 64, 96, 128, 40, 32), n_out=7):
                acts[7](96), pb.Binop_Add(96, 0), acts[8](96), acts[9](96)]
     layers += [pb.Matvec(rng.normal(0, 0.12, (96, 64))), acts[10](64), acts[11](64), pb.Binop_Add(64, 3),
                acts[12](64), ln(64)]
-    layers += [pb.Matvec(rng.normal(0, 0.15, (64, 40))), pb.Bias(rng.normal(0, 0.1, 40)), pb.Relu(40),
+    layers += [pb.Matvec(rng.normal(0, 0.15, (64, 40))), pb.Bias(rng.normal(0, 0.1, 40)), pb.Relu(40), ln(40),
                pb.Matvec(rng.normal(0, 0.2, (40, n_out))), pb.Bias(rng.normal(0, 0.1, n_out))]
     return layers
 
