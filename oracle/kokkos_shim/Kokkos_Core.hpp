@@ -156,12 +156,12 @@ constexpr float bhalf_bits_to_float(std::uint16_t h) { return std::bit_cast<floa
 // result once).
 template <std::uint16_t (*ToBits)(float), float (*FromBits)(std::uint16_t)>
 struct Half16 {
-  std::uint16_t bits = 0;
+  std::uint16_t bits;  // (uninitialised by default: arrays allocated without initialising stay untouched)
   Half16() = default;
   template <class T, class = std::enable_if_t<std::is_arithmetic_v<T>>>
   constexpr Half16(T v) : bits(ToBits((float)v)) {}
   static constexpr Half16 from_bits(std::uint16_t b) {
-    Half16 h;
+    Half16 h{};
     h.bits = b;
     return h;
   }
@@ -334,6 +334,15 @@ struct ViewAllocProp {
   std::string label;
   bool initialize = true;
 };
+// One allocation and its label (shared by every view of it).
+struct Record {
+  std::string label;
+  unsigned char* mem;
+  Record(std::size_t bytes, const std::string& l) : label(l), mem(new unsigned char[bytes ? bytes : 1]) {}
+  ~Record() { delete[] mem; }
+  Record(const Record&) = delete;
+  Record& operator=(const Record&) = delete;
+};
 }  // namespace shim
 
 struct WithoutInitializing_t {};
@@ -405,7 +414,8 @@ template <class DataType, class... Properties> class View {
   template <class D2, class... P2,
             class = std::enable_if_t<View<D2, P2...>::rank == rank &&
                                      std::is_convertible_v<typename View<D2, P2...>::value_type*, value_type*>>>
-  View(const View<D2, P2...>& o) : owner_(o.owner_), ptr_(o.ptr_), label_(o.label_) {
+  View(const View<D2, P2...>& o) : rec_(o.rec_), ptr_(o.ptr_) {
+    if (!omp_in_parallel()) owner_ = o.owner_;
     for (int i = 0; i < 8; ++i) ext_[i] = o.ext_[i];
   }
 
@@ -418,7 +428,7 @@ template <class DataType, class... Properties> class View {
   }
   std::size_t span() const { return size(); }
   value_type* data() const { return ptr_; }
-  std::string label() const { return label_; }
+  std::string label() const { return rec_ ? rec_->label : std::string(); }
   bool is_allocated() const { return ptr_ != nullptr; }
   int use_count() const { return (int)owner_.use_count(); }
   std::size_t stride(int i) const {
@@ -446,11 +456,29 @@ template <class DataType, class... Properties> class View {
   }
   template <class I0> value_type& operator[](I0 i0) const { return ptr_[i0]; }
 
-  // shim internals (public so that views of other types can share them)
-  std::shared_ptr<non_const_value_type[]> owner_;
+  // shim internals (public so that views of other types can share them).
+  // Like Kokkos, a copy made inside a parallel region does not take part in
+  // the reference counting (no atomic traffic per sample): it points at the
+  // allocation record without owning it.
+  std::shared_ptr<shim::Record> owner_;
+  shim::Record* rec_ = nullptr;
   value_type* ptr_ = nullptr;
   std::size_t ext_[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  std::string label_;
+
+  View(const View& o) : rec_(o.rec_), ptr_(o.ptr_) {
+    if (!omp_in_parallel()) owner_ = o.owner_;
+    for (int i = 0; i < 8; ++i) ext_[i] = o.ext_[i];
+  }
+  View& operator=(const View& o) {
+    if (this != &o) {
+      if (!omp_in_parallel()) owner_ = o.owner_;
+      else owner_.reset();
+      rec_ = o.rec_;
+      ptr_ = o.ptr_;
+      for (int i = 0; i < 8; ++i) ext_[i] = o.ext_[i];
+    }
+    return *this;
+  }
 
  private:
   template <class... I> void set_extents(I... n) {
@@ -460,10 +488,22 @@ template <class DataType, class... Properties> class View {
   }
   template <class... I> void allocate(const shim::ViewAllocProp& p, I... n) {
     set_extents(n...);
-    label_ = p.label;
-    const std::size_t s = size();
-    owner_ = std::shared_ptr<non_const_value_type[]>(new non_const_value_type[s ? s : 1]());
-    ptr_ = owner_.get();
+    const std::size_t s = size() ? size() : 1;
+    if (p.initialize) {
+      // value-initialised in parallel (first touch by the threads that use it)
+      non_const_value_type* q = raw_alloc(s, p.label);
+#pragma omp parallel for schedule(static)
+      for (std::int64_t i = 0; i < (std::int64_t)s; ++i) q[i] = non_const_value_type();
+      ptr_ = q;
+    } else {
+      ptr_ = raw_alloc(s, p.label);  // WithoutInitializing: no construction, no touch
+    }
+  }
+  non_const_value_type* raw_alloc(std::size_t s, const std::string& label = std::string()) {
+    static_assert(std::is_trivially_copyable_v<non_const_value_type>, "the shim's Views hold trivial types");
+    owner_ = std::make_shared<shim::Record>(s * sizeof(non_const_value_type), label);
+    rec_ = owner_.get();
+    return reinterpret_cast<non_const_value_type*>(rec_->mem);
   }
 };
 
@@ -516,9 +556,9 @@ inline View<typename View<D, P...>::non_const_data_type, LayoutRight, HostSpace>
   using R = View<typename View<D, P...>::non_const_data_type, LayoutRight, HostSpace>;
   R r;
   r.owner_ = v.owner_;
+  r.rec_ = v.rec_;
   r.ptr_ = const_cast<typename R::value_type*>(v.data());
   for (int i = 0; i < 8; ++i) r.ext_[i] = v.ext_[i];
-  r.label_ = v.label_;
   return r;
 }
 

@@ -33,6 +33,9 @@
 
 #include "ponni.h"
 
+static_assert(sizeof(Kokkos::Experimental::half_t) == 2 && sizeof(Kokkos::Experimental::bhalf_t) == 2,
+              "16-bit types hold exactly their bits");
+
 namespace {
 
 using Half = Kokkos::Experimental::half_t;
@@ -64,7 +67,16 @@ int run(Model& model, const double* params, int64_t nparams, const void* in, int
   View1<real> p("ref_parameters", need);
   for (int i = 0; i < need; ++i) p(i) = static_cast<real>(params[i]);
   model.set_trainable_parameters(p);
-  const int nin = model.template get_num_inputs();
+  const int nin = model.template get_num_inputs(), nout = model.template get_num_outputs();
+  if (in_ld == batch && out_ld == batch) {
+    // Unmanaged Views over the caller's arrays (the 16-bit types have the
+    // memory layout of their bits): no copies around the forward.
+    using U2 = Kokkos::View<real**, Kokkos::LayoutRight, Kokkos::HostSpace, Kokkos::MemoryTraits<Kokkos::Unmanaged>>;
+    U2 x(reinterpret_cast<real*>(const_cast<void*>(in)), nin, batch);
+    U2 y(reinterpret_cast<real*>(out), nout, batch);
+    model.forward_batch_parallel(x, y);
+    return 0;
+  }
   View2<real> x("ref_input", nin, batch);
   for (int f = 0; f < nin; ++f)
     for (int64_t c = 0; c < batch; ++c) x(f, c) = load<real>(in, f * in_ld + c);
