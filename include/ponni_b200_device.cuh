@@ -191,12 +191,12 @@ __device__ void infer_one(const Model& m, const T* x, int64_t x_stride, T* y, in
         C<T> mx = buf[src][0];
         for (int i = 1; i < n; ++i) mx = buf[src][i] > mx ? buf[src][i] : mx;
         C<T> sum = C<T>(0);
-        for (int i = 0; i < n; ++i) sum = radd<T>(sum, m_exp(rsub<T>(buf[src][i], mx)));
+        for (int i = 0; i < n; ++i) sum = radd<T>(sum, sizeof(T) == 2 ? ponni_b200::e16_exp(rsub<T>(buf[src][i], mx)) : m_exp(rsub<T>(buf[src][i], mx)));
         if (s.kind == STEP_LOGSOFTMAX) {
-          const C<T> lse = radd<T>(m_log(sum), mx);
+          const C<T> lse = radd<T>(sizeof(T) == 2 ? ponni_b200::e16_log(sum) : m_log(sum), mx);
           for (int i = 0; i < n; ++i) buf[src][i] = rsub<T>(buf[src][i], lse);
         } else {
-          for (int i = 0; i < n; ++i) buf[src][i] = rdiv<T>(m_exp(rsub<T>(buf[src][i], mx)), sum);
+          for (int i = 0; i < n; ++i) buf[src][i] = rdiv<T>(sizeof(T) == 2 ? ponni_b200::e16_exp(rsub<T>(buf[src][i], mx)) : m_exp(rsub<T>(buf[src][i], mx)), sum);
         }
         break;
       }

@@ -94,40 +94,50 @@ __device__ __forceinline__ C activation(int kind, int flags, C x, C s0, C s1) {
 // stores it in a `real` (a local variable or the return value).  Each case
 // follows the apply() of the file listed in activation() above.  `r` rounds
 // a float to the model type and back.
+// The float transcendental functions of the 16-bit path, evaluated in double
+// and rounded once to float: the correctly rounded float value, which is what
+// a host C library returns in all but rare cases, so that the 16-bit result
+// (a rounding of that float) agrees with the reference's host arithmetic
+// instead of flipping wherever two float implementations differ by a unit.
+__device__ __forceinline__ float e16_exp(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float e16_log(float x) { return (float)log((double)x); }
+__device__ __forceinline__ float e16_tanh(float x) { return (float)tanh((double)x); }
+__device__ __forceinline__ float e16_erf(float x) { return (float)erf((double)x); }
+
 template <class R>
 __device__ __forceinline__ float activation16(int kind, int flags, float x, float s0, float s1, R r) {
   switch (kind) {
     case EPI_RELU: return x > 0.0f ? x : 0.0f;
     case EPI_LEAKY_RELU: return x > 0.0f ? x : r(s0 * x);
-    case EPI_ELU: return x > 0.0f ? x : r(s0 * (m_exp(x) - 1.0f));
+    case EPI_ELU: return x > 0.0f ? x : r(s0 * (e16_exp(x) - 1.0f));
     case EPI_SELU: {
       const float alpha = r(1.6732632423543772848f), scale = r(1.0507009873554804934f);
-      return x > 0.0f ? r(scale * x) : r(r(scale * alpha) * (m_exp(x) - 1.0f));
+      return x > 0.0f ? r(scale * x) : r(r(scale * alpha) * (e16_exp(x) - 1.0f));
     }
     case EPI_GELU: {
       if (flags & 0x2) {
         const float k = r(0.79788456080286535588f), c = r(0.044715f);
         const float x3 = r(r(x * x) * x);
-        const float t = m_tanh(r(k * r(x + r(c * x3))));
+        const float t = e16_tanh(r(k * r(x + r(c * x3))));
         return r(r(0.5f * x) * (1.0f + t));
       }
-      return r(r(0.5f * x) * (1.0f + m_erf(r(x / r(1.4142135623730950488f)))));
+      return r(r(0.5f * x) * (1.0f + e16_erf(r(x / r(1.4142135623730950488f)))));
     }
     case EPI_SILU: {
-      if (x >= 0.0f) return r(x / (1.0f + m_exp(-x)));
-      const float e = r(m_exp(x));
+      if (x >= 0.0f) return r(x / (1.0f + e16_exp(-x)));
+      const float e = r(e16_exp(x));
       return r(r(x * e) / r(1.0f + e));
     }
     case EPI_SIGMOID: {
-      if (x >= 0.0f) return r(1.0f / (1.0f + m_exp(-x)));
-      const float e = r(m_exp(x));
+      if (x >= 0.0f) return r(1.0f / (1.0f + e16_exp(-x)));
+      const float e = r(e16_exp(x));
       return r(e / r(1.0f + e));
     }
-    case EPI_TANH: return r(m_tanh(x));
+    case EPI_TANH: return r(e16_tanh(x));
     case EPI_SOFTPLUS: {
       const float sx = r(s0 * x);
-      if (sx > 0.0f) return r((sx + m_log(1.0f + m_exp(-sx))) / s0);
-      return r(m_log(1.0f + m_exp(sx)) / s0);
+      if (sx > 0.0f) return r((sx + e16_log(1.0f + e16_exp(-sx))) / s0);
+      return r(e16_log(1.0f + e16_exp(sx)) / s0);
     }
     case EPI_HARD_SIGMOID: {
       float v = r(r(s0 * x) + s1);
@@ -141,8 +151,8 @@ __device__ __forceinline__ float activation16(int kind, int flags, float x, floa
       return r(r(x * r6) / 6.0f);
     }
     case EPI_MISH: {
-      const float sp = x > 0.0f ? r(x + m_log(1.0f + m_exp(-x))) : r(m_log(1.0f + m_exp(x)));
-      return r(x * m_tanh(sp));
+      const float sp = x > 0.0f ? r(x + e16_log(1.0f + e16_exp(-x))) : r(e16_log(1.0f + e16_exp(x)));
+      return r(x * e16_tanh(sp));
     }
     default: return x;
   }

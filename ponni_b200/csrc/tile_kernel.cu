@@ -379,6 +379,17 @@ template <class T> __device__ __forceinline__ CT<T> rsub(CT<T> a, CT<T> b) { ret
 template <class T> __device__ __forceinline__ CT<T> rmul(CT<T> a, CT<T> b) { return rnd<T>(mul_rn(a, b)); }
 template <class T> __device__ __forceinline__ CT<T> rdiv(CT<T> a, CT<T> b) { return rnd<T>(div_rn(a, b)); }
 
+// exp / log of the softmax barriers: 16-bit models take the correctly rounded
+// float value (e16_exp / e16_log, the host C library's result).
+template <class T> __device__ __forceinline__ CT<T> x_exp(CT<T> v) {
+  if constexpr (sizeof(T) == 2) return e16_exp(v);
+  else return m_exp(v);
+}
+template <class T> __device__ __forceinline__ CT<T> x_log(CT<T> v) {
+  if constexpr (sizeof(T) == 2) return e16_log(v);
+  else return m_log(v);
+}
+
 // LayerNorm per column: two-pass mean and biased variance,
 // 1/sqrt(var + eps), gamma * xhat + beta (src/layers/ponni_LayerNorm.h:77-99).
 template <class T>
@@ -470,14 +481,14 @@ __device__ void softmax_step(const StepDesc& s, int bt, T* x) {
     // the reference stores them (src/layers/ponni_Softmax.h:46-57)
     C sum = C(0);
     for (int i = 0; i < n; ++i)
-      sum = radd<T>(sum, m_exp(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx)));
+      sum = radd<T>(sum, x_exp<T>(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx)));
     if (LOG) {
-      const C lse = radd<T>(m_log(sum), mx);
+      const C lse = radd<T>(x_log<T>(sum), mx);
       for (int i = 0; i < n; ++i)
         x[i * bt + c] = Num<T>::from_c(rsub<T>(Num<T>::to_c(x[i * bt + c]), lse));
     } else {
       for (int i = 0; i < n; ++i) {
-        const C e = m_exp(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx));
+        const C e = x_exp<T>(rsub<T>(Num<T>::to_c(x[i * bt + c]), mx));
         x[i * bt + c] = Num<T>::from_c(rdiv<T>(e, sum));
       }
     }
