@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include "tc_program.h"
+#include "f32x2.cuh"
 
 // Bound of every spin-wait of the tensor-core kernels, in SM cycles (about
 // one second).  The wait-bound test build (PONNI_B200_WAIT_TEST) shortens it.
@@ -269,6 +270,20 @@ __device__ __forceinline__ void split3(float x, uint32_t& h0, uint32_t& h1, uint
   h2 = __float_as_uint(r1 - __uint_as_float(h1));
 }
 
+// split3 of two values with packed fp32 subtractions (the same results).
+__device__ __forceinline__ void split3x2(float x, float y, uint32_t& h0, uint32_t& h1, uint32_t& h2, uint32_t& g0,
+                                         uint32_t& g1, uint32_t& g2) {
+  h0 = __float_as_uint(x) & 0xFFFF0000u;
+  g0 = __float_as_uint(y) & 0xFFFF0000u;
+  float r, t;
+  f2::sub(r, t, x, y, __uint_as_float(h0), __uint_as_float(g0));
+  h1 = __float_as_uint(r) & 0xFFFF0000u;
+  g1 = __float_as_uint(t) & 0xFFFF0000u;
+  f2::sub(r, t, r, t, __uint_as_float(h1), __uint_as_float(g1));
+  h2 = __float_as_uint(r);
+  g2 = __float_as_uint(t);
+}
+
 // Two bf16 parts (as fp32 bit patterns) -> one packed bf16x2 word (lo first).
 __device__ __forceinline__ uint32_t pack_hi16(uint32_t lo, uint32_t hi) { return __byte_perm(lo, hi, 0x7632); }
 
@@ -289,7 +304,8 @@ __device__ __forceinline__ void store_row8(const uint32_t* a, int m, int k0, con
   if constexpr (sizeof(T) == 4) {
     uint32_t p0[8], p1[8], p2[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) split3(v[e], p0[e], p1[e], p2[e]);
+    for (int e = 0; e < 8; e += 2)
+      split3x2(v[e], v[e + 1], p0[e], p1[e], p2[e], p0[e + 1], p1[e + 1], p2[e + 1]);
     st_shared_v4(a[0] + off, pack_hi16(p0[0], p0[1]), pack_hi16(p0[2], p0[3]), pack_hi16(p0[4], p0[5]),
                  pack_hi16(p0[6], p0[7]));
     st_shared_v4(a[1] + off, pack_hi16(p1[0], p1[1]), pack_hi16(p1[2], p1[3]), pack_hi16(p1[4], p1[5]),

@@ -48,6 +48,7 @@
 #include <cuda_runtime.h>
 
 #include "device_math.cuh"
+#include "f32x2.cuh"
 #include "tc_common.cuh"
 #include "tc_resid.h"
 
@@ -91,15 +92,28 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // error on [0, 12] (fit_gelu.py).  In float its maximum absolute error is
 // 3.8e-7 (the erf form in float: 4.5e-7) and its relative error in the left
 // tail stays below 1.5e-6, where the erf form cancels.
-__device__ __forceinline__ float gelu_phi(float x) {
-  const float t = fminf(fabsf(x), 12.0f);
-  const float e = ex2_approx(-(t * t) * 0.72134752044448170f);  // exp(-t^2 / 2)
-  const float p = fmaf(fmaf(fmaf(fmaf(0.00794154778122902f, t, 0.07927434146404266f), t, 0.3605049252510071f), t,
-                           0.8684397339820862f), t, 1.0f);
-  const float q = fmaf(fmaf(fmaf(fmaf(fmaf(0.009953089989721775f, t, 0.09936375170946121f), t, 0.4616026282310486f), t,
-                                1.1900357007980347f), t, 1.6663246154785156f), t, 1.0f);
-  const float tail = 0.5f * e * __fdividef(p, q);  // Phi(-|x|)
-  return x * (x >= 0.0f ? 1.0f - tail : tail);
+// Two values at a time with packed fp32 arithmetic.
+__device__ __forceinline__ void gelu_phi2(float& x0, float& x1) {
+  const float t0 = fminf(fabsf(x0), 12.0f), t1 = fminf(fabsf(x1), 12.0f);
+  float s0, s1;
+  f2::mul(s0, s1, t0, t1, t0, t1);
+  f2::mul(s0, s1, s0, s1, -0.72134752044448170f, -0.72134752044448170f);
+  const float e0 = ex2_approx(s0), e1 = ex2_approx(s1);
+  float p0, p1, q0, q1;
+  f2::fma(p0, p1, 0.00794154778122902f, 0.00794154778122902f, t0, t1, 0.07927434146404266f, 0.07927434146404266f);
+  f2::fma(p0, p1, p0, p1, t0, t1, 0.3605049252510071f, 0.3605049252510071f);
+  f2::fma(p0, p1, p0, p1, t0, t1, 0.8684397339820862f, 0.8684397339820862f);
+  f2::fma(p0, p1, p0, p1, t0, t1, 1.0f, 1.0f);
+  f2::fma(q0, q1, 0.009953089989721775f, 0.009953089989721775f, t0, t1, 0.09936375170946121f, 0.09936375170946121f);
+  f2::fma(q0, q1, q0, q1, t0, t1, 0.4616026282310486f, 0.4616026282310486f);
+  f2::fma(q0, q1, q0, q1, t0, t1, 1.1900357007980347f, 1.1900357007980347f);
+  f2::fma(q0, q1, q0, q1, t0, t1, 1.6663246154785156f, 1.6663246154785156f);
+  f2::fma(q0, q1, q0, q1, t0, t1, 1.0f, 1.0f);
+  float a0, a1;
+  f2::mul(a0, a1, e0, e1, 0.5f, 0.5f);
+  f2::mul(a0, a1, a0, a1, __fdividef(p0, q0), __fdividef(p1, q1));  // Phi(-|x|)
+  const float f0 = x0 >= 0.0f ? 1.0f - a0 : a0, f1 = x1 >= 0.0f ? 1.0f - a1 : a1;
+  f2::mul(x0, x1, x0, x1, f0, f1);
 }
 
 template <int K>
@@ -107,7 +121,7 @@ __device__ __forceinline__ void act32(float (&v)[32], int flags, float s0, float
   if constexpr (K == EPI_GELU) {
     if (!(flags & 0x2)) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_phi(v[j]);
+      for (int j = 0; j < 32; j += 2) gelu_phi2(v[j], v[j + 1]);
       return;
     }
   }
@@ -175,10 +189,8 @@ __device__ __forceinline__ void tr_ops(const TrOp* ops, int o0, int o1, float (&
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 b = __ldg(b4 + q);
-        v[4 * q] = __fadd_rn(v[4 * q], b.x);
-        v[4 * q + 1] = __fadd_rn(v[4 * q + 1], b.y);
-        v[4 * q + 2] = __fadd_rn(v[4 * q + 2], b.z);
-        v[4 * q + 3] = __fadd_rn(v[4 * q + 3], b.w);
+        f2::add(v[4 * q], v[4 * q + 1], v[4 * q], v[4 * q + 1], b.x, b.y);
+        f2::add(v[4 * q + 2], v[4 * q + 3], v[4 * q + 2], v[4 * q + 3], b.z, b.w);
       }
     } else if (o.kind == TR_ACT) {
 #if !(PONNI_B200_TR_DIAG & 1)  // diagnostic builds: bit 1 skips activations
@@ -189,10 +201,8 @@ __device__ __forceinline__ void tr_ops(const TrOp* ops, int o0, int o1, float (&
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 t = sv[q * 128];
-        v[4 * q] = __fadd_rn(v[4 * q], t.x);
-        v[4 * q + 1] = __fadd_rn(v[4 * q + 1], t.y);
-        v[4 * q + 2] = __fadd_rn(v[4 * q + 2], t.z);
-        v[4 * q + 3] = __fadd_rn(v[4 * q + 3], t.w);
+        f2::add(v[4 * q], v[4 * q + 1], v[4 * q], v[4 * q + 1], t.x, t.y);
+        f2::add(v[4 * q + 2], v[4 * q + 3], v[4 * q + 2], v[4 * q + 3], t.z, t.w);
       }
     } else if (o.kind == TR_SAVE) {
       float4* sv = E.saved + (size_t)o.arg * (kTrMaxN / 4) * 128 + (c0 / 4) * 128 + E.m;
@@ -246,13 +256,11 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
     float w[32];
     const uint32_t corr = E.tmem_row + (uint32_t)((groups - 1) * n_pad);
     tmem_ld32x2(corr + (uint32_t)c0, E.tmem_row + (uint32_t)c0, v, w);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += w[j];
+    f2::add_n(v, w);
 #pragma unroll 1
     for (int g = 1; g + 1 < groups; ++g) {
       tmem_ld32(E.tmem_row + (uint32_t)(g * n_pad + c0), w);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += w[j];
+      f2::add_n(v, w);
     }
     tr_ops(p.ops, o0, o_ln, v, c0, E);
   }
@@ -262,8 +270,10 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
     float psum = 0.f;
     if (active) {
       if (nv >= 32) {
+        float s0 = v[0], s1 = v[1];  // even and odd columns, combined at the end
 #pragma unroll
-        for (int j = 0; j < 32; ++j) psum = __fadd_rn(psum, v[j]);
+        for (int j = 2; j < 32; j += 2) f2::add(s0, s1, s0, s1, v[j], v[j + 1]);
+        psum = __fadd_rn(s0, s1);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
@@ -279,11 +289,15 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
     float pvar = 0.f;
     if (active) {
       if (nv >= 32) {
+        float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float d = __fsub_rn(v[j], mean);
-          pvar = __fadd_rn(pvar, __fmul_rn(d, d));
+        for (int j = 0; j < 32; j += 2) {
+          float d0, d1;
+          f2::sub(d0, d1, v[j], v[j + 1], mean, mean);
+          f2::mul(d0, d1, d0, d1, d0, d1);
+          f2::add(s0, s1, s0, s1, d0, d1);
         }
+        pvar = __fadd_rn(s0, s1);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
@@ -307,9 +321,13 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
         const float4 g = __ldg(g4 + q), b = __ldg(b4 + q);
         const float gg[4] = {g.x, g.y, g.z, g.w}, bb[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float xhat = __fmul_rn(__fsub_rn(v[4 * q + e], mean), inv_std);
-          v[4 * q + e] = __fadd_rn(__fmul_rn(gg[e], xhat), bb[e]);
+        for (int e = 0; e < 4; e += 2) {
+          float& x0 = v[4 * q + e];
+          float& x1 = v[4 * q + e + 1];
+          f2::sub(x0, x1, x0, x1, mean, mean);
+          f2::mul(x0, x1, x0, x1, inv_std, inv_std);  // xhat
+          f2::mul(x0, x1, x0, x1, gg[e], gg[e + 1]);
+          f2::add(x0, x1, x0, x1, bb[e], bb[e + 1]);
         }
       }
       tr_ops(p.ops, o_ln + 1, o_end, v, c0, E);
