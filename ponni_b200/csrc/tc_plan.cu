@@ -293,14 +293,22 @@ bool ts_plan(const ponni_b200_model* m, TsProgram& p, std::vector<unsigned char>
   }
   p.stage_bytes = (uint32_t)(p.layers[0].k_pad / 8) * 2048;
   p.a_bytes = std::max(a_blocks * (uint32_t)(kTcM * 128), (p.stage_bytes + 1023u) & ~1023u);
-  const uint32_t fixed = 1024 + kTsSlots * p.a_bytes + 256 + (uint32_t)(kTsMaxLayers * sizeof(TsLayer));
+  const uint32_t fixed = 1024 + kTsSlots * p.a_bytes + kTsBarBytes + (uint32_t)(kTsMaxLayers * sizeof(TsLayer));
   const uint32_t budget = 227 * 1024;
-  if (fixed + 2 * kTsChunkBytes > budget) {
+  // CTA pairs (M = 256 over two SMs, each staging half of every chunk) with
+  // PONNI_B200_TS_PAIR=1.  Off by default: on the 64->256x5->32 bf16 chain
+  // the pair is slower (148.6 against 126.2 ms per 2^27 columns), because the
+  // single CTA's MMA issue already runs at tensor-pipe speed and the pair
+  // couples two epilogues and adds a relay hop to every weight stage.
+  const char* pe = getenv("PONNI_B200_TS_PAIR");
+  p.pair = (pe && atoi(pe) == 1) ? 1 : 0;
+  const uint32_t stage = p.pair ? kTsChunkBytes / 2 : kTsChunkBytes;
+  if (fixed + 2 * stage > budget) {
     why = "operand tiles exceed shared memory";
     return false;
   }
-  p.ring_stages = std::min<uint32_t>(kTsMaxStages, (budget - fixed) / kTsChunkBytes);
-  p.smem_bytes = fixed + p.ring_stages * kTsChunkBytes;
+  p.ring_stages = std::min<uint32_t>(kTsMaxStages, (budget - fixed) / stage);
+  p.smem_bytes = fixed + p.ring_stages * stage;
   return true;
 }
 

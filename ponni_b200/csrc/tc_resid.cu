@@ -184,6 +184,9 @@ __device__ __forceinline__ int epi_sync_or(int pred) {
 __device__ __forceinline__ void tr_ops(const TrOp* ops, int o0, int o1, float (&v)[32], int c0, const TrEpi& E) {
   for (int i = o0; i < o1; ++i) {
     const TrOp o = ops[i];
+#if PONNI_B200_TR_DIAG & 8  // diagnostic builds: bit 8 skips the saved-state traffic
+    if (o.kind == TR_ADD || o.kind == TR_SAVE) continue;
+#endif
     if (o.kind == TR_BIAS) {
       const float4* b4 = reinterpret_cast<const float4*>(E.image + o.off) + c0 / 4;
 #pragma unroll
@@ -246,7 +249,7 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
   const int n_pad = L.n_pad, nout = L.nout, groups = L.groups;
   const bool last = l == p.n_layers - 1;
   const int o0 = L.op_first, o_end = o0 + L.n_ops;
-  const bool has_ln = L.ln >= 0;
+  const bool has_ln = L.ln >= 0 && !(PONNI_B200_TR_DIAG & 2);  // diagnostic builds: bit 2 skips LayerNorm
   const int o_ln = has_ln ? o0 + L.ln : o_end;
   const int c0 = E.cq * 32;
   const bool active = c0 < n_pad;  // warp-uniform
@@ -375,7 +378,8 @@ __device__ __forceinline__ bool tr_chunk(TrIssue& I, int kb, int nsteps, uint32_
   (void)w_full;
   const uint32_t st = use & 1u;
   TR_T(tf);
-  if (!wait_phase_abort(b_full + 8u * st, (use >> 1) & 1u, abort_flag, kWaitCycles)) return false;
+  if (!__all_sync(0xffffffffu, wait_phase_abort(b_full + 8u * st, (use >> 1) & 1u, abort_flag, kWaitCycles)))
+    return false;
   TR_ACC(w_full, tf);
   tc_fence_after();
   const uint32_t b = ring_lo + st * (kTrChunkBytes >> 4);
@@ -385,14 +389,14 @@ __device__ __forceinline__ bool tr_chunk(TrIssue& I, int kb, int nsteps, uint32_
       const uint32_t ao = (uint32_t)kb * 1024u + (uint32_t)kk * 2u;  // K block: 16 KB; K step: 32 B
       const uint32_t bk = b + (uint32_t)kk * 2u;
       if constexpr (J == 0) {
-        umma_f16_lh(I.dc, I.a0 + ao, bk, I.hi, I.idesc, (kb | kk) ? 1u : 0u);
+        umma_f16_lh_warp(I.dc, I.a0 + ao, bk, I.hi, I.idesc, (kb | kk) ? 1u : 0u);
       } else if constexpr (J == 1) {
-        umma_f16_lh(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
-        umma_f16_lh(I.dc, I.a0 + ao, bk, I.hi, I.idesc, 1u);
+        umma_f16_lh_warp(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
+        umma_f16_lh_warp(I.dc, I.a0 + ao, bk, I.hi, I.idesc, 1u);
       } else {
-        umma_f16_lh(I.dc, I.a2 + ao, bk, I.hi, I.idesc, 1u);
-        umma_f16_lh(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
-        umma_f16_lh(I.d_main, I.a0 + ao, bk, I.hi, I.idesc, I.g_in ? 1u : 0u);
+        umma_f16_lh_warp(I.dc, I.a2 + ao, bk, I.hi, I.idesc, 1u);
+        umma_f16_lh_warp(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
+        umma_f16_lh_warp(I.d_main, I.a0 + ao, bk, I.hi, I.idesc, I.g_in ? 1u : 0u);
         if (++I.g_in == I.gs) {
           I.g_in = 0;
           I.d_main += I.n_pad;
@@ -400,7 +404,7 @@ __device__ __forceinline__ bool tr_chunk(TrIssue& I, int kb, int nsteps, uint32_
       }
     }
   }
-  umma_commit(b_empty + 8u * st);
+  umma_commit_warp(b_empty + 8u * st);
   ++use;
   return true;
 }
@@ -505,7 +509,9 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     __syncwarp();
   } else if (warp == kTrMmaWarp) {
     // --------------------------------------------- MMA issuer ----
-    if (lane == 0) {
+    // The whole warp runs the issue loop (its values stay warp-uniform); one
+    // elected lane issues each MMA and commit.
+    {
       uint32_t use = 0, ep0 = 0, ep1 = 0;
       bool ok = true;
       bool skip = PONNI_B200_SKIP_ARRIVE();  // wait-bound test build: drop the first job's signal
@@ -524,7 +530,8 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             if (r >= (s ? jobs.c1 : jobs.c0)) continue;
             // The slot's operand is written and its accumulators are free.
             TR_T(te);
-            if (!(ok = wait_phase_abort(b_epid + 8u * s, s ? ep1 : ep0, abort_flag, kWaitCycles))) break;
+            if (!(ok = __all_sync(0xffffffffu, wait_phase_abort(b_epid + 8u * s, s ? ep1 : ep0, abort_flag, kWaitCycles))))
+              break;
             if (s) ep1 ^= 1u;
             else ep0 ^= 1u;
             TR_ACC(w_epi, te);
@@ -546,21 +553,23 @@ __global__ void __launch_bounds__(kTrThreads, 1)
                    tr_chunk<1>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full) &&
                    tr_chunk<2>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full);
             }
-            if (ok && !skip) umma_commit(b_accf + 8u * s);
+            if (ok && !skip) umma_commit_warp(b_accf + 8u * s);
             skip = false;
           }
         }
       // Drain: every MMA issued has completed before TMEM is freed.
-      umma_commit(b_drain);
+      umma_commit_warp(b_drain);
       const long long t0 = clock64();
       while (!mbar_try_wait(b_drain, 0))
         if (clock64() - t0 > kWaitCycles) break;
-      if (!ok) atomicExch(err, 3);
-      TR_FLUSH(1, w_epi);
-      TR_FLUSH(2, w_full);
+      if (lane == 0) {
+        if (!ok) atomicExch(err, 3);
+        TR_FLUSH(1, w_epi);
+        TR_FLUSH(2, w_full);
 #ifdef PONNI_B200_TC_PROFILE
-      TR_FLUSH(7, clock64() - t_all);
+        TR_FLUSH(7, clock64() - t_all);
 #endif
+      }
     }
     __syncwarp();
   } else {

@@ -8,7 +8,8 @@
 //     reads the same image) into a ring of shared-memory stages with 1-D bulk
 //     copies (cp.async.bulk, completion counted in bytes on the stage's
 //     "full" mbarrier; no multicast);
-//   MMA issuer (warp 17, one thread): per job (one layer of one tile)
+//   MMA issuer (warp 17, issue loop run by the whole warp, one elected lane
+//     issues): per job (one layer of one tile)
 //     issues D[128 x N<=256] += A[128 x K] * B[N x K]^T chunk by chunk
 //     (tcgen05.mma kind::f16, fp32 accumulator in the slot's 256 TMEM
 //     columns), frees each ring stage with tcgen05.commit and signals the
@@ -22,6 +23,11 @@
 //     signals its own mbarrier.  They also stage each tile's input (cp.async,
 //     the MN-major layer-0 operand, in the same buffer) once the slot's last
 //     layer has consumed the buffer.
+// Pair mode (the default; clusters of two CTAs on two SMs): the even CTA
+// issues M = 256 MMAs (tcgen05 cta_group::2) over both CTAs' tiles, each
+// CTA streams only half of every weight chunk (N / 2 rows) into its own
+// ring, and the odd CTA's MMA warp relays the arrival of its half; this
+// halves the weight bytes staged and the MMA instructions issued per SM.
 // Two tiles (slots) are in flight and their jobs alternate layer by layer,
 // so one slot's epilogue runs while the tensor core works on the other's;
 // the two epilogue groups run independently, which keeps the MUFU unit fed
@@ -34,6 +40,8 @@
 // Every wait is bounded; a role that gives up raises a shared abort flag
 // (the others see it and leave), records an error code, and the CTA drains
 // its bulk copies and MMAs before it frees TMEM and returns.
+#include <algorithm>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -205,20 +213,33 @@ __device__ __forceinline__ void ts_load_tile(uint32_t buf, unsigned char* buf_pt
 
 // Job order shared by the three roles: rounds of two tiles (one per slot);
 // within a round, layer by layer, slot 0's job then slot 1's.  Slot s's
-// j-th tile is this CTA's tile 2j + s of the grid-strided sequence.
+// j-th tile is this CTA's tile 2j + s of the grid-strided sequence.  In pair
+// mode the sequence runs over pairs of adjacent tiles, one per cluster of
+// two CTAs, and CTA r of the pair takes tile 2 * pair + r (a tile past the
+// batch is computed on zero columns and not stored).
 struct TsJobs {
-  int64_t first, stride, ntiles;
+  int64_t first, stride, units;
   int64_t count[kTsSlots];
-  __device__ TsJobs(int64_t ntiles_, int64_t first_, int64_t stride_) : first(first_), stride(stride_), ntiles(ntiles_) {
-    const int64_t mine = first_ < ntiles_ ? (ntiles_ - first_ + stride_ - 1) / stride_ : 0;
+  int per, rank;
+  __device__ TsJobs(int64_t units_, int64_t first_, int64_t stride_, int per_, int rank_)
+      : first(first_), stride(stride_), units(units_), per(per_), rank(rank_) {
+    const int64_t mine = first_ < units_ ? (units_ - first_ + stride_ - 1) / stride_ : 0;
     count[0] = (mine + 1) / 2;
     count[1] = mine / 2;
   }
   __device__ int64_t rounds() const { return count[0]; }
-  __device__ int64_t tile(int s, int64_t r) const { return first + (2 * r + s) * stride; }
+  __device__ int64_t tile(int s, int64_t r) const { return (first + (2 * r + s) * stride) * per + rank; }
 };
 
-template <class T>
+// Single CTA (PAIR false): the CTA issues M = 128 MMAs over its own tile.
+// CTA pair (PAIR true, clusters of two): the even CTA issues M = 256 MMAs
+// (cta_group::2) over both CTAs' tiles; each CTA streams half of every
+// weight chunk (N / 2 rows) into its own ring with its own bulk copies, the
+// odd CTA's MMA warp relays "my half has landed" to the even CTA, the
+// commits signal both CTAs, and the odd CTA's epilogue warps arrive on the
+// even CTA's operand barriers.  Per SM this halves the weight bytes staged
+// and the MMA instructions issued.
+template <class T, bool PAIR>
 __global__ void __launch_bounds__(kTsThreads, 1)
     ts_forward_kernel(const __grid_constant__ TsProgram p, const unsigned char* __restrict__ image,
                       const T* __restrict__ in, int64_t in_ld, T* __restrict__ out, int64_t out_ld, int64_t batch,
@@ -229,10 +250,13 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   unsigned char* base_ptr = smem_raw + (base - raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int R = (int)p.ring_stages;
+  const uint32_t crank = PAIR ? cluster_rank() : 0u;
+  const bool leader = crank == 0;
+  constexpr uint32_t kStage = PAIR ? kTsChunkBytes / 2 : kTsChunkBytes;
 
   const uint32_t s_a[kTsSlots] = {base, base + p.a_bytes};  // per-slot operand buffer (input stage inside)
   const uint32_t s_ring = base + kTsSlots * p.a_bytes;
-  const uint32_t s_bars = s_ring + (uint32_t)R * kTsChunkBytes;
+  const uint32_t s_bars = s_ring + (uint32_t)R * kStage;
   const uint32_t b_full = s_bars;          // [R]
   const uint32_t b_empty = s_bars + 64;    // [R]
   const uint32_t b_accf = s_bars + 128;    // [slot]
@@ -240,25 +264,39 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   const uint32_t b_stage = s_bars + 208;   // [slot]
   const uint32_t b_drain = s_bars + 224;
   const uint32_t s_tmem = s_bars + 232;
+  const uint32_t b_pfull = s_bars + 256;   // [R] pair mode: the odd CTA's half of the stage has landed
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(base_ptr + (s_tmem - base));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + (s_tmem + 4 - base));
-  TsLayer* layers = reinterpret_cast<TsLayer*>(base_ptr + (s_bars + 256 - base));
+  TsLayer* layers = reinterpret_cast<TsLayer*>(base_ptr + (s_bars + kTsBarBytes - base));
 
   const int64_t ntiles = (batch + kTcM - 1) / kTcM;
-  if ((int64_t)blockIdx.x >= ntiles) return;
-  const TsJobs jobs(ntiles, blockIdx.x, gridDim.x);
+  const int64_t units = PAIR ? (ntiles + 1) / 2 : ntiles;
+  const int64_t unit = PAIR ? (int64_t)(blockIdx.x >> 1) : (int64_t)blockIdx.x;
+  const int64_t nunits_grid = PAIR ? (int64_t)(gridDim.x >> 1) : (int64_t)gridDim.x;
+  if (unit >= units) return;  // both CTAs of a pair leave together
+  const TsJobs jobs(units, unit, nunits_grid, PAIR ? 2 : 1, (int)crank);
+
+  // Where this CTA's epilogue signals the MMA issuer: its own barriers, or
+  // in pair mode the even CTA's.
+  const uint32_t kbar_sig = PAIR ? mapa_shared(b_kbar, 0) : b_kbar;
+  const uint32_t stage_sig = PAIR ? mapa_shared(b_stage, 0) : b_stage;
 
   // ---- set-up ----
-  if (warp == kTsMmaWarp) tmem_alloc(s_tmem, 512);
+  if (warp == kTsMmaWarp) {
+    if constexpr (PAIR) tmem_alloc_pair(s_tmem, 512);
+    else tmem_alloc(s_tmem, 512);
+  }
   if (tid == 0) {
+    const uint32_t peers = PAIR ? 2u : 1u;
     for (int r = 0; r < R; ++r) {
       mbar_init(b_full + 8u * r, 1);
       mbar_init(b_empty + 8u * r, 1);
+      mbar_init(b_pfull + 8u * r, 1);
     }
     for (int s = 0; s < kTsSlots; ++s) {
       mbar_init(b_accf + 8u * s, 1);
-      for (int h = 0; h < 2; ++h) mbar_init(b_kbar + 8u * (2 * s + h), 4);
-      mbar_init(b_stage + 8u * s, kTsGroupWarps);
+      for (int h = 0; h < 2; ++h) mbar_init(b_kbar + 8u * (2 * s + h), 4 * peers);
+      mbar_init(b_stage + 8u * s, kTsGroupWarps * peers);
     }
     mbar_init(b_drain, 1);
     *abort_flag = 0;
@@ -266,7 +304,8 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   }
   for (int i = tid; i < p.n_layers; i += kTsThreads) layers[i] = p.layers[i];
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers exist before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int nl = p.n_layers;
@@ -281,7 +320,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
           for (int s = 0; s < kTsSlots && ok; ++s) {
             if (r >= jobs.count[s]) continue;
             const TsLayer& L = layers[l];
-            const uint32_t bytes = (uint32_t)L.n_pad * 128u;
+            // pair mode: this CTA's half of the chunk's n_pad rows
+            const uint32_t bytes = (uint32_t)L.n_pad * (PAIR ? 64u : 128u);
+            const uint64_t half = PAIR ? (uint64_t)crank * bytes : 0u;
             for (int kb = 0; kb < L.kblk; ++kb) {
               const uint32_t st = use % (uint32_t)R;
               if (use >= (uint32_t)R && !wait_phase(b_empty + 8u * st, ((use / R) - 1) & 1u, abort_flag)) {
@@ -289,7 +330,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
                 break;
               }
               mbar_expect_tx(b_full + 8u * st, bytes);
-              bulk_load(s_ring + st * kTsChunkBytes, image + L.w_off + (uint64_t)kb * kTsChunkBytes, bytes,
+              bulk_load(s_ring + st * kStage, image + L.w_off + (uint64_t)kb * kTsChunkBytes + half, bytes,
                         b_full + 8u * st);
               ++use;
             }
@@ -304,9 +345,33 @@ __global__ void __launch_bounds__(kTsThreads, 1)
       if (!ok) atomicExch(err, 2);
     }
     __syncwarp();
+  } else if (warp == kTsMmaWarp && PAIR && !leader) {
+    // ----------------------------- relay (odd CTA of a pair) ----
+    // Tell the even CTA, stage by stage and in job order, that this CTA's
+    // half of the chunk has landed.
+    if (lane == 0) {
+      const uint32_t pfull_sig = mapa_shared(b_pfull, 0);
+      uint32_t use = 0;
+      bool ok = true;
+      for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
+        for (int l = 0; l < nl && ok; ++l)
+          for (int s = 0; s < kTsSlots && ok; ++s) {
+            if (r >= jobs.count[s]) continue;
+            for (int kb = 0; kb < layers[l].kblk; ++kb) {
+              const uint32_t st = use % (uint32_t)R;
+              if (!(ok = wait_phase(b_full + 8u * st, (use / R) & 1u, abort_flag))) break;
+              mbar_arrive_cluster(pfull_sig + 8u * st);
+              ++use;
+            }
+          }
+      if (!ok) atomicExch(err, 3);
+    }
+    __syncwarp();
   } else if (warp == kTsMmaWarp) {
     // --------------------------------------------- MMA issuer ----
-    if (lane == 0) {
+    // The whole warp runs the issue loop (warp-uniform values), one elected
+    // lane issues each MMA and commit.
+    {
       uint32_t use = 0, st_ph[kTsSlots] = {0, 0}, k_ph[kTsSlots] = {0, 0};
       bool has_prev[kTsSlots] = {false, false};
       bool ok = true;
@@ -314,6 +379,17 @@ __global__ void __launch_bounds__(kTsThreads, 1)
       long long w_epi = 0, w_full = 0;
       (void)w_epi; (void)w_full;
       TS_T(t_all);
+      // Cluster-scope acquire where the odd CTA arrives (pair mode).
+      auto wait_x = [&](uint32_t bar, uint32_t par) -> bool {
+        const bool got = PAIR ? wait_phase_abort_cluster(bar, par, abort_flag, kWaitCycles)
+                              : wait_phase(bar, par, abort_flag);
+        return __all_sync(0xffffffffu, got);
+      };
+      const uint32_t hi_k = (uint32_t)(smem_desc(0, 16, 1024) >> 32);
+      const uint32_t lo_k = (uint32_t)smem_desc(0, 16, 1024);
+      const uint32_t hi_mn = (uint32_t)(smem_desc(0, 1024, 2048) >> 32);
+      const uint32_t lo_mn = (uint32_t)smem_desc(0, 1024, 2048);
+      const uint32_t ring_lo = lo_k | ((s_ring >> 4) & 0x3FFFu);
       for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
         for (int l = 0; l < nl && ok; ++l)
           for (int s = 0; s < kTsSlots && ok; ++s) {
@@ -321,13 +397,13 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             const TsLayer& L = layers[l];
             TS_T(tw);
             if (l == 0) {
-              if (!(ok = wait_phase(b_stage + 8u * s, st_ph[s], abort_flag))) break;
+              if (!(ok = wait_x(b_stage + 8u * s, st_ph[s]))) break;
               st_ph[s] ^= 1u;
             }
             // The slot's previous epilogue has read its accumulator and
-            // written the operand (both column halves).
+            // written the operand (both column halves, both CTAs).
             if (has_prev[s]) {
-              for (int h = 0; h < 2 && ok; ++h) ok = wait_phase(b_kbar + 8u * (2 * s + h), k_ph[s], abort_flag);
+              for (int h = 0; h < 2 && ok; ++h) ok = wait_x(b_kbar + 8u * (2 * s + h), k_ph[s]);
               k_ph[s] ^= 1u;
             }
             if (!ok) break;
@@ -335,38 +411,53 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             has_prev[s] = true;
             tc_fence_after();
             const int nsteps = L.k_pad / 16;
-            const uint32_t idesc = idesc_of(p.dtype, L.n_pad, l == 0);
+            uint32_t idesc = idesc_of(p.dtype, L.n_pad, l == 0);
+            if constexpr (PAIR) idesc = (idesc & ~(0x1Fu << 24)) | ((uint32_t)(2 * kTcM >> 4) << 24);  // M = 256
             const uint32_t d = tmem_base + (uint32_t)(s * kTsMaxN);
-            const uint64_t a0 = l == 0 ? smem_desc(s_a[s], 1024, 2048) : smem_desc(s_a[s], 16, 1024);
+            const uint32_t a_lo = (l == 0 ? lo_mn : lo_k) | ((s_a[s] >> 4) & 0x3FFFu);
+            const uint32_t a_hi = l == 0 ? hi_mn : hi_k;  // the weights (B) are always K-major
             for (int kb = 0; kb < L.kblk; ++kb) {
               const uint32_t st = use % (uint32_t)R;
               TS_T(t2);
-              if (!(ok = wait_phase(b_full + 8u * st, (use / R) & 1u, abort_flag))) break;
+              ok = __all_sync(0xffffffffu, wait_phase(b_full + 8u * st, (use / R) & 1u, abort_flag));
+              if (PAIR && ok) ok = wait_x(b_pfull + 8u * st, (use / R) & 1u);
+              if (!ok) break;
               TS_ACC(w_full, t2);
               tc_fence_after();
-              const uint64_t b0 = smem_desc(s_ring + st * kTsChunkBytes, 16, 1024);
+              const uint32_t b_lo = ring_lo + st * (kStage >> 4);
               const int s_end = min(nsteps, kb * 4 + 4);
               for (int k = kb * 4; k < s_end; ++k) {
-                const uint64_t a = l == 0 ? a0 + (uint64_t)k * 256 : a0 + (uint64_t)(k >> 2) * 1024 + (uint64_t)(k & 3) * 2;
-                umma_f16(d, a, b0 + (uint64_t)(k & 3) * 2, idesc, k > 0 ? 1u : 0u);
+                // start-address advance in 16-byte units: MN-major, 4 KB per K step of 16;
+                // K-major, 16 KB per K block of 64 and 32 B per K step
+                const uint32_t ao = l == 0 ? (uint32_t)k * 256u : (uint32_t)(k >> 2) * 1024u + (uint32_t)(k & 3) * 2u;
+                const uint32_t bk = b_lo + (uint32_t)(k & 3) * 2u;
+                if constexpr (PAIR) umma_f16_pair_warp(d, a_lo + ao, a_hi, bk, hi_k, idesc, k > 0 ? 1u : 0u);
+                else umma_f16_desc_warp(d, a_lo + ao, a_hi, bk, hi_k, idesc, k > 0 ? 1u : 0u);
               }
-              umma_commit(b_empty + 8u * st);
+              if constexpr (PAIR) umma_commit_pair_warp(b_empty + 8u * st);
+              else umma_commit_warp(b_empty + 8u * st);
               ++use;
             }
-            if (ok && !skip) umma_commit(b_accf + 8u * s);
+            if (ok && !skip) {
+              if constexpr (PAIR) umma_commit_pair_warp(b_accf + 8u * s);
+              else umma_commit_warp(b_accf + 8u * s);
+            }
             skip = false;
           }
-      // Drain: every MMA issued has completed before TMEM is freed.
-      umma_commit(b_drain);
+      // Drain: every MMA issued has completed before TMEM is freed (both CTAs).
+      if constexpr (PAIR) umma_commit_pair_warp(b_drain);
+      else umma_commit_warp(b_drain);
       const long long t0 = clock64();
       while (!mbar_try_wait(b_drain, 0))
         if (clock64() - t0 > kWaitCycles) break;
-      if (!ok) atomicExch(err, 3);
-      TS_FLUSH(1, w_epi);
-      TS_FLUSH(6, w_full);
+      if (lane == 0) {
+        if (!ok) atomicExch(err, 3);
+        TS_FLUSH(1, w_epi);
+        TS_FLUSH(6, w_full);
 #ifdef PONNI_B200_TC_PROFILE
-      TS_FLUSH(7, clock64() - t_all);
+        TS_FLUSH(7, clock64() - t_all);
 #endif
+      }
     }
     __syncwarp();
   } else {
@@ -382,12 +473,18 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     long long w_acc = 0, c_epi = 0, t_ph[3] = {0, 0, 0};
     (void)w_acc; (void)c_epi;
     unsigned char* a_ptr = base_ptr + (s_a[s] - base);
+    // Operand written / accumulator read: local arrive, or in pair mode a
+    // cluster-scope arrive on the even CTA's barrier.
+    auto signal = [&](uint32_t bar) {
+      if constexpr (PAIR) mbar_arrive_cluster(bar);
+      else mbar_arrive(bar);
+    };
     if (jobs.count[s] > 0) {
       ts_load_tile<T>(s_a[s], a_ptr, in, in_ld, p.nin, k0, jobs.tile(s, 0), batch, vec, gtid);
       cp_async_wait_0();
       fence_proxy_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(b_stage + 8u * s);
+      if (lane == 0) signal(stage_sig + 8u * s);
     }
     for (int64_t r = 0; r < jobs.count[s] && ok; ++r)
       for (int l = 0; l < nl && ok; ++l) {
@@ -418,12 +515,12 @@ __global__ void __launch_bounds__(kTsThreads, 1)
         fence_proxy_async();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(b_kbar + 8u * (2 * s + ch));
+        if (lane == 0) signal(kbar_sig + 8u * (2 * s + ch));
         if (refill) {
           cp_async_wait_0();
           fence_proxy_async();
           __syncwarp();
-          if (lane == 0) mbar_arrive(b_stage + 8u * s);
+          if (lane == 0) signal(stage_sig + 8u * s);
         }
         TS_ACC(c_epi, t1);
       }
@@ -438,24 +535,49 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the even CTA's MMAs (which read this CTA's memory) are complete
+  else __syncthreads();
   if (warp == kTsMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, 512);
+    else tmem_dealloc(tmem_base, 512);
   }
 }
 
 template <class T>
 cudaError_t launch_impl(const TsProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
                         int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream) {
-  auto kern = ts_forward_kernel<T>;
+  const bool vec = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && ((in_ld * (int64_t)sizeof(T)) % 16 == 0);
+  const unsigned char* img = static_cast<const unsigned char*>(image);
+  const T* x = static_cast<const T*>(in);
+  T* y = static_cast<T*>(out);
+  if (!p.pair) {
+    auto kern = ts_forward_kernel<T, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kTsThreads, p.smem_bytes, stream>>>(p, img, x, in_ld, y, out_ld, batch, vec ? 1 : 0, err);
+    return cudaGetLastError();
+  }
+  // Clusters of two CTAs; the grid is a whole number of pairs, at most one
+  // pair per pair of tiles.
+  auto kern = ts_forward_kernel<T, true>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
   if (e != cudaSuccess) return e;
-  const bool vec = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && ((in_ld * (int64_t)sizeof(T)) % 16 == 0);
-  kern<<<grid, kTsThreads, p.smem_bytes, stream>>>(p, static_cast<const unsigned char*>(image),
-                                                   static_cast<const T*>(in), in_ld, static_cast<T*>(out), out_ld,
-                                                   batch, vec ? 1 : 0, err);
-  return cudaGetLastError();
+  const int64_t ntiles = (batch + kTcM - 1) / kTcM;
+  const int64_t pairs = std::max<int64_t>(1, std::min<int64_t>(grid / 2, (ntiles + 1) / 2));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kTsThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem_bytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p, img, x, in_ld, y, out_ld, batch, vec ? 1 : 0, err);
 }
 
 }  // namespace

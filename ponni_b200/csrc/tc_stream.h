@@ -31,6 +31,7 @@ constexpr int kTsProducerWarp = kTsEpiWarps;
 constexpr int kTsMmaWarp = kTsEpiWarps + 1;
 constexpr int kTsThreads = (kTsEpiWarps + 2) * 32;  // + producer warp + MMA warp
 constexpr int kTsMaxStages = 8;
+constexpr int kTsBarBytes = 320;                // mbarriers, TMEM address and abort flag, then the layer table
 
 struct TsLayer {
   int32_t nin, nout;
@@ -50,7 +51,8 @@ struct TsProgram {
   int32_t fast_act;       // SiLU / sigmoid / tanh through the hardware approximations (fp32 accumulation mode)
   uint32_t a_bytes;       // one tile's activation operand buffer (also holds its MN-major input stage)
   uint32_t stage_bytes;   // MN-major layer-0 input stage (inside the operand buffer)
-  uint32_t ring_stages;   // weight ring stages of kTsChunkBytes
+  uint32_t ring_stages;   // weight ring stages of kTsChunkBytes (pair mode: of kTsChunkBytes / 2)
+  int32_t pair;           // clusters of two CTAs sharing M = 256 MMAs (cta_group::2)
   uint32_t smem_bytes;    // dynamic shared memory requested
   uint64_t image_bytes;   // weight chunks + biases
   TsLayer layers[kTsMaxLayers];

@@ -195,6 +195,25 @@ def test_ts_strided_misaligned(oracle_lib):
     assert torch.isnan(out_big[:, 0].float()).all() and torch.isnan(out_big[:, 1001:].float()).all()
 
 
+@pytest.mark.parametrize("batch", [1, 129, 3000, 70000])
+def test_ts_cta_pair_mode(batch, oracle_lib, monkeypatch):
+    """Clusters of two CTAs sharing M = 256 MMAs (cta_group::2), each staging
+    half of every weight chunk: same results as the single-CTA kernel."""
+    monkeypatch.setenv("PONNI_B200_TS_PAIR", "1")
+    cfg = configs.cfg5(batch=batch)
+    x = configs.host_inputs(cfg, batch)
+    y = run_ts(cfg.layers, cfg.dtype, x)
+    check_acc32(y, cfg.layers, cfg.dtype, x, oracle_lib)
+    monkeypatch.setenv("PONNI_B200_TS_PAIR", "0")
+    assert np.array_equal(y, run_ts(cfg.layers, cfg.dtype, x))
+
+
+@pytest.mark.parametrize("dtype", [pb.F16, pb.BF16])
+def test_ts_cta_pair_odd_widths(dtype, oracle_lib, monkeypatch):
+    monkeypatch.setenv("PONNI_B200_TS_PAIR", "1")
+    test_ts_odd_widths_all_activations(dtype, oracle_lib, monkeypatch)
+
+
 # ---- LayerNorm / residual chains (fp32 split, weights streamed) ----
 
 def run_tr(layers, x_raw, monkeypatch=None, grid=None, arithmetic=None):
