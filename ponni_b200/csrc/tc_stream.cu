@@ -41,9 +41,13 @@
 // (the others see it and leave), records an error code, and the CTA drains
 // its bulk copies and MMAs before it frees TMEM and returns.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <type_traits>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "device_math.cuh"
@@ -52,11 +56,30 @@
 
 PONNI_B200_SKIP_ARRIVE_FLAG(ts)
 
+#ifndef PONNI_B200_TS_DIAG
+#define PONNI_B200_TS_DIAG 0
+#endif
+#if PONNI_B200_TS_DIAG & 4  // diagnostic builds: bit 4 removes the epilogue work
+#define PONNI_B200_TS_NO_EPI
+#endif
+
 namespace ponni_b200 {
 namespace {
 using namespace tc;
 
 constexpr long long kWaitCycles = PONNI_B200_WAIT_LIMIT;
+
+// Epilogue organisation: all 16 epilogue warps on every job (4 TMEM lane
+// quarters x 4 column quarters of 64), or (diagnostic builds, bit 8) one
+// group of 8 warps per slot (4 lane quarters x 2 column halves of 128).
+#if PONNI_B200_TS_DIAG & 8
+constexpr bool kTsEpiAll = false;
+#else
+constexpr bool kTsEpiAll = true;
+#endif
+constexpr int kTsEpiCols = kTsEpiAll ? kTsMaxN / 4 : kTsMaxN / 2;     // accumulator columns per warp and job
+constexpr int kTsEpiLoaders = kTsEpiAll ? kTsEpiWarps * 32 : kTsGroupThreads;  // threads staging a tile
+constexpr int kTsEpiHalfWarps = kTsEpiAll ? 8 : 4;                   // warps signalling one column half
 
 // Optional phase timing (compiled only with -DPONNI_B200_TC_PROFILE): each
 // role sums the cycles of its waits locally and adds them once per CTA to
@@ -128,7 +151,7 @@ __device__ __forceinline__ void ts_act32(float (&v)[32], int fast, int flags, fl
   for (int j = 0; j < 32; ++j) v[j] = ts_act<ACT>(v[j], fast, flags, s0, s1);
 }
 
-// Epilogue of the columns [c_begin, c_begin + kTsColsPerWarp) of one job
+// Epilogue of the columns [c_begin, c_begin + kTsEpiCols) of one job
 // for this thread's row m: accumulator -> bias -> activation -> the tile's
 // K-major operand (in place: the job's MMAs have completed) or the output.
 template <class T, int ACT>
@@ -139,7 +162,7 @@ __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool las
   const int n_pad = L.n_pad, nout = L.nout, has_bias = L.has_bias, flags = L.act_flags;
   const float s0 = L.s0, s1 = L.s1;
 #pragma unroll 1
-  for (int c0 = c_begin; c0 < c_begin + kTsColsPerWarp && c0 < n_pad; c0 += 32) {
+  for (int c0 = c_begin; c0 < c_begin + kTsEpiCols && c0 < n_pad; c0 += 32) {
     float v[32];
     TS_T(tl);
     tmem_ld32(tmem_row + (uint32_t)c0, v);
@@ -156,7 +179,9 @@ __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool las
         v[4 * q + 3] += b.w;
       }
     }
+#if !(PONNI_B200_TS_DIAG & 2)  // diagnostic builds: bit 2 skips activations
     ts_act32<ACT>(v, fast, flags, s0, s1);
+#endif
     TS_ACC(t_ph[1], ta);
     if (last) {
       if (col < batch) {
@@ -195,20 +220,56 @@ __device__ __forceinline__ void ts_epilogue_dispatch(const TsLayer& L, int fast,
 #undef PONNI_TS_EPI
 }
 
-// Stage tile `t`'s input into a slot's operand buffer as the MN-major
-// layer-0 operand (cp.async), and zero its padding K rows nin..k_pad (the
-// buffer holds the previous tile's activations).  Epilogue threads only.
+// Layer-0 operand (MN-major, 128-byte swizzle) of one tile: two 64-column
+// halves, each k0 feature rows of 128 B (row f at f * 128, its 16-byte
+// chunks XOR-ed with f % 8), half h at h * k0 * 128.  This is the layout a
+// 2-D tensor copy with 128-byte swizzle writes for a box of 64 columns x k0
+// features, so the loader warp fills it with two copies; the fallback below
+// writes the same bytes with cp.async.
+__device__ __forceinline__ uint32_t ts_stage_off(int f, int j, int k0) {
+  return (uint32_t)(j >> 3) * (uint32_t)(k0 * 128) + (uint32_t)f * 128u + ((((uint32_t)j & 7u) ^ ((uint32_t)f & 7u)) << 4);
+}
+
+// Stage tile `t`'s input into a slot's operand buffer with cp.async (the
+// epilogue threads; used when the input cannot go through a tensor map),
+// and zero its padding K rows nin..k0 (the buffer holds the previous
+// tile's activations).
 template <class T>
 __device__ __forceinline__ void ts_load_tile(uint32_t buf, unsigned char* buf_ptr, const T* in, int64_t in_ld,
                                              int nin, int k0, int64_t t, int64_t batch, bool vec, int tid) {
-  load_input<T, kTsGroupThreads>(buf, in, in_ld, nin, t * kTcM, batch, vec, tid);
-  cp_async_commit();
-  for (int i = tid; i < (k0 - nin) * 16; i += kTsGroupThreads) {
-    const int f = nin + i / 16, j = i % 16;
-    const uint32_t off = (uint32_t)(f >> 3) * 2048 + (uint32_t)(j >> 3) * 1024 + (uint32_t)(f & 7) * 128 +
-                         ((((uint32_t)j & 7) ^ ((uint32_t)f & 7)) << 4);
-    *reinterpret_cast<uint4*>(buf_ptr + off) = make_uint4(0, 0, 0, 0);
+  const int64_t col0 = t * kTcM;
+  if (vec) {
+    for (int i = tid; i < nin * 16; i += kTsEpiLoaders) {
+      const int f = i >> 4, j = i & 15;
+      const int64_t col = col0 + (int64_t)j * 8;
+      const int64_t valid = batch - col;
+      const int bytes = valid >= 8 ? 16 : (valid > 0 ? (int)valid * 2 : 0);
+      cp_async16(buf + ts_stage_off(f, j, k0), in + (int64_t)f * in_ld + (bytes > 0 ? col : 0), bytes);
+    }
+  } else {
+    for (int i = tid; i < nin * kTcM; i += kTsEpiLoaders) {
+      const int f = i / kTcM, mm = i - f * kTcM;
+      const int64_t col = col0 + mm;
+      const T v = col < batch ? in[(int64_t)f * in_ld + col] : Store<T>::from(0.0f);
+      const uint32_t dst = buf + ts_stage_off(f, mm >> 3, k0) + (uint32_t)(mm & 7) * 2;
+      asm volatile("st.shared.b16 [%0], %1;\n" ::"r"(dst), "h"(*reinterpret_cast<const unsigned short*>(&v)) : "memory");
+    }
   }
+  cp_async_commit();
+  for (int i = tid; i < (k0 - nin) * 16; i += kTsEpiLoaders) {
+    const int f = nin + (i >> 4), j = i & 15;
+    *reinterpret_cast<uint4*>(buf_ptr + ts_stage_off(f, j, k0)) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// One box of the input tensor map (64 columns x k0 features, 128-byte
+// swizzle) into shared memory, completion counted in bytes on `bar`.  No
+// multicast; the column coordinate is a multiple of 64 (the 16-byte rule).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
 
 // Job order shared by the three roles: rounds of two tiles (one per slot);
@@ -243,7 +304,7 @@ template <class T, bool PAIR>
 __global__ void __launch_bounds__(kTsThreads, 1)
     ts_forward_kernel(const __grid_constant__ TsProgram p, const unsigned char* __restrict__ image,
                       const T* __restrict__ in, int64_t in_ld, T* __restrict__ out, int64_t out_ld, int64_t batch,
-                      int in_vec, int* __restrict__ err) {
+                      int in_vec, const __grid_constant__ CUtensorMap in_map, int in_tma, int* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -262,6 +323,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   const uint32_t b_accf = s_bars + 128;    // [slot]
   const uint32_t b_kbar = s_bars + 144;    // [slot][2 column halves]
   const uint32_t b_stage = s_bars + 208;   // [slot]
+  const uint32_t b_free = s_bars + 176;    // [slot] the slot's last layer has read its operand buffer
   const uint32_t b_drain = s_bars + 224;
   const uint32_t s_tmem = s_bars + 232;
   const uint32_t b_pfull = s_bars + 256;   // [R] pair mode: the odd CTA's half of the stage has landed
@@ -295,8 +357,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     }
     for (int s = 0; s < kTsSlots; ++s) {
       mbar_init(b_accf + 8u * s, 1);
-      for (int h = 0; h < 2; ++h) mbar_init(b_kbar + 8u * (2 * s + h), 4 * peers);
-      mbar_init(b_stage + 8u * s, kTsGroupWarps * peers);
+      for (int h = 0; h < 2; ++h) mbar_init(b_kbar + 8u * (2 * s + h), kTsEpiHalfWarps * peers);
+      mbar_init(b_stage + 8u * s, in_tma ? 1u : (kTsEpiLoaders / 32) * peers);
+      mbar_init(b_free + 8u * s, 1);
     }
     mbar_init(b_drain, 1);
     *abort_flag = 0;
@@ -345,6 +408,42 @@ __global__ void __launch_bounds__(kTsThreads, 1)
       if (!ok) atomicExch(err, 2);
     }
     __syncwarp();
+  } else if (warp == kTsLoaderWarp) {
+    // -------------------------------------------------- loader ----
+    // Input tiles through the input tensor map (single CTA, aligned input):
+    // a slot's next tile as soon as its previous tile's last layer has read
+    // the operand buffer, two boxes of 64 columns x k0 features per tile.
+    if (in_tma && lane == 0) {
+      const int k0 = layers[0].k_pad;
+      const uint32_t bytes = 2u * 64u * (uint32_t)k0 * 2u;
+      uint32_t fr_ph[kTsSlots] = {0, 0}, n_issued[kTsSlots] = {0, 0};
+      bool ok = true;
+      for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
+        for (int s = 0; s < kTsSlots && ok; ++s) {
+          if (r >= jobs.count[s]) continue;
+          if (r > 0) {
+            if (!(ok = wait_phase(b_free + 8u * s, fr_ph[s], abort_flag))) break;
+            fr_ph[s] ^= 1u;
+          }
+          const int32_t x = (int32_t)(jobs.tile(s, r) * kTcM);
+          mbar_expect_tx(b_stage + 8u * s, bytes);
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d(s_a[s] + (uint32_t)h * (uint32_t)k0 * 128u, &in_map, x + 64 * h, 0, b_stage + 8u * s);
+          ++n_issued[s];
+        }
+      // Drain: a copy still in flight (after an abort) lands before the CTA
+      // exits.  Load k of a slot completes phase k of its stage barrier, and
+      // load k - 1 had landed before load k was issued (the MMAs of its tile
+      // had run), so the parity of the last load identifies its phase.
+      for (int s = 0; s < kTsSlots; ++s) {
+        if (n_issued[s] == 0) continue;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(b_stage + 8u * s, (n_issued[s] - 1) & 1u))
+          if (clock64() - t0 > kWaitCycles) break;
+      }
+      if (!ok) atomicExch(err, 2);
+    }
+    __syncwarp();
   } else if (warp == kTsMmaWarp && PAIR && !leader) {
     // ----------------------------- relay (odd CTA of a pair) ----
     // Tell the even CTA, stage by stage and in job order, that this CTA's
@@ -387,8 +486,11 @@ __global__ void __launch_bounds__(kTsThreads, 1)
       };
       const uint32_t hi_k = (uint32_t)(smem_desc(0, 16, 1024) >> 32);
       const uint32_t lo_k = (uint32_t)smem_desc(0, 16, 1024);
-      const uint32_t hi_mn = (uint32_t)(smem_desc(0, 1024, 2048) >> 32);
-      const uint32_t lo_mn = (uint32_t)smem_desc(0, 1024, 2048);
+      // layer 0 (MN-major input stage): 64-column halves k0 * 128 B apart,
+      // 8-feature groups 1024 B apart
+      const uint32_t k0b = (uint32_t)layers[0].k_pad * 128u;
+      const uint32_t hi_mn = (uint32_t)(smem_desc(0, k0b, 1024) >> 32);
+      const uint32_t lo_mn = (uint32_t)smem_desc(0, k0b, 1024);
       const uint32_t ring_lo = lo_k | ((s_ring >> 4) & 0x3FFFu);
       for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
         for (int l = 0; l < nl && ok; ++l)
@@ -427,9 +529,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
               const uint32_t b_lo = ring_lo + st * (kStage >> 4);
               const int s_end = min(nsteps, kb * 4 + 4);
               for (int k = kb * 4; k < s_end; ++k) {
-                // start-address advance in 16-byte units: MN-major, 4 KB per K step of 16;
+                // start-address advance in 16-byte units: MN-major, 2 KB per K step of 16;
                 // K-major, 16 KB per K block of 64 and 32 B per K step
-                const uint32_t ao = l == 0 ? (uint32_t)k * 256u : (uint32_t)(k >> 2) * 1024u + (uint32_t)(k & 3) * 2u;
+                const uint32_t ao = l == 0 ? (uint32_t)k * 128u : (uint32_t)(k >> 2) * 1024u + (uint32_t)(k & 3) * 2u;
                 const uint32_t bk = b_lo + (uint32_t)(k & 3) * 2u;
                 if constexpr (PAIR) umma_f16_pair_warp(d, a_lo + ao, a_hi, bk, hi_k, idesc, k > 0 ? 1u : 0u);
                 else umma_f16_desc_warp(d, a_lo + ao, a_hi, bk, hi_k, idesc, k > 0 ? 1u : 0u);
@@ -442,6 +544,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
               if constexpr (PAIR) umma_commit_pair_warp(b_accf + 8u * s);
               else umma_commit_warp(b_accf + 8u * s);
             }
+            if (!PAIR && in_tma && ok && l == nl - 1) umma_commit_warp(b_free + 8u * s);  // stage the next tile
             skip = false;
           }
       // Drain: every MMA issued has completed before TMEM is freed (both CTAs).
@@ -462,68 +565,76 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     __syncwarp();
   } else {
     // ----------------------------------------------- epilogue ----
-    const int s = warp / kTsGroupWarps;  // this group's slot
-    const int q = warp & 3, ch = (warp >> 2) & 1;
-    const int gtid = tid & (kTsGroupThreads - 1);
+    // Every epilogue warp runs the jobs in the MMA issuer's order (both slots)
+    // or, with per-slot groups, only its slot's jobs.
+    const int q = warp & 3;
+    const int cq = kTsEpiAll ? (warp >> 2) : ((warp >> 2) & 1);  // column quarter / half
+    const int ch = kTsEpiAll ? (cq >> 1) : cq;                     // column half (signals)
+    const int gs = kTsEpiAll ? -1 : warp / kTsGroupWarps;          // group's slot (per-slot groups)
+    const int ltid = kTsEpiAll ? tid : (tid & (kTsGroupThreads - 1));
     const int m = q * 32 + lane;
     const bool vec = in_vec != 0;
     const int k0 = layers[0].k_pad;
-    uint32_t acc_ph = 0;
+    uint32_t acc_ph[kTsSlots] = {0, 0};
     bool ok = true;
     long long w_acc = 0, c_epi = 0, t_ph[3] = {0, 0, 0};
     (void)w_acc; (void)c_epi;
-    unsigned char* a_ptr = base_ptr + (s_a[s] - base);
     // Operand written / accumulator read: local arrive, or in pair mode a
     // cluster-scope arrive on the even CTA's barrier.
     auto signal = [&](uint32_t bar) {
       if constexpr (PAIR) mbar_arrive_cluster(bar);
       else mbar_arrive(bar);
     };
-    if (jobs.count[s] > 0) {
-      ts_load_tile<T>(s_a[s], a_ptr, in, in_ld, p.nin, k0, jobs.tile(s, 0), batch, vec, gtid);
-      cp_async_wait_0();
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) signal(stage_sig + 8u * s);
-    }
-    for (int64_t r = 0; r < jobs.count[s] && ok; ++r)
-      for (int l = 0; l < nl && ok; ++l) {
-        const TsLayer& L = layers[l];
-        const bool last = l == nl - 1;
-        const int64_t t = jobs.tile(s, r);
-        // One lane waits, the warp follows (the TMEM loads are warp-collective).
-        TS_T(t0);
-        int got = 0;
-        if (lane == 0) got = wait_phase(b_accf + 8u * s, acc_ph, abort_flag) ? 1 : 0;
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!(ok = got != 0)) break;
-        acc_ph ^= 1u;
-        TS_ACC(w_acc, t0);
-        TS_T(t1);
-        tc_fence_after();
-        const bool refill = last && r + 1 < jobs.count[s];
-        if (refill)  // the slot's MMAs are done with its operand buffer: stage the next tile
-          ts_load_tile<T>(s_a[s], a_ptr, in, in_ld, p.nin, k0, jobs.tile(s, r + 1), batch, vec, gtid);
-        const uint32_t tmem_row = tmem_base + (uint32_t)(s * kTsMaxN) + ((uint32_t)(q * 32) << 16);
-#ifndef PONNI_B200_TS_NO_EPI  // diagnostic build: handoffs only, no epilogue work
-        ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, ch * kTsColsPerWarp,
-                                reinterpret_cast<const float*>(image + L.bias_off), s_a[s], out, out_ld,
-                                t * kTcM + m, batch, m, t_ph);
-#else
-        (void)tmem_row;
-#endif
+    for (int s = 0; s < kTsSlots; ++s)
+      if (!in_tma && (gs < 0 || gs == s) && jobs.count[s] > 0) {
+        ts_load_tile<T>(s_a[s], base_ptr + (s_a[s] - base), in, in_ld, p.nin, k0, jobs.tile(s, 0), batch, vec, ltid);
+        cp_async_wait_0();
         fence_proxy_async();
-        tc_fence_before();
         __syncwarp();
-        if (lane == 0) signal(kbar_sig + 8u * (2 * s + ch));
-        if (refill) {
-          cp_async_wait_0();
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) signal(stage_sig + 8u * s);
-        }
-        TS_ACC(c_epi, t1);
+        if (lane == 0) signal(stage_sig + 8u * s);
       }
+    for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
+      for (int l = 0; l < nl && ok; ++l)
+        for (int s = 0; s < kTsSlots && ok; ++s) {
+          if (r >= jobs.count[s] || (gs >= 0 && gs != s)) continue;
+          const TsLayer& L = layers[l];
+          const bool last = l == nl - 1;
+          const int64_t t = jobs.tile(s, r);
+          // One lane waits, the warp follows (the TMEM loads are warp-collective).
+          TS_T(t0);
+          int got = 0;
+          if (lane == 0) got = wait_phase(b_accf + 8u * s, acc_ph[s], abort_flag) ? 1 : 0;
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!(ok = got != 0)) break;
+          acc_ph[s] ^= 1u;
+          TS_ACC(w_acc, t0);
+          TS_T(t1);
+          tc_fence_after();
+          const bool refill = !in_tma && last && r + 1 < jobs.count[s];
+          if (refill && !(PONNI_B200_TS_DIAG & 1))  // (diagnostic builds: bit 1 skips the input loads)
+            // the slot's MMAs are done with its operand buffer: stage the next tile
+            ts_load_tile<T>(s_a[s], base_ptr + (s_a[s] - base), in, in_ld, p.nin, k0, jobs.tile(s, r + 1), batch,
+                            vec, ltid);
+          const uint32_t tmem_row = tmem_base + (uint32_t)(s * kTsMaxN) + ((uint32_t)(q * 32) << 16);
+#ifndef PONNI_B200_TS_NO_EPI  // diagnostic build: handoffs only, no epilogue work
+          ts_epilogue_dispatch<T>(L, p.fast_act, last, tmem_row, cq * kTsEpiCols,
+                                  reinterpret_cast<const float*>(image + L.bias_off), s_a[s], out, out_ld,
+                                  t * kTcM + m, batch, m, t_ph);
+#else
+          (void)tmem_row;
+#endif
+          fence_proxy_async();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) signal(kbar_sig + 8u * (2 * s + ch));
+          if (refill) {
+            cp_async_wait_0();
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) signal(stage_sig + 8u * s);
+          }
+          TS_ACC(c_epi, t1);
+        }
     cp_async_wait_0();
     if (!ok && lane == 0) atomicExch(err, 4);
     if (tid == 0) {
@@ -544,6 +655,52 @@ __global__ void __launch_bounds__(kTsThreads, 1)
   }
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+bool getenv_flag_off(const char* name) {
+  const char* v = getenv(name);
+  return v && atoi(v) == 0;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      f = nullptr;
+    }
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// Tensor map of the caller's input [nin features x batch columns] (row
+// stride in_ld elements) with boxes of 64 columns x k0 features and 128-byte
+// swizzle; features nin..k0 and columns past the batch read as zeros.
+// False when the input does not meet the copy engine's alignment rules (base
+// and row stride multiples of 16 bytes) or the entry point is missing; the
+// kernel then stages its tiles with cp.async.
+template <class T>
+bool make_input_map(CUtensorMap& map, const void* in, int64_t in_ld, int nin, int k0, int64_t batch) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc || getenv_flag_off("PONNI_B200_TS_TMA")) return false;
+  if (reinterpret_cast<uintptr_t>(in) % 16 != 0 || (in_ld * 2) % 16 != 0 || k0 > 256 || batch < 1) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)batch, (cuuint64_t)nin};
+  const cuuint64_t strides[1] = {(cuuint64_t)in_ld * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)k0};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return enc(&map, dt, 2, const_cast<void*>(in), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <class T>
 cudaError_t launch_impl(const TsProgram& p, const void* image, const void* in, int64_t in_ld, void* out,
                         int64_t out_ld, int64_t batch, int grid, int* err, cudaStream_t stream) {
@@ -555,7 +712,11 @@ cudaError_t launch_impl(const TsProgram& p, const void* image, const void* in, i
     auto kern = ts_forward_kernel<T, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kTsThreads, p.smem_bytes, stream>>>(p, img, x, in_ld, y, out_ld, batch, vec ? 1 : 0, err);
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof map);
+    const bool tma = make_input_map<T>(map, in, in_ld, p.nin, p.layers[0].k_pad, batch);
+    kern<<<grid, kTsThreads, p.smem_bytes, stream>>>(p, img, x, in_ld, y, out_ld, batch, vec ? 1 : 0, map,
+                                                     tma ? 1 : 0, err);
     return cudaGetLastError();
   }
   // Clusters of two CTAs; the grid is a whole number of pairs, at most one
@@ -577,7 +738,9 @@ cudaError_t launch_impl(const TsProgram& p, const void* image, const void* in, i
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p, img, x, in_ld, y, out_ld, batch, vec ? 1 : 0, err);
+  CUtensorMap map;  // pair mode stages its tiles with cp.async
+  std::memset(&map, 0, sizeof map);
+  return cudaLaunchKernelEx(&cfg, kern, p, img, x, in_ld, y, out_ld, batch, vec ? 1 : 0, map, 0, err);
 }
 
 }  // namespace

@@ -29,7 +29,8 @@ constexpr int kTsGroupThreads = kTsGroupWarps * 32;
 constexpr int kTsColsPerWarp = kTsMaxN / 2;     // accumulator columns per warp and job
 constexpr int kTsProducerWarp = kTsEpiWarps;
 constexpr int kTsMmaWarp = kTsEpiWarps + 1;
-constexpr int kTsThreads = (kTsEpiWarps + 2) * 32;  // + producer warp + MMA warp
+constexpr int kTsLoaderWarp = kTsEpiWarps + 2;       // input tiles through the tensor memory accelerator
+constexpr int kTsThreads = (kTsEpiWarps + 3) * 32;  // + producer, MMA and loader warps
 constexpr int kTsMaxStages = 8;
 constexpr int kTsBarBytes = 320;                // mbarriers, TMEM address and abort flag, then the layer table
 
