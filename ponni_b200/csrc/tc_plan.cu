@@ -496,7 +496,7 @@ bool tr_plan(const ponni_b200_model* m, TrProgram& p, std::vector<unsigned char>
   // Shared memory: per slot three operand parts of 2 K blocks, the weight
   // ring, the LayerNorm exchange and the mbarriers.  The dynamic shared
   // memory base is 1024-byte aligned (checked by the kernel), so no slack.
-  p.smem_bytes = kTrSlots * 3 * kTrPartBytes + kTrStages * kTrChunkBytes + kTrSlots * 2 * 128 * 4 + 128;
+  p.smem_bytes = kTrSlots * 3 * kTrPartBytes + kTrStages * kTrChunkBytes + 128;
   if (p.smem_bytes > 227 * 1024) {
     why = "operand tiles exceed shared memory";
     return false;

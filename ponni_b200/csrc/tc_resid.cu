@@ -23,13 +23,15 @@
 //       activations             v = f(v)              (activation.cuh)
 //       Binop_Add<I>            v += saved[I]         (ponni_Binop_Add.h:58-68)
 //       Save_State<I>           saved[I] = v          (ponni_Save_State.h:58-67)
-//       LayerNorm               two-pass mean / biased variance,
-//                               gamma * (v - mean) / sqrt(var + eps) + beta
-//                               (ponni_LayerNorm.h:77-99)
+//       LayerNorm               mean / biased variance (each column quarter
+//                               two-pass over its values, quarters combined
+//                               pairwise), gamma * (v - mean) / sqrt(var + eps)
+//                               + beta (ponni_LayerNorm.h:77-99)
 //     then split the result into the three bf16 parts of the next job's A
 //     operand (shared memory, K-major SW128) or write the caller's output.
-//     LayerNorm keeps the row's values in registers and exchanges the four
-//     column quarters' partial sums through shared memory.  Saved states
+//     LayerNorm keeps the row's values in registers; the four column
+//     quarters exchange (mean, squared deviations) pairs through two
+//     already-read accumulator columns of TMEM, one barrier.  Saved states
 //     live in a per-CTA, per-slot global scratch area (64 KB per slot and
 //     state; L2-resident), written and read back by the same thread.
 // Two tiles are in flight and their jobs alternate Matvec by Matvec, so the
@@ -147,6 +149,32 @@ __device__ __forceinline__ void act_dispatch(int kind, float (&v)[32], int flags
   }
 }
 
+// Two TMEM columns of this warp's 32 lanes (one value per lane each).
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, float a, float b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};\n" ::"r"(taddr), "r"(__float_as_uint(a)),
+               "r"(__float_as_uint(b))
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+// Pairs of columns at four TMEM addresses of this warp's lanes, one wait.
+__device__ __forceinline__ void tmem_ld2x4(const uint32_t (&t)[4], float (&a)[4], float (&b)[4]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%8];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x2.b32 {%2, %3}, [%9];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x2.b32 {%4, %5}, [%10];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x2.b32 {%6, %7}, [%11];\n\t"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(t[0]), "r"(t[1]), "r"(t[2]), "r"(t[3])
+      : "memory");
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    a[q] = __uint_as_float(r[2 * q]);
+    b[q] = __uint_as_float(r[2 * q + 1]);
+  }
+}
+
 // Per-thread context of the epilogue.  All 16 epilogue warps work on one
 // job at a time: warp w reads TMEM lane quarter w % 4 (rows 32 (w % 4) ..)
 // and handles accumulator columns 32 (w / 4) .. + 31, so each thread holds
@@ -155,7 +183,6 @@ struct TrEpi {
   const unsigned char* image;
   float4* saved_cta;  // this CTA's saved states: [slot][state][f / 4][128 rows] float4
   int n_saved;
-  float* xch;         // LayerNorm exchange [4 column quarters][128 rows]
   int cq, m;          // column quarter, row
   // the job's slot
   float4* saved;      // the slot's saved states
@@ -269,51 +296,77 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
   }
   if (has_ln) {
     // LayerNorm over the row (src/layers/ponni_LayerNorm.h:77-99): the four
-    // column quarters of a row exchange partial sums.
-    float psum = 0.f;
+    // column quarters of a row combine their partial statistics.
+    // Each column quarter's mean and sum of squared deviations (two passes
+    // over its registers), combined across the row's quarters with the
+    // pairwise update of Chan, Golub and LeVeque (mean = sum n_q m_q / n,
+    // M2 = sum M2_q + sum n_q (m_q - mean)^2, var = M2 / n).  The pairs go
+    // through TMEM: each warp writes its pair into the first two of its own,
+    // already read, correction-accumulator columns; one barrier; each warp
+    // reads the pairs of the row's quarters.
+    const uint32_t corr_row = E.tmem_row + (uint32_t)((groups - 1) * n_pad);
     if (active) {
+      float qmean, qm2;
       if (nv >= 32) {
-        float s0 = v[0], s1 = v[1];  // even and odd columns, combined at the end
+        float s0 = v[0], s1 = v[1];
 #pragma unroll
         for (int j = 2; j < 32; j += 2) f2::add(s0, s1, s0, s1, v[j], v[j + 1]);
-        psum = __fadd_rn(s0, s1);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j < nv) psum = __fadd_rn(psum, v[j]);
-      }
-    }
-    const float n = (float)nout;
-    E.xch[E.cq * 128 + E.m] = psum;
-    epi_sync();
-    const float mean =
-        __fdiv_rn(__fadd_rn(__fadd_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), E.xch[256 + E.m]), E.xch[384 + E.m]), n);
-    epi_sync();
-    float pvar = 0.f;
-    if (active) {
-      if (nv >= 32) {
-        float s0 = 0.f, s1 = 0.f;
+        qmean = __fdiv_rn(__fadd_rn(s0, s1), 32.0f);
+        float t0 = 0.f, t1 = 0.f;
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           float d0, d1;
-          f2::sub(d0, d1, v[j], v[j + 1], mean, mean);
+          f2::sub(d0, d1, v[j], v[j + 1], qmean, qmean);
           f2::mul(d0, d1, d0, d1, d0, d1);
-          f2::add(s0, s1, s0, s1, d0, d1);
+          f2::add(t0, t1, t0, t1, d0, d1);
         }
-        pvar = __fadd_rn(s0, s1);
+        qm2 = __fadd_rn(t0, t1);
       } else {
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nv) sum = __fadd_rn(sum, v[j]);
+        qmean = __fdiv_rn(sum, (float)nv);
+        qm2 = 0.f;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (j < nv) {
-            const float d = __fsub_rn(v[j], mean);
-            pvar = __fadd_rn(pvar, __fmul_rn(d, d));
+            const float d = __fsub_rn(v[j], qmean);
+            qm2 = __fadd_rn(qm2, __fmul_rn(d, d));
           }
       }
+      tmem_st2(corr_row + (uint32_t)c0, qmean, qm2);
     }
-    E.xch[E.cq * 128 + E.m] = pvar;
+    tc_fence_before();
     epi_sync();
-    const float var =
-        __fdiv_rn(__fadd_rn(__fadd_rn(__fadd_rn(E.xch[E.m], E.xch[128 + E.m]), E.xch[256 + E.m]), E.xch[384 + E.m]), n);
+    tc_fence_after();
+    float mean = 0.f, var = 0.f;
+    if (active) {
+      float qm[4], q2[4];
+      uint32_t ta[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)  // quarters past n_pad read quarter 0 (ignored below)
+        ta[q] = corr_row + (uint32_t)(32 * q < n_pad ? 32 * q : 0);
+      tmem_ld2x4(ta, qm, q2);
+      const float n = (float)nout;
+      float tot = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int nq = min(32, nout - 32 * q);
+        if (nq > 0) tot = __fadd_rn(tot, __fmul_rn((float)nq, qm[q]));
+      }
+      mean = __fdiv_rn(tot, n);
+      float m2 = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int nq = min(32, nout - 32 * q);
+        if (nq > 0) {
+          const float d = __fsub_rn(qm[q], mean);
+          m2 = __fadd_rn(m2, __fadd_rn(q2[q], __fmul_rn((float)nq, __fmul_rn(d, d))));
+        }
+      }
+      var = __fdiv_rn(m2, n);
+    }
     if (active) {
       const TrOp ln = p.ops[o_ln];
       const float inv_std = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, ln.s0)));
@@ -335,8 +388,8 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
       }
       tr_ops(p.ops, o_ln + 1, o_end, v, c0, E);
     }
-    // (the exchange buffer is rewritten only by a later job, which starts
-    // after every epilogue warp has arrived for this one)
+    // (the exchange columns belong to this job's accumulators, which the MMA
+    // issuer reuses only after every epilogue warp has released the slot)
   }
   if (active) tr_finish(v, c0, last, nout, E, out, out_ld, col, batch);
 }
@@ -434,8 +487,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     return;
   }
   const uint32_t s_ring = base + kTrSlots * 3 * kTrPartBytes;
-  const uint32_t s_xch = s_ring + kTrStages * kTrChunkBytes;
-  const uint32_t s_bars = s_xch + kTrSlots * 2 * 128 * 4;
+  const uint32_t s_bars = s_ring + kTrStages * kTrChunkBytes;
   const uint32_t b_full = s_bars;        // [stage]
   const uint32_t b_empty = s_bars + 16;  // [stage]
   const uint32_t b_accf = s_bars + 32;   // [slot] accumulator ready (MMA -> epilogue)
@@ -583,7 +635,6 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     E.image = image;
     E.n_saved = p.n_saved;
     E.saved_cta = reinterpret_cast<float4*>(scratch + (size_t)blockIdx.x * (p.scratch_per_cta / 4));
-    E.xch = reinterpret_cast<float*>(smem_raw + (s_xch - base));
     auto select_slot = [&](int s) {
       E.saved = E.saved_cta + (size_t)s * p.n_saved * (kTrMaxN / 4) * 128;
       for (int q = 0; q < 3; ++q) E.a[q] = base + (uint32_t)(s * 3 + q) * kTrPartBytes;

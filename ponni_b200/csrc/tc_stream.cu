@@ -131,18 +131,20 @@ __device__ __forceinline__ float ts_act(float x, int fast, int flags, float s0, 
 // sigmoid(x) = (1 + tanh(x / 2)) / 2 with the hardware tanh approximation:
 // one MUFU operation per value (absolute error near 2^-11, below one
 // fp16/bf16 unit of the activations the next layer consumes).
-__device__ __forceinline__ float sigmoid_fast(float x) { return fmaf(0.5f, tanh_fast(0.5f * x), 0.5f); }
-
 // Activation of 32 values; in the fast mode SiLU and sigmoid use
-// sigmoid_fast, tanh the fp32 tanh approximation.
+// the sigmoid above (two values at a time), tanh the fp32 tanh approximation.
 template <int ACT>
 __device__ __forceinline__ void ts_act32(float (&v)[32], int fast, int flags, float s0, float s1) {
   if constexpr (ACT == EPI_SILU || ACT == EPI_SIGMOID) {
     if (fast) {
+      // packed fp32 for the multiplies and the fma
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float g = sigmoid_fast(v[j]);
-        v[j] = ACT == EPI_SILU ? v[j] * g : g;
+      for (int j = 0; j < 32; j += 2) {
+        float h0, h1, g0, g1;
+        f2::mul(h0, h1, v[j], v[j + 1], 0.5f, 0.5f);
+        f2::fma(g0, g1, 0.5f, 0.5f, tanh_fast(h0), tanh_fast(h1), 0.5f, 0.5f);
+        if (ACT == EPI_SILU) f2::mul(v[j], v[j + 1], v[j], v[j + 1], g0, g1);
+        else v[j] = g0, v[j + 1] = g1;
       }
       return;
     }
@@ -173,10 +175,8 @@ __device__ __forceinline__ void ts_epilogue(const TsLayer& L, int fast, bool las
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 b = __ldg(b4 + q);
-        v[4 * q] += b.x;
-        v[4 * q + 1] += b.y;
-        v[4 * q + 2] += b.z;
-        v[4 * q + 3] += b.w;
+        f2::add(v[4 * q], v[4 * q + 1], v[4 * q], v[4 * q + 1], b.x, b.y);
+        f2::add(v[4 * q + 2], v[4 * q + 3], v[4 * q + 2], v[4 * q + 3], b.z, b.w);
       }
     }
 #if !(PONNI_B200_TS_DIAG & 2)  // diagnostic builds: bit 2 skips activations
