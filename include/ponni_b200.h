@@ -186,6 +186,15 @@ ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* model, int a
  * 0 on a planning error (see last_error). */
 int ponni_b200_model_kernel(ponni_b200_model* model);
 
+/* 1 when the kernel the next forward uses was compiled for this model's
+ * structure at plan time (NVRTC): kernel 4, or kernel 2 in its
+ * model-specialised build (layer count, widths, activations as compile-time
+ * constants; PONNI_B200_TC_JIT=0 disables it); 0 otherwise, with the reason
+ * in `why` (a static-lifetime string owned by the model, may be empty) when
+ * `why` is not NULL.  Plans the model.  No reference counterpart: this
+ * library's diagnostic. */
+int ponni_b200_model_specialised(ponni_b200_model* model, const char** why);
+
 /* Diagnostic counters of the tensor-core kernel (up to 7 values; per-phase
  * cycle sums in a build with -DPONNI_B200_TC_PROFILE, zeros otherwise). */
 ponni_b200_status ponni_b200_model_diagnostics(ponni_b200_model* model, uint64_t* out, int n);

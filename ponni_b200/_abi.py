@@ -71,6 +71,7 @@ SIGNATURES = {
     "ponni_b200_model_synchronize": (_STATUS, [_P]),
     "ponni_b200_model_set_arithmetic": (_STATUS, [_P, _I]),
     "ponni_b200_model_kernel": (_I, [_P]),
+    "ponni_b200_model_specialised": (_I, [_P, ctypes.POINTER(ctypes.c_char_p)]),
     "ponni_b200_model_device_program": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_I),
                                             ctypes.POINTER(_I)]),
     "ponni_b200_model_diagnostics": (_STATUS, [_P, ctypes.POINTER(ctypes.c_uint64), _I]),

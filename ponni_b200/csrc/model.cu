@@ -599,8 +599,12 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       e = cudaMemcpyAsync(m->tc_image_dev, image.data(), image.size(), cudaMemcpyHostToDevice, m->stream);
       if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
       if (e != cudaSuccess) return cuda_fail(m, e, "tensor-core parameter upload");
-      m->tc_grid = m->num_sms;  // one persistent CTA (up to four tile slots) per SM
+      m->tc_grid = m->num_sms;  // one persistent CTA (up to eight tile slots) per SM
       m->kernel = 2;
+      // The model-specialised build of the same kernel (NVRTC), when it compiles.
+      m->tc_jit = nullptr;
+      m->tc_jit_why.clear();
+      if (!tc_jit_build(m->tcp, &m->tc_jit, &m->tc_jit_why)) m->tc_jit = nullptr;
       m->pmap.recs.insert(m->pmap.recs.end(), tc_rec.recs.begin(), tc_rec.recs.end());
       m->pmap.overflow |= tc_rec.overflow;
     } else if (m->dtype == PONNI_B200_F32 && !(getenv("PONNI_B200_TC_RESID") && getenv("PONNI_B200_TC_RESID")[0] == '0') &&
@@ -893,7 +897,9 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
   if (m->kernel == 2) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, (ntiles + m->tcp.slots - 1) / m->tcp.slots);
-    e = launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
+    e = m->tc_jit ? launch_tc_forward_jit(m->tc_jit, m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch,
+                                          grid, m->err_dev, s)
+                  : launch_tc_forward(m->tcp, m->tc_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
   } else if (m->kernel == 5) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
@@ -989,6 +995,17 @@ int ponni_b200_model_kernel(ponni_b200_model* m) {
   if (!m) return 0;
   DeviceGuard guard(m->device);
   return pb_plan(m) == PONNI_B200_OK ? m->kernel : 0;
+}
+
+int ponni_b200_model_specialised(ponni_b200_model* m, const char** why) {
+  if (why) *why = "";
+  if (!m) return 0;
+  DeviceGuard guard(m->device);
+  if (pb_plan(m) != PONNI_B200_OK) return 0;
+  if (m->kernel == 4) return 1;
+  if (m->kernel == 2 && m->tc_jit) return 1;
+  if (why) *why = m->kernel == 2 ? m->tc_jit_why.c_str() : m->kernel == 3 ? m->jit_why.c_str() : "";
+  return 0;
 }
 
 ponni_b200_status ponni_b200_model_diagnostics(ponni_b200_model* m, uint64_t* out, int n) {

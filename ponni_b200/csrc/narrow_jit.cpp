@@ -1,7 +1,12 @@
-// Model-specialised narrow-chain kernel: source generation, NVRTC
-// compilation (libnvrtc is opened at run time, so the library has no link
-// dependency on it), loading, caching and launch.  See narrow_jit.h.
+// Model-specialised kernels compiled at plan time: the narrow-chain kernel
+// (source generated from the program, see narrow_jit.h) and the resident
+// tensor-core kernel (tc_kernel_body.cuh with the layer structure as
+// compile-time constants, see tc_kernel.h).  NVRTC compilation (libnvrtc is
+// opened at run time, so the library has no link dependency on it), loading,
+// caching and launch.
 #include "narrow_jit.h"
+
+#include "tc_kernel.h"
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -10,6 +15,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <vector>
 #include <map>
 #include <mutex>
 #include <sstream>
@@ -17,7 +24,8 @@
 namespace ponni_b200 {
 namespace {
 
-// Texts of epi_kinds.h and activation.cuh, embedded at build time.
+// Texts of the headers the generated kernels include, embedded at build time
+// (kJit_<name>).
 #include "jit_headers.inc"
 
 constexpr int kJitThreads = 256;
@@ -258,21 +266,54 @@ std::map<std::string, CacheEntry>& cache() {
   return c;
 }
 
-bool compile_and_load(const std::string& src, cudaKernel_t* kernel, std::string* why) {
+// Headers the generated sources may include: this library's device headers
+// and stand-ins for the two host headers they name (the CUDA type headers
+// cuda_fp16.h / cuda_bf16.h come from the toolkit's include directory).
+const char kJitStdint[] =
+    "#pragma once\n"
+    "typedef signed char int8_t; typedef short int16_t; typedef int int32_t; typedef long long int64_t;\n"
+    "typedef unsigned char uint8_t; typedef unsigned short uint16_t; typedef unsigned int uint32_t;\n"
+    "typedef unsigned long long uint64_t; typedef unsigned long long uintptr_t;\n";
+const char kJitCudaRuntime[] = "#pragma once\n";
+
+// The CUDA toolkit's include directory (cuda_fp16.h), or "" when none is found.
+std::string cuda_include_dir() {
+  std::vector<std::string> cands;
+  for (const char* env : {"CUDA_HOME", "CUDA_PATH"})
+    if (const char* v = getenv(env)) cands.push_back(std::string(v) + "/include");
+  cands.push_back("/usr/local/cuda/include");
+  for (const std::string& d : cands) {
+    FILE* f = fopen((d + "/cuda_fp16.h").c_str(), "r");
+    if (f) {
+      fclose(f);
+      return d;
+    }
+  }
+  return "";
+}
+
+bool compile_and_load(const std::string& src, const char* name, cudaKernel_t* kernel, std::string* why) {
   const Nvrtc& n = nvrtc();
   if (!n.ok) {
     *why = n.why;
     return false;
   }
-  const char* hdr_src[2] = {kJitEpiKinds, kJitActivation};
-  const char* hdr_name[2] = {"epi_kinds.h", "activation.cuh"};
+  const char* hdr_src[] = {kJit_epi_kinds_h, kJit_activation_cuh, kJit_program_h,    kJit_device_math_cuh,
+                           kJit_tc_program_h, kJit_f32x2_cuh,     kJit_tc_common_cuh, kJit_tc_kernel_body_cuh,
+                           kJitStdint,        kJitCudaRuntime};
+  const char* hdr_name[] = {"epi_kinds.h",  "activation.cuh", "program.h",     "device_math.cuh",     "tc_program.h",
+                            "f32x2.cuh",    "tc_common.cuh",  "tc_kernel_body.cuh", "stdint.h", "cuda_runtime.h"};
+  constexpr int nh = (int)(sizeof(hdr_src) / sizeof(hdr_src[0]));
   nvrtcProgram prog = nullptr;
-  if (n.create(&prog, src.c_str(), "ponni_narrow_jit.cu", 2, hdr_src, hdr_name) != NVRTC_SUCCESS) {
+  if (n.create(&prog, src.c_str(), "ponni_jit.cu", nh, hdr_src, hdr_name) != NVRTC_SUCCESS) {
     *why = "nvrtcCreateProgram failed";
     return false;
   }
-  const char* opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "--fmad=true"};
-  const nvrtcResult rc = n.compile(prog, 3, opts);
+  const std::string inc = cuda_include_dir();
+  const std::string inc_opt = "-I" + inc;
+  std::vector<const char*> opts = {"--gpu-architecture=sm_100a", "-std=c++17", "--fmad=true"};
+  if (!inc.empty()) opts.push_back(inc_opt.c_str());
+  const nvrtcResult rc = n.compile(prog, (int)opts.size(), opts.data());
   if (rc != NVRTC_SUCCESS) {
     size_t ls = 0;
     n.log_size(prog, &ls);
@@ -289,7 +330,7 @@ bool compile_and_load(const std::string& src, cudaKernel_t* kernel, std::string*
   n.destroy(&prog);
   cudaLibrary_t lib = nullptr;
   cudaError_t e = cudaLibraryLoadData(&lib, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0);
-  if (e == cudaSuccess) e = cudaLibraryGetKernel(kernel, lib, "ponni_narrow_jit");
+  if (e == cudaSuccess) e = cudaLibraryGetKernel(kernel, lib, name);
   if (e != cudaSuccess) {
     cudaGetLastError();
     *why = std::string("loading the compiled kernel failed: ") + cudaGetErrorString(e);
@@ -353,7 +394,7 @@ bool narrow_jit_build(int dtype, const Program& p, int maxw, const std::vector<u
     std::lock_guard<std::mutex> lk(g_cache_mu);
     auto it = cache().find(src);
     if (it != cache().end()) kernel = it->second.kernel;
-    else if (!compile_and_load(src, &kernel, why)) return false;
+    else if (!compile_and_load(src, "ponni_narrow_jit", &kernel, why)) return false;
   }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void*>(kernel), kJitThreads, 0) !=
@@ -379,6 +420,82 @@ cudaError_t narrow_jit_launch(const NarrowJit& J, const void* in, int64_t in_ld,
   long long a_in_ld = in_ld, a_out_ld = out_ld, a_batch = batch;
   void* args[] = {const_cast<unsigned char*>(J.params.data()), &in, &a_in_ld, &out, &a_out_ld, &a_batch, &vec};
   return cudaLaunchKernel(J.kernel, dim3(grid), dim3(kJitThreads), args, 0, stream);
+}
+
+
+// ---------------------------------------- resident tensor-core kernel ----
+
+namespace {
+
+std::string tc_jit_source(const TcProgram& p) {
+  const char* T = p.dtype == 0 ? "float" : p.dtype == 2 ? "__half" : "__nv_bfloat16";
+  const int tps = p.slot_threads;
+  const int bound = (tps == 128 && p.dtype != 0) ? kTcMaxThreads : kTcMaxThreads / 2;
+  std::ostringstream o;
+  auto arr = [&](const char* name, auto get) {
+    o << "    constexpr int " << name << "[] = {";
+    for (int l = 0; l < p.n_layers; ++l) o << (l ? ", " : "") << get(p.layers[l]);
+    o << "};\n";
+  };
+  o << "// generated: resident tensor-core kernel, dtype " << p.dtype << ", " << p.n_layers << " layers\n"
+    << "#include \"tc_kernel_body.cuh\"\n"
+    << "namespace ponni_b200 {\nnamespace tck {\n"
+    << "struct JitShape {\n"
+    << "  static constexpr bool kStatic = true;\n"
+    << "  static constexpr int kNL = " << p.n_layers << ";\n"
+    << "  static __device__ __forceinline__ void fix(int l, TcLayer& L) {\n";
+  arr("kK", [](const TcLayer& L) { return L.k_pad; });
+  arr("kN", [](const TcLayer& L) { return L.n_pad; });
+  arr("kOut", [](const TcLayer& L) { return L.nout; });
+  arr("kG", [](const TcLayer& L) { return L.groups; });
+  arr("kGS", [](const TcLayer& L) { return L.group_steps; });
+  arr("kAct", [](const TcLayer& L) { return L.act; });
+  arr("kFl", [](const TcLayer& L) { return L.act_flags; });
+  arr("kB", [](const TcLayer& L) { return L.has_bias; });
+  o << "    L.k_pad = kK[l]; L.n_pad = kN[l]; L.nout = kOut[l]; L.groups = kG[l]; L.group_steps = kGS[l];\n"
+    << "    L.act = kAct[l]; L.act_flags = kFl[l]; L.has_bias = kB[l];\n"
+    << "  }\n};\n}  // namespace tck\n}  // namespace ponni_b200\n"
+    << "extern \"C\" __global__ void __launch_bounds__(" << bound << ", 1)\n"
+    << "ponni_tc_jit(const __grid_constant__ ponni_b200::TcProgram p, const unsigned char* __restrict__ image,\n"
+    << "             const " << T << "* __restrict__ in, long long in_ld, " << T << "* __restrict__ out,\n"
+    << "             long long out_ld, long long batch, int in_vec, int* __restrict__ err) {\n"
+    << "  ponni_b200::tck::tc_forward_body<" << T << ", " << tps << ", ponni_b200::tck::JitShape>(\n"
+    << "      p, image, in, in_ld, out, out_ld, batch, in_vec, err);\n"
+    << "}\n";
+  return o.str();
+}
+
+}  // namespace
+
+bool tc_jit_build(const TcProgram& p, const void** kernel, std::string* why) {
+  if (const char* v = getenv("PONNI_B200_TC_JIT"))
+    if (atoi(v) == 0) {
+      *why = "disabled (PONNI_B200_TC_JIT=0)";
+      return false;
+    }
+  const std::string src = tc_jit_source(p);
+  cudaKernel_t k = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    auto it = cache().find(src);
+    if (it != cache().end()) k = it->second.kernel;
+    else if (!compile_and_load(src, "ponni_tc_jit", &k, why)) return false;
+  }
+  *kernel = reinterpret_cast<const void*>(k);
+  return true;
+}
+
+cudaError_t launch_tc_forward_jit(const void* kernel, const TcProgram& p, const void* image, const void* in,
+                                  int64_t in_ld, void* out, int64_t out_ld, int64_t batch, int grid, int* err,
+                                  cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
+  if (e != cudaSuccess) return e;
+  const int64_t es = p.dtype == 0 ? 4 : 2;
+  int vec = (reinterpret_cast<uintptr_t>(in) % 16 == 0) && ((in_ld * es) % 16 == 0);
+  long long a_in_ld = in_ld, a_out_ld = out_ld, a_batch = batch;
+  TcProgram prog = p;
+  void* args[] = {&prog, const_cast<void**>(&image), const_cast<void**>(&in), &a_in_ld, &out, &a_out_ld, &a_batch, &vec, &err};
+  return cudaLaunchKernel(kernel, dim3(grid), dim3(p.slots * p.slot_threads), args, p.smem_bytes, stream);
 }
 
 }  // namespace ponni_b200

@@ -263,6 +263,13 @@ class Inference:
         tensor-core kernel)."""
         _check(_abi.lib().ponni_b200_model_set_arithmetic(self._m, int(mode)), self._m)
 
+    def specialised(self):
+        """(True, "") when the next forward runs a kernel compiled for this model's
+        structure at plan time (NVRTC), else (False, reason)."""
+        why = ctypes.c_char_p()
+        r = int(_abi.lib().ponni_b200_model_specialised(self._m, ctypes.byref(why)))
+        return bool(r), (why.value or b"").decode()
+
     def kernel(self) -> int:
         """Kernel the next forward uses: 1 tile kernel, 2 tensor-core kernel (plans the model)."""
         k = int(_abi.lib().ponni_b200_model_kernel(self._m))

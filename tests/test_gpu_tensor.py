@@ -95,6 +95,49 @@ def test_tc_odd_widths_all_activations(dtype, oracle_lib):
         check_acc32(y, layers, dtype, x, oracle_lib)
 
 
+def _odd_layers(dtype):
+    rng = np.random.default_rng(11)
+    dims = [3, 17, 40, 96, 9, 64, 5] if dtype == pb.F32 else [3, 17, 40, 130, 9, 256, 5]
+    acts = [pb.Relu, pb.Silu, pb.Gelu, pb.Tanh, pb.Sigmoid, lambda n: pb.LeakyRelu(n, 0.2)]
+    layers = []
+    for i in range(len(dims) - 1):
+        layers.append(pb.Matvec(rng.normal(0, 1.0 / np.sqrt(dims[i]), (dims[i], dims[i + 1]))))
+        if i % 2 == 0:
+            layers.append(pb.Bias(rng.normal(0, 0.1, dims[i + 1])))
+        if i < len(dims) - 2:
+            layers.append(acts[i % len(acts)](dims[i + 1]))
+    return layers, pb.to_dtype_bytes(rng.normal(0, 1, (3, 777)), dtype)
+
+
+@pytest.mark.parametrize("case", ["cfg2", "cfg3_f16", "cfg3_bf16", "odd_f32", "odd_f16", "odd_bf16"])
+def test_tc_specialised_build_matches_generic(case, oracle_lib, monkeypatch):
+    """The model-specialised build of the resident kernel (NVRTC at plan time,
+    layer structure as compile-time constants) runs, passes the parity gates
+    and gives the generic build's results bit for bit."""
+    if case.startswith("odd"):
+        dtype = {"odd_f32": pb.F32, "odd_f16": pb.F16, "odd_bf16": pb.BF16}[case]
+        layers, x = _odd_layers(dtype)
+    else:
+        cfg = configs.ALL[case[:4]](batch=5000)
+        dtype = {"cfg2": pb.F32, "cfg3_f16": pb.F16, "cfg3_bf16": pb.BF16}[case]
+        layers = cfg.layers
+        x = pb.to_dtype_bytes(K.as_float(configs.host_inputs(cfg, 5000), cfg.dtype), dtype)
+    monkeypatch.delenv("PONNI_B200_TC_JIT", raising=False)
+    m = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR
+    spec, why = m.specialised()
+    assert spec, why
+    y = run_tc(layers, dtype, x)
+    if dtype == pb.F32:
+        check(y, oracle_lib.forward(layers, dtype, x), dtype, layers, x)
+    else:
+        check_acc32(y, layers, dtype, x, oracle_lib)
+    monkeypatch.setenv("PONNI_B200_TC_JIT", "0")
+    g = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    assert not g.specialised()[0]
+    assert np.array_equal(np.asarray(y), np.asarray(run_tc(layers, dtype, x)))
+
+
 def test_tc_strided_misaligned(oracle_lib):
     cfg = configs.cfg2(batch=1000)
     x = configs.host_inputs(cfg, 1000)

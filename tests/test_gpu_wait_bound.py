@@ -28,7 +28,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 WAITTEST_LIB = os.path.join(ROOT, "ponni_b200", "libponni_b200_waittest.so")
 
 CHILD = r'''
-import json, sys
+import json, os, sys
 import numpy as np
 import torch
 import ponni_b200 as pb
@@ -37,6 +37,10 @@ from oracle import oracle
 from tests import kat_models as K
 
 kind = sys.argv[1]
+# The resident kernel's model-specialised (NVRTC) build runs the same body
+# (tc_kernel_body.cuh) but is compiled without the test hook: use the
+# library's generic build here.
+os.environ["PONNI_B200_TC_JIT"] = "0"
 cfg, arith, kernel = {
     "tc": (configs.cfg2(batch=100), None, pb._abi.KERNEL_TENSOR),
     "ts": (configs.cfg5(batch=100), pb._abi.ARITH_TENSOR, pb._abi.KERNEL_TENSOR_STREAM),
