@@ -298,11 +298,12 @@ bool compile_and_load(const std::string& src, const char* name, cudaKernel_t* ke
     *why = n.why;
     return false;
   }
-  const char* hdr_src[] = {kJit_epi_kinds_h, kJit_activation_cuh, kJit_program_h,    kJit_device_math_cuh,
-                           kJit_tc_program_h, kJit_f32x2_cuh,     kJit_tc_common_cuh, kJit_tc_kernel_body_cuh,
-                           kJitStdint,        kJitCudaRuntime};
-  const char* hdr_name[] = {"epi_kinds.h",  "activation.cuh", "program.h",     "device_math.cuh",     "tc_program.h",
-                            "f32x2.cuh",    "tc_common.cuh",  "tc_kernel_body.cuh", "stdint.h", "cuda_runtime.h"};
+  const char* hdr_src[] = {kJit_epi_kinds_h,   kJit_activation_cuh, kJit_program_h,     kJit_device_math_cuh,
+                           kJit_tc_program_h,  kJit_f32x2_cuh,      kJit_tc_common_cuh, kJit_tc_kernel_body_cuh,
+                           kJitStdint,         kJitCudaRuntime};
+  const char* hdr_name[] = {"epi_kinds.h",  "activation.cuh", "program.h",          "device_math.cuh",
+                            "tc_program.h", "f32x2.cuh",      "tc_common.cuh",      "tc_kernel_body.cuh",
+                            "stdint.h",     "cuda_runtime.h"};
   constexpr int nh = (int)(sizeof(hdr_src) / sizeof(hdr_src[0]));
   nvrtcProgram prog = nullptr;
   if (n.create(&prog, src.c_str(), "ponni_jit.cu", nh, hdr_src, hdr_name) != NVRTC_SUCCESS) {
@@ -313,7 +314,18 @@ bool compile_and_load(const std::string& src, const char* name, cudaKernel_t* ke
   const std::string inc_opt = "-I" + inc;
   std::vector<const char*> opts = {"--gpu-architecture=sm_100a", "-std=c++17", "--fmad=true"};
   if (!inc.empty()) opts.push_back(inc_opt.c_str());
+  // PONNI_B200_JIT_LOG=1: print the generated source's resource usage (ptxas)
+  const char* logv = getenv("PONNI_B200_JIT_LOG");
+  const bool verbose = logv && atoi(logv) != 0;
+  if (verbose) opts.push_back("--ptxas-options=-v");
   const nvrtcResult rc = n.compile(prog, (int)opts.size(), opts.data());
+  if (verbose) {
+    size_t ls = 0;
+    n.log_size(prog, &ls);
+    std::string log(ls, '\0');
+    if (ls) n.log(prog, &log[0]);
+    fprintf(stderr, "[ponni_b200 jit] %s: %s\n", name, log.c_str());
+  }
   if (rc != NVRTC_SUCCESS) {
     size_t ls = 0;
     n.log_size(prog, &ls);
@@ -497,5 +509,6 @@ cudaError_t launch_tc_forward_jit(const void* kernel, const TcProgram& p, const 
   void* args[] = {&prog, const_cast<void**>(&image), const_cast<void**>(&in), &a_in_ld, &out, &a_out_ld, &a_batch, &vec, &err};
   return cudaLaunchKernel(kernel, dim3(grid), dim3(p.slots * p.slot_threads), args, p.smem_bytes, stream);
 }
+
 
 }  // namespace ponni_b200
