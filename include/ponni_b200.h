@@ -187,9 +187,9 @@ ponni_b200_status ponni_b200_model_set_arithmetic(ponni_b200_model* model, int a
 int ponni_b200_model_kernel(ponni_b200_model* model);
 
 /* 1 when the kernel the next forward uses was compiled for this model's
- * structure at plan time (NVRTC): kernel 4, or kernel 2 in its
- * model-specialised build (layer count, widths, activations as compile-time
- * constants; PONNI_B200_TC_JIT=0 disables it); 0 otherwise, with the reason
+ * structure at plan time (NVRTC): kernel 4, or kernels 2 and 5 in their
+ * model-specialised builds (layer count, widths, activations as compile-time
+ * constants; PONNI_B200_TC_JIT=0 disables them); 0 otherwise, with the reason
  * in `why` (a static-lifetime string owned by the model, may be empty) when
  * `why` is not NULL.  Plans the model.  No reference counterpart: this
  * library's diagnostic. */

@@ -670,6 +670,9 @@ ponni_b200_status pb_plan(ponni_b200_model* m) {
       if (e != cudaSuccess) return cuda_fail(m, e, "streamed tensor-core parameter upload");
       m->tc_grid = m->num_sms;
       m->kernel = 5;
+      m->tc_jit = nullptr;
+      m->tc_jit_why.clear();
+      if (!ts_jit_build(m->tsp, &m->tc_jit, &m->tc_jit_why)) m->tc_jit = nullptr;
       m->pmap.recs.insert(m->pmap.recs.end(), tc_rec.recs.begin(), tc_rec.recs.end());
       m->pmap.overflow |= tc_rec.overflow;
     }
@@ -903,7 +906,9 @@ ponni_b200_status ponni_b200_forward(ponni_b200_model* m, const void* input, int
   } else if (m->kernel == 5) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
-    e = launch_ts_forward(m->tsp, m->ts_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
+    e = m->tc_jit ? launch_ts_forward_jit(m->tc_jit, m->tsp, m->ts_image_dev, input, in_ld, output, out_ld, batch,
+                                          grid, m->err_dev, s)
+                  : launch_ts_forward(m->tsp, m->ts_image_dev, input, in_ld, output, out_ld, batch, grid, m->err_dev, s);
   } else if (m->kernel == 6) {
     const int64_t ntiles = (batch + kTcM - 1) / kTcM;
     const int grid = (int)std::min<int64_t>(m->tc_grid, ntiles);
@@ -1003,8 +1008,9 @@ int ponni_b200_model_specialised(ponni_b200_model* m, const char** why) {
   DeviceGuard guard(m->device);
   if (pb_plan(m) != PONNI_B200_OK) return 0;
   if (m->kernel == 4) return 1;
-  if (m->kernel == 2 && m->tc_jit) return 1;
-  if (why) *why = m->kernel == 2 ? m->tc_jit_why.c_str() : m->kernel == 3 ? m->jit_why.c_str() : "";
+  if ((m->kernel == 2 || m->kernel == 5) && m->tc_jit) return 1;
+  if (why)
+    *why = (m->kernel == 2 || m->kernel == 5) ? m->tc_jit_why.c_str() : m->kernel == 3 ? m->jit_why.c_str() : "";
   return 0;
 }
 

@@ -80,7 +80,7 @@ struct ponni_b200_model {
   size_t scratch_bytes = 0;
   int* err_dev = nullptr;  // device error word (bounded waits that gave up)
   std::string tc_why;      // why the tensor-core kernel is not used
-  const void* tc_jit = nullptr;  // model-specialised build of the resident tensor-core kernel (NVRTC)
+  const void* tc_jit = nullptr;  // model-specialised build of the tensor-core kernel 2 or 5 (NVRTC)
   std::string tc_jit_why;        // why it is not used
 
   int64_t capacity = 0;  // reference internal_state_capacity()

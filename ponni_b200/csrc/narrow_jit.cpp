@@ -7,6 +7,7 @@
 #include "narrow_jit.h"
 
 #include "tc_kernel.h"
+#include "tc_stream.h"
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -275,6 +276,11 @@ const char kJitStdint[] =
     "typedef unsigned char uint8_t; typedef unsigned short uint16_t; typedef unsigned int uint32_t;\n"
     "typedef unsigned long long uint64_t; typedef unsigned long long uintptr_t;\n";
 const char kJitCudaRuntime[] = "#pragma once\n";
+// The one driver type the kernels use: the tensor-map kernel parameter (the
+// driver API's definition: 16 64-bit words, 64-byte aligned).
+const char kJitCuda[] =
+    "#pragma once\n"
+    "typedef struct CUtensorMap_st { alignas(64) unsigned long long opaque[16]; } CUtensorMap;\n";
 
 // The CUDA toolkit's include directory (cuda_fp16.h), or "" when none is found.
 std::string cuda_include_dir() {
@@ -298,12 +304,15 @@ bool compile_and_load(const std::string& src, const char* name, cudaKernel_t* ke
     *why = n.why;
     return false;
   }
-  const char* hdr_src[] = {kJit_epi_kinds_h,   kJit_activation_cuh, kJit_program_h,     kJit_device_math_cuh,
-                           kJit_tc_program_h,  kJit_f32x2_cuh,      kJit_tc_common_cuh, kJit_tc_kernel_body_cuh,
-                           kJitStdint,         kJitCudaRuntime};
-  const char* hdr_name[] = {"epi_kinds.h",  "activation.cuh", "program.h",          "device_math.cuh",
-                            "tc_program.h", "f32x2.cuh",      "tc_common.cuh",      "tc_kernel_body.cuh",
-                            "stdint.h",     "cuda_runtime.h"};
+  const char* hdr_src[] = {kJit_epi_kinds_h,        kJit_activation_cuh,    kJit_program_h,
+                           kJit_device_math_cuh,    kJit_tc_program_h,      kJit_f32x2_cuh,
+                           kJit_tc_common_cuh,      kJit_tc_kernel_body_cuh, kJit_tc_stream_program_h,
+                           kJit_tc_stream_body_cuh, kJitStdint,             kJitCudaRuntime,
+                           kJitCuda};
+  const char* hdr_name[] = {"epi_kinds.h",        "activation.cuh",    "program.h",     "device_math.cuh",
+                            "tc_program.h",       "f32x2.cuh",         "tc_common.cuh", "tc_kernel_body.cuh",
+                            "tc_stream_program.h", "tc_stream_body.cuh", "stdint.h",    "cuda_runtime.h",
+                            "cuda.h"};
   constexpr int nh = (int)(sizeof(hdr_src) / sizeof(hdr_src[0]));
   nvrtcProgram prog = nullptr;
   if (n.create(&prog, src.c_str(), "ponni_jit.cu", nh, hdr_src, hdr_name) != NVRTC_SUCCESS) {
@@ -510,5 +519,75 @@ cudaError_t launch_tc_forward_jit(const void* kernel, const TcProgram& p, const 
   return cudaLaunchKernel(kernel, dim3(grid), dim3(p.slots * p.slot_threads), args, p.smem_bytes, stream);
 }
 
+
+
+// ------------------------------------------- streamed tensor-core kernel ----
+
+namespace {
+
+std::string ts_jit_source(const TsProgram& p) {
+  const char* T = p.dtype == 2 ? "__half" : "__nv_bfloat16";
+  std::ostringstream o;
+  o << "// generated: streamed tensor-core kernel, dtype " << p.dtype << ", " << p.n_layers << " layers\n"
+    << "#include \"tc_stream_body.cuh\"\n"
+    << "namespace ponni_b200 {\nnamespace tsk {\n"
+    << "struct TsJitShape {\n"
+    << "  static constexpr bool kStatic = true;\n"
+    << "  static constexpr int kNL = " << p.n_layers << ";\n"
+    << "  template <class T>\n"
+    << "  static __device__ __forceinline__ void epilogue(int l, const TsLayer& Lr, int, bool last, uint32_t tmem_row,\n"
+    << "      int c_begin, const float* bias, uint32_t a_out, T* __restrict__ out, int64_t out_ld, int64_t col,\n"
+    << "      int64_t batch, int m, long long (&t_ph)[3]) {\n"
+    << "    TsLayer L = Lr;\n"
+    << "    switch (l) {\n";
+  for (int l = 0; l < p.n_layers; ++l) {
+    const TsLayer& L = p.layers[l];
+    int act = L.act;  // the activations the streamed epilogue instantiates (others run as none, as its dispatch)
+    if (act != EPI_RELU && act != EPI_LEAKY_RELU && act != EPI_SILU && act != EPI_GELU && act != EPI_TANH &&
+        act != EPI_SIGMOID)
+      act = EPI_NONE;
+    o << "      case " << l << ":\n"
+      << "        L.n_pad = " << L.n_pad << "; L.nout = " << L.nout << "; L.has_bias = " << L.has_bias
+      << "; L.act_flags = " << L.act_flags << ";\n"
+      << "        ts_epilogue<T, " << act << ">(L, " << p.fast_act
+      << ", last, tmem_row, c_begin, bias, a_out, out, out_ld, col, batch, m, t_ph);\n"
+      << "        break;\n";
+  }
+  o << "      default: break;\n    }\n  }\n};\n"
+    << "}  // namespace tsk\n}  // namespace ponni_b200\n"
+    << "extern \"C\" __global__ void __launch_bounds__(" << kTsThreads << ", 1)\n"
+    << "ponni_ts_jit(const __grid_constant__ ponni_b200::TsProgram p, const unsigned char* __restrict__ image,\n"
+    << "             const " << T << "* __restrict__ in, long long in_ld, " << T << "* __restrict__ out,\n"
+    << "             long long out_ld, long long batch, int in_vec, const __grid_constant__ CUtensorMap in_map,\n"
+    << "             int in_tma, int* __restrict__ err) {\n"
+    << "  ponni_b200::tsk::ts_forward_body<" << T << ", false, ponni_b200::tsk::TsJitShape>(\n"
+    << "      p, image, in, in_ld, out, out_ld, batch, in_vec, in_map, in_tma, err);\n"
+    << "}\n";
+  return o.str();
+}
+
+}  // namespace
+
+bool ts_jit_build(const TsProgram& p, const void** kernel, std::string* why) {
+  if (const char* v = getenv("PONNI_B200_TC_JIT"))
+    if (atoi(v) == 0) {
+      *why = "disabled (PONNI_B200_TC_JIT=0)";
+      return false;
+    }
+  if (p.pair) {
+    *why = "CTA-pair mode runs the library's kernel";
+    return false;
+  }
+  const std::string src = ts_jit_source(p);
+  cudaKernel_t k = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    auto it = cache().find(src);
+    if (it != cache().end()) k = it->second.kernel;
+    else if (!compile_and_load(src, "ponni_ts_jit", &k, why)) return false;
+  }
+  *kernel = reinterpret_cast<const void*>(k);
+  return true;
+}
 
 }  // namespace ponni_b200

@@ -238,6 +238,55 @@ def test_ts_strided_misaligned(oracle_lib):
     assert torch.isnan(out_big[:, 0].float()).all() and torch.isnan(out_big[:, 1001:].float()).all()
 
 
+@pytest.mark.parametrize("case", ["cfg5", "odd_f16", "odd_bf16", "strided"])
+def test_ts_specialised_build_matches_generic(case, oracle_lib, monkeypatch):
+    """The model-specialised build of the streamed kernel (NVRTC at plan time,
+    the epilogue's layer loop unrolled with constant widths and activations)
+    runs, passes the gates and equals the generic build bit for bit."""
+    monkeypatch.delenv("PONNI_B200_TC_JIT", raising=False)
+    if case.startswith("odd"):
+        monkeypatch.setenv("PONNI_B200_TC_STREAM", "1")
+        dtype = pb.F16 if case == "odd_f16" else pb.BF16
+        rng = np.random.default_rng(12)
+        dims = [3, 17, 40, 130, 9, 256, 5]
+        acts = [pb.Relu, pb.Silu, pb.Gelu, pb.Tanh, pb.Sigmoid, lambda n: pb.LeakyRelu(n, 0.2)]
+        layers = []
+        for i in range(len(dims) - 1):
+            layers.append(pb.Matvec(rng.normal(0, 1.0 / np.sqrt(dims[i]), (dims[i], dims[i + 1]))))
+            if i % 2 == 0:
+                layers.append(pb.Bias(rng.normal(0, 0.1, dims[i + 1])))
+            if i < len(dims) - 2:
+                layers.append(acts[i % len(acts)](dims[i + 1]))
+        x = pb.to_dtype_bytes(rng.normal(0, 1, (3, 777)), dtype)
+    else:
+        cfg = configs.cfg5(batch=3000)
+        layers, dtype, x = cfg.layers, cfg.dtype, configs.host_inputs(cfg, 3000)
+    m = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_TENSOR)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_STREAM
+    spec, why = m.specialised()
+    assert spec, why
+
+    def run():
+        mm = pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_TENSOR)
+        if case != "strided":
+            y = mm.forward_batch_parallel(to_torch(x, dtype).cuda())
+            mm.synchronize()
+            return from_torch(y, dtype)
+        n = x.shape[1] if hasattr(x, "shape") else 3000
+        big = torch.zeros((64, 3000 + 17), dtype=torch.bfloat16, device="cuda")
+        big[:, 3:3003] = to_torch(x, dtype).cuda()
+        out_big = torch.zeros((32, 3009), dtype=torch.bfloat16, device="cuda")
+        mm.forward_batch_parallel(big[:, 3:3003], out_big[:, 1:3001])
+        mm.synchronize()
+        return from_torch(out_big[:, 1:3001].contiguous(), dtype)
+
+    y = run()
+    check_acc32(y, layers, dtype, x, oracle_lib)
+    monkeypatch.setenv("PONNI_B200_TC_JIT", "0")
+    assert not pb.Inference(layers, dtype=dtype, arithmetic=pb._abi.ARITH_TENSOR).specialised()[0]
+    assert np.array_equal(np.asarray(y), np.asarray(run()))
+
+
 @pytest.mark.parametrize("batch", [1, 129, 3000, 70000])
 def test_ts_cta_pair_mode(batch, oracle_lib, monkeypatch):
     """Clusters of two CTAs sharing M = 256 MMAs (cta_group::2), each staging
