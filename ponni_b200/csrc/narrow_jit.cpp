@@ -533,7 +533,13 @@ std::string ts_jit_source(const TsProgram& p) {
     << "namespace ponni_b200 {\nnamespace tsk {\n"
     << "struct TsJitShape {\n"
     << "  static constexpr bool kStatic = true;\n"
-    << "  static constexpr int kNL = " << p.n_layers << ";\n"
+    << "  static constexpr int kNL = " << p.n_layers << ";\n";
+  // the MMA issuer's per-layer loop bounds
+  o << "  static __device__ __forceinline__ void fix(int l, TsLayer& L) {\n    switch (l) {\n";
+  for (int l = 0; l < p.n_layers; ++l)
+    o << "      case " << l << ": L.k_pad = " << p.layers[l].k_pad << "; L.kblk = " << p.layers[l].kblk
+      << "; L.n_pad = " << p.layers[l].n_pad << "; break;\n";
+  o << "      default: break;\n    }\n  }\n"
     << "  template <class T>\n"
     << "  static __device__ __forceinline__ void epilogue(int l, const TsLayer& Lr, int, bool last, uint32_t tmem_row,\n"
     << "      int c_begin, const float* bias, uint32_t a_out, T* __restrict__ out, int64_t out_ld, int64_t col,\n"

@@ -260,6 +260,7 @@ struct TsJobs {
 struct TsRuntimeShape {
   static constexpr bool kStatic = false;
   static constexpr int kNL = 0;
+  static __device__ __forceinline__ void fix(int, TsLayer&) {}
   template <class T>
   static __device__ __forceinline__ void epilogue(int, const TsLayer& L, int fast, bool last, uint32_t tmem_row,
                                                   int c_begin, const float* bias, uint32_t a_out,
@@ -461,14 +462,12 @@ __device__ __forceinline__ void ts_forward_body(const TsProgram& p, const unsign
       const uint32_t hi_mn = (uint32_t)(smem_desc(0, k0b, 1024) >> 32);
       const uint32_t lo_mn = (uint32_t)smem_desc(0, k0b, 1024);
       const uint32_t ring_lo = lo_k | ((s_ring >> 4) & 0x3FFFu);
-      for (int64_t r = 0; r < jobs.rounds() && ok; ++r)
-        for (int l = 0; l < nl && ok; ++l)
-          for (int s = 0; s < kTsSlots && ok; ++s) {
-            if (r >= jobs.count[s]) continue;
-            const TsLayer& L = layers[l];
+      // One job (layer l of slot s's tile); false when a wait gave up.
+      auto mma_job = [&](int l, int s, const TsLayer& L) -> bool {
+          {
             TS_T(tw);
             if (l == 0) {
-              if (!(ok = wait_x(b_stage + 8u * s, st_ph[s]))) break;
+              if (!(ok = wait_x(b_stage + 8u * s, st_ph[s]))) return false;
               st_ph[s] ^= 1u;
             }
             // The slot's previous epilogue has read its accumulator and
@@ -477,7 +476,7 @@ __device__ __forceinline__ void ts_forward_body(const TsProgram& p, const unsign
               for (int h = 0; h < 2 && ok; ++h) ok = wait_x(b_kbar + 8u * (2 * s + h), k_ph[s]);
               k_ph[s] ^= 1u;
             }
-            if (!ok) break;
+            if (!ok) return false;
             TS_ACC(w_epi, tw);
             has_prev[s] = true;
             tc_fence_after();
@@ -516,6 +515,23 @@ __device__ __forceinline__ void ts_forward_body(const TsProgram& p, const unsign
             if (!PAIR && in_tma && ok && l == nl - 1) umma_commit_warp(b_free + 8u * s);  // stage the next tile
             skip = false;
           }
+          return ok;
+      };
+      for (int64_t r = 0; r < jobs.rounds() && ok; ++r) {
+        if constexpr (Shape::kStatic) {
+#pragma unroll
+          for (int l = 0; l < Shape::kNL; ++l) {
+            TsLayer L = layers[l];
+            Shape::fix(l, L);
+            for (int s = 0; s < kTsSlots; ++s)
+              if (ok && r < jobs.count[s]) ok = mma_job(l, s, L);
+          }
+        } else {
+          for (int l = 0; l < nl && ok; ++l)
+            for (int s = 0; s < kTsSlots && ok; ++s)
+              if (r < jobs.count[s]) ok = mma_job(l, s, layers[l]);
+        }
+      }
       // Drain: every MMA issued has completed before TMEM is freed (both CTAs).
       if constexpr (PAIR) umma_commit_pair_warp(b_drain);
       else umma_commit_warp(b_drain);
