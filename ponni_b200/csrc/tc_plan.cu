@@ -357,12 +357,13 @@ bool tr_plan(const ponni_b200_model* m, TrProgram& p, std::vector<unsigned char>
     L.op_first = nops;
     L.ln = -1;
     L.idesc = make_idesc(dt, L.n_pad, false);
-    // Accumulators: main groups of the dominant products plus one correction
-    // accumulator, within the slot's 256 TMEM columns.
+    // Accumulators: groups of one K block (four K steps) of the dominant
+    // products where the job's 128 accumulator columns allow, else one
+    // group; the smaller products go into group 0 before its x0*w0 steps.
     int gs = std::min(4, L.nsteps);
-    while ((int64_t)((L.nsteps + gs - 1) / gs + 1) * L.n_pad > (int64_t)kTrSlotTmem) ++gs;
+    if ((int64_t)((L.nsteps + gs - 1) / gs) * L.n_pad > (int64_t)kTrAccCols) gs = L.nsteps;
     L.group_steps = gs;
-    L.groups = (L.nsteps + gs - 1) / gs + 1;
+    L.groups = (L.nsteps + gs - 1) / gs;
     ++i;
     for (; i < Ls.size() && Ls[i].d.kind != PONNI_B200_MATVEC; ++i) {
       const auto& e = Ls[i].d;
@@ -434,10 +435,10 @@ bool tr_plan(const ponni_b200_model* m, TrProgram& p, std::vector<unsigned char>
   p.nparts = 3;
   p.nin = p.layers[0].nin;
   p.nout = p.layers[nl - 1].nout;
-  // Image: per layer, per K block, the three weight parts as chunks of
-  // n_pad rows x 128 B (SW128 K-major), in the order the MMAs consume them
-  // (part 2, part 1, part 0); then the float vectors (bias[128] or
-  // gamma[128] beta[128]).
+  // Image: per layer the weight chunks of n_pad rows x 128 B (SW128
+  // K-major) in the order the MMAs consume them: parts 2 and 1 of each K
+  // block, then part 0 of each K block; then the float vectors (bias[128]
+  // or gamma[128] beta[128]).
   uint64_t off = 0;
   for (int l = 0; l < nl; ++l) {
     p.layers[l].w_off = off;
@@ -468,10 +469,10 @@ bool tr_plan(const ponni_b200_model* m, TrProgram& p, std::vector<unsigned char>
         const float r = w - __bfloat162float(b0);
         const __nv_bfloat16 b1 = __float2bfloat16_rn(r);
         const __nv_bfloat16 b2 = __float2bfloat16_rn(r - __bfloat162float(b1));
-        const size_t kb_base = L.w_off + (size_t)(k / 64) * 3 * chunk;
-        const size_t o2 = put_kmajor(image, kb_base + 0 * chunk, L.n_pad, n, k % 64, 2, &b2);
-        const size_t o1 = put_kmajor(image, kb_base + 1 * chunk, L.n_pad, n, k % 64, 2, &b1);
-        const size_t o0 = put_kmajor(image, kb_base + 2 * chunk, L.n_pad, n, k % 64, 2, &b0);
+        const size_t kb = (size_t)(k / 64);
+        const size_t o2 = put_kmajor(image, L.w_off + (2 * kb + 0) * chunk, L.n_pad, n, k % 64, 2, &b2);
+        const size_t o1 = put_kmajor(image, L.w_off + (2 * kb + 1) * chunk, L.n_pad, n, k % 64, 2, &b1);
+        const size_t o0 = put_kmajor(image, L.w_off + (2 * (size_t)L.kblk + kb) * chunk, L.n_pad, n, k % 64, 2, &b0);
         if (rec) {
           rec->add(src, PIMG_TS, PENC_SPLIT0, o0);
           rec->add(src, PIMG_TS, PENC_SPLIT1, o1);
@@ -492,7 +493,10 @@ bool tr_plan(const ponni_b200_model* m, TrProgram& p, std::vector<unsigned char>
         if (rec) rec->add(src, PIMG_TS, PENC_F32, o.off + 4 * ((size_t)q * 128 + i));
       }
   }
-  p.scratch_per_cta = (uint64_t)kTrSlots * (uint64_t)p.n_saved * kTrMaxN * 128 * 4;
+  // One saved state fits in TMEM beside each slot's accumulators; two go to
+  // the global scratch area.
+  p.saved_tmem = p.n_saved <= 1 ? 1 : 0;
+  p.scratch_per_cta = p.saved_tmem ? 0 : (uint64_t)kTrSlots * (uint64_t)p.n_saved * kTrMaxN * 128 * 4;
   // Shared memory: per slot three operand parts of 2 K blocks, the weight
   // ring, the LayerNorm exchange and the mbarriers.  The dynamic shared
   // memory base is 1024-byte aligned (checked by the kernel), so no slack.

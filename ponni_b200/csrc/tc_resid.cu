@@ -7,13 +7,14 @@
 //     (cp.async.bulk, byte-counted mbarriers, no multicast).  A chunk is one
 //     bf16 part of one K block of 64 of a layer's weights, N rows x 128 B,
 //     pre-swizzled (SW128 K-major) on the host;
-//   MMA issuer (warp 17, one thread): per job (one Matvec of one tile of 128
-//     batch columns) issues the six split products chunk by chunk
-//     (tcgen05.mma kind::f16, bf16 operands, fp32 accumulators in the slot's
-//     256 TMEM columns): x0*w0 into the main accumulator, the five smaller
-//     products into a correction accumulator (the tensor core's fp32
-//     accumulation truncates; keeping the small products apart keeps the
-//     result fp32-accurate);
+//   MMA issuer (warp 17, the whole warp, one elected lane issues): per job
+//     (one Matvec of one tile of 128 batch columns) issues the six split
+//     products chunk by chunk (tcgen05.mma kind::f16, bf16 operands, fp32
+//     accumulators in the slot's first 128 TMEM columns): the five smaller
+//     products first, then the dominant x0*w0 (the tensor core's fp32
+//     accumulation truncates; summing the small products while the
+//     accumulator is small keeps the result fp32-accurate), x0*w0 in groups
+//     of one K block where the columns allow;
 //   epilogue (warps 0-15, 4 TMEM lane quarters x 4 column quarters; a
 //     thread holds one 32-column chunk of one row = one batch column): all
 //     16 warps take the jobs one at a time in the issuer's order; per job
@@ -31,9 +32,12 @@
 //     operand (shared memory, K-major SW128) or write the caller's output.
 //     LayerNorm keeps the row's values in registers; the four column
 //     quarters exchange (mean, squared deviations) pairs through two
-//     already-read accumulator columns of TMEM, one barrier.  Saved states
-//     live in a per-CTA, per-slot global scratch area (64 KB per slot and
-//     state; L2-resident), written and read back by the same thread.
+//     already-read accumulator columns of TMEM, one barrier per lane
+//     quarter.  A single saved state lives in the slot's other 128 TMEM
+//     columns (tcgen05.st / tcgen05.ld by the thread that owns the row and
+//     columns); models with two saved states keep them in a per-CTA, per-slot
+//     global scratch area (64 KB per slot and state; L2-resident), written
+//     and read back by the same thread.
 // Two tiles are in flight and their jobs alternate Matvec by Matvec, so the
 // epilogue of one tile's job overlaps the MMAs of the other tile's job.
 //
@@ -44,8 +48,8 @@
 //
 // Every wait is bounded: a role that gives up raises the CTA's abort flag,
 // records an error code and the CTA drains its copies and MMAs before it
-// frees TMEM; the epilogue warps decide to leave together (a barrier
-// reduction), so none is left waiting at a named barrier.
+// frees TMEM; the epilogue warps of a lane quarter decide to leave together
+// (a barrier reduction), so none is left waiting at a named barrier.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -183,28 +187,47 @@ struct TrEpi {
   const unsigned char* image;
   float4* saved_cta;  // this CTA's saved states: [slot][state][f / 4][128 rows] float4
   int n_saved;
+  int saved_tmem;     // the saved state lives in TMEM (columns kTrAccCols.. of the slot)
   int cq, m;          // column quarter, row
+  int lq;             // TMEM lane quarter (warp % 4)
   // the job's slot
   float4* saved;      // the slot's saved states
   uint32_t a[3];      // the slot's A operand parts
   uint32_t tmem_row;  // the slot's accumulators + this warp's lane quarter
 };
 
-// Named barrier over the 16 epilogue warps (id 1; 0 is __syncthreads).
-__device__ __forceinline__ void epi_sync() {
-  asm volatile("bar.sync 1, %0;\n" ::"r"(kTrEpiWarps * 32) : "memory");
+// Named barrier over the four epilogue warps of one TMEM lane quarter (the
+// warps w, w + 4, w + 8, w + 12 that hold the four column quarters of the
+// same rows; ids 1-4, 0 is __syncthreads).  Only these warps exchange data,
+// so the quarters run independently of one another.
+__device__ __forceinline__ void epi_sync(int lq) {
+  asm volatile("bar.sync %0, 128;\n" ::"r"(1 + lq) : "memory");
 }
-__device__ __forceinline__ int epi_sync_or(int pred) {
+__device__ __forceinline__ int epi_sync_or(int lq, int pred) {
   int r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "bar.red.or.pred q, %2, 128, p;\n\t"
       "selp.b32 %0, 1, 0, q;\n\t}\n"
       : "=r"(r)
-      : "r"(pred), "r"(kTrEpiWarps * 32)
+      : "r"(pred), "r"(1 + lq)
       : "memory");
   return r;
+}
+
+// 32 columns of this warp's 32 TMEM lanes, completed before returning.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+      "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]),
+      "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]),
+      "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
 
 // Element-wise operations [o0, o1) on the 32 columns c0.. of this row.
@@ -226,6 +249,12 @@ __device__ __forceinline__ void tr_ops(const TrOp* ops, int o0, int o1, float (&
 #if !(PONNI_B200_TR_DIAG & 1)  // diagnostic builds: bit 1 skips activations
       act_dispatch(o.arg, v, o.flags, o.s0, o.s1);
 #endif
+    } else if (o.kind == TR_ADD && E.saved_tmem) {
+      float t[32];
+      tmem_ld32(E.tmem_row + kTrAccCols + (uint32_t)c0, t);
+      f2::add_n(v, t);
+    } else if (o.kind == TR_SAVE && E.saved_tmem) {
+      tmem_st32(E.tmem_row + kTrAccCols + (uint32_t)c0, v);
     } else if (o.kind == TR_ADD) {
       const float4* sv = E.saved + (size_t)o.arg * (kTrMaxN / 4) * 128 + (c0 / 4) * 128 + E.m;
 #pragma unroll
@@ -283,13 +312,11 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
   const int nv = min(32, nout - c0);  // valid columns of the chunk
   float v[32];
   if (active) {
-    float w[32];
-    const uint32_t corr = E.tmem_row + (uint32_t)((groups - 1) * n_pad);
-    tmem_ld32x2(corr + (uint32_t)c0, E.tmem_row + (uint32_t)c0, v, w);
-    f2::add_n(v, w);
-#pragma unroll 1
-    for (int g = 1; g + 1 < groups; ++g) {
-      tmem_ld32(E.tmem_row + (uint32_t)(g * n_pad + c0), w);
+    if (groups == 1) {
+      tmem_ld32(E.tmem_row + (uint32_t)c0, v);
+    } else {
+      float w[32];
+      tmem_ld32x2(E.tmem_row + (uint32_t)c0, E.tmem_row + (uint32_t)(n_pad + c0), v, w);
       f2::add_n(v, w);
     }
     tr_ops(p.ops, o0, o_ln, v, c0, E);
@@ -302,9 +329,9 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
     // pairwise update of Chan, Golub and LeVeque (mean = sum n_q m_q / n,
     // M2 = sum M2_q + sum n_q (m_q - mean)^2, var = M2 / n).  The pairs go
     // through TMEM: each warp writes its pair into the first two of its own,
-    // already read, correction-accumulator columns; one barrier; each warp
-    // reads the pairs of the row's quarters.
-    const uint32_t corr_row = E.tmem_row + (uint32_t)((groups - 1) * n_pad);
+    // already read, accumulator columns; one barrier; each warp reads the
+    // pairs of the row's quarters.
+    const uint32_t corr_row = E.tmem_row;
     if (active) {
       float qmean, qm2;
       if (nv >= 32) {
@@ -338,7 +365,7 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
       tmem_st2(corr_row + (uint32_t)c0, qmean, qm2);
     }
     tc_fence_before();
-    epi_sync();
+    epi_sync(E.lq);
     tc_fence_after();
     float mean = 0.f, var = 0.f;
     if (active) {
@@ -416,49 +443,90 @@ __device__ __forceinline__ void tr_stage_input(const float* __restrict__ in, int
 struct TrIssue {
   uint32_t a0, a1, a2;  // low descriptor halves of the slot's A operand parts
   uint32_t hi;          // shared upper descriptor half
-  uint32_t d_main, dc;  // current main accumulator, correction accumulator
-  uint32_t g_in, gs;    // K steps issued into the current main accumulator, steps per main accumulator
+  uint32_t d;           // the job's accumulator group 0 (group 1 at d + n_pad)
   uint32_t n_pad, idesc;
 };
 
-// One weight chunk (part 2 - J of K block kb): wait for it, issue its
-// products (x0 w2 | x1 w1, x0 w1 | x2 w0, x1 w0, x0 w0; smallest first
-// into the correction accumulator), release the ring stage.
-template <int J>
-__device__ __forceinline__ bool tr_chunk(TrIssue& I, int kb, int nsteps, uint32_t& use, uint32_t ring_lo,
-                                         uint32_t b_full, uint32_t b_empty, volatile int* abort_flag,
-                                         long long& w_full) {
+// Wait (bounded, whole warp) for the weight chunk of ring use `use`.
+__device__ __forceinline__ bool tr_wait_chunk(uint32_t use, uint32_t b_full, volatile int* abort_flag,
+                                              long long& w_full) {
   (void)w_full;
-  const uint32_t st = use & 1u;
   TR_T(tf);
-  if (!__all_sync(0xffffffffu, wait_phase_abort(b_full + 8u * st, (use >> 1) & 1u, abort_flag, kWaitCycles)))
-    return false;
+  const bool ok =
+      __all_sync(0xffffffffu, wait_phase_abort(b_full + 8u * (use & 1u), (use >> 1) & 1u, abort_flag, kWaitCycles));
   TR_ACC(w_full, tf);
   tc_fence_after();
-  const uint32_t b = ring_lo + st * (kTrChunkBytes >> 4);
+  return ok;
+}
+
+// One job's MMAs (NS K steps of 16, accumulator groups of GS steps), all
+// offsets and accumulate flags compile-time constants.  Ring chunks in
+// image order: parts 2 and 1 of each K block (x0 w2 | x1 w1, x0 w1), then
+// part 0 of each K block (x2 w0, x1 w0; the stage is held), then the
+// dominant x0 w0 products from the held stages, each stage released after
+// its last MMA.  The five small products all go into group 0 before any
+// x0 w0 product, so the truncating accumulation loses nothing of them that
+// matters; group g takes x0 w0 of K steps [g GS, (g + 1) GS).
+template <int NS, int GS>
+__device__ __forceinline__ bool tr_job(const TrIssue& I, uint32_t& use, uint32_t ring_lo, uint32_t b_full,
+                                       uint32_t b_empty, volatile int* abort_flag, long long& w_full) {
+  constexpr int KB = (NS + 3) / 4;
+  static_assert(KB <= kTrStages, "part-0 chunks of every K block are held in the ring at once");
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    if (kb * 4 + kk < nsteps) {
-      const uint32_t ao = (uint32_t)kb * 1024u + (uint32_t)kk * 2u;  // K block: 16 KB; K step: 32 B
-      const uint32_t bk = b + (uint32_t)kk * 2u;
-      if constexpr (J == 0) {
-        umma_f16_lh_warp(I.dc, I.a0 + ao, bk, I.hi, I.idesc, (kb | kk) ? 1u : 0u);
-      } else if constexpr (J == 1) {
-        umma_f16_lh_warp(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
-        umma_f16_lh_warp(I.dc, I.a0 + ao, bk, I.hi, I.idesc, 1u);
-      } else {
-        umma_f16_lh_warp(I.dc, I.a2 + ao, bk, I.hi, I.idesc, 1u);
-        umma_f16_lh_warp(I.dc, I.a1 + ao, bk, I.hi, I.idesc, 1u);
-        umma_f16_lh_warp(I.d_main, I.a0 + ao, bk, I.hi, I.idesc, I.g_in ? 1u : 0u);
-        if (++I.g_in == I.gs) {
-          I.g_in = 0;
-          I.d_main += I.n_pad;
+  for (int kb = 0; kb < KB; ++kb) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {  // part 2, then part 1
+      if (!tr_wait_chunk(use, b_full, abort_flag, w_full)) return false;
+      const uint32_t b = ring_lo + (use & 1u) * (kTrChunkBytes >> 4);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        if (kb * 4 + kk < NS) {
+          const uint32_t ao = (uint32_t)kb * 1024u + (uint32_t)kk * 2u;  // K block: 16 KB; K step: 32 B
+          const uint32_t bk = b + (uint32_t)kk * 2u;
+          if (j == 0) {
+            umma_f16_lh_warp(I.d, I.a0 + ao, bk, I.hi, I.idesc, (kb | kk) ? 1u : 0u);
+          } else {
+            umma_f16_lh_warp(I.d, I.a1 + ao, bk, I.hi, I.idesc, 1u);
+            umma_f16_lh_warp(I.d, I.a0 + ao, bk, I.hi, I.idesc, 1u);
+          }
         }
       }
+      umma_commit_warp(b_empty + 8u * (use & 1u));
+      ++use;
     }
   }
-  umma_commit_warp(b_empty + 8u * st);
-  ++use;
+  uint32_t held[KB];
+#pragma unroll
+  for (int kb = 0; kb < KB; ++kb) {  // part 0: the small products x2 w0, x1 w0
+    if (!tr_wait_chunk(use, b_full, abort_flag, w_full)) return false;
+    held[kb] = use & 1u;
+    const uint32_t b = ring_lo + held[kb] * (kTrChunkBytes >> 4);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      if (kb * 4 + kk < NS) {
+        const uint32_t ao = (uint32_t)kb * 1024u + (uint32_t)kk * 2u;
+        umma_f16_lh_warp(I.d, I.a2 + ao, b + (uint32_t)kk * 2u, I.hi, I.idesc, 1u);
+        umma_f16_lh_warp(I.d, I.a1 + ao, b + (uint32_t)kk * 2u, I.hi, I.idesc, 1u);
+      }
+    }
+    ++use;
+  }
+#pragma unroll
+  for (int kb = 0; kb < KB; ++kb) {  // the dominant products x0 w0
+    const uint32_t b = ring_lo + held[kb] * (kTrChunkBytes >> 4);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      constexpr int kGS = GS;
+      const int step = kb * 4 + kk;
+      if (step < NS) {
+        const int g = step / kGS;
+        const uint32_t acc = (g == 0 || step % kGS != 0) ? 1u : 0u;
+        umma_f16_lh_warp(I.d + (uint32_t)g * I.n_pad, I.a0 + (uint32_t)kb * 1024u + (uint32_t)kk * 2u,
+                         b + (uint32_t)kk * 2u, I.hi, I.idesc, acc);
+      }
+    }
+    umma_commit_warp(b_empty + 8u * held[kb]);
+  }
   return true;
 }
 
@@ -577,7 +645,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
         for (int l = 0; l < nl && ok; ++l) {
           const TrLayer& L = p.layers[l];
           const uint32_t n_pad = (uint32_t)L.n_pad, gs = (uint32_t)L.group_steps, idesc = L.idesc;
-          const int kblk = L.kblk, nsteps = L.nsteps, groups = L.groups;
+          const int nsteps = L.nsteps;
           for (int s = 0; s < kTrSlots && ok; ++s) {
             if (r >= (s ? jobs.c1 : jobs.c0)) continue;
             // The slot's operand is written and its accumulators are free.
@@ -589,10 +657,7 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             TR_ACC(w_epi, te);
             tc_fence_after();
             TrIssue I;
-            I.d_main = tmem_base + (uint32_t)s * kTrSlotTmem;
-            I.dc = I.d_main + (uint32_t)(groups - 1) * n_pad;
-            I.g_in = 0;
-            I.gs = gs;
+            I.d = tmem_base + (uint32_t)s * kTrSlotTmem;
             I.n_pad = n_pad;
             I.idesc = idesc;
             I.hi = hi;
@@ -600,10 +665,13 @@ __global__ void __launch_bounds__(kTrThreads, 1)
             I.a0 = lo_flags | ((a_base >> 4) & 0x3FFFu);
             I.a1 = I.a0 + (kTrPartBytes >> 4);
             I.a2 = I.a0 + 2 * (kTrPartBytes >> 4);
-            for (int kb = 0; kb < kblk && ok; ++kb) {
-              ok = tr_chunk<0>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full) &&
-                   tr_chunk<1>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full) &&
-                   tr_chunk<2>(I, kb, nsteps, use, ring_lo, b_full, b_empty, abort_flag, w_full);
+            switch (nsteps * 16 + (int)gs) {
+#define TR_JOB(n, g) \
+  case n * 16 + g: ok = tr_job<n, g>(I, use, ring_lo, b_full, b_empty, abort_flag, w_full); break;
+              TR_JOB(1, 1) TR_JOB(2, 2) TR_JOB(3, 3) TR_JOB(4, 4) TR_JOB(5, 5) TR_JOB(6, 6) TR_JOB(7, 7)
+              TR_JOB(8, 8) TR_JOB(5, 4) TR_JOB(6, 4) TR_JOB(7, 4) TR_JOB(8, 4)
+#undef TR_JOB
+              default: ok = false; break;
             }
             if (ok && !skip) umma_commit_warp(b_accf + 8u * s);
             skip = false;
@@ -631,9 +699,11 @@ __global__ void __launch_bounds__(kTrThreads, 1)
     // the other slot's job.
     TrEpi E;
     E.cq = warp >> 2;
+    E.lq = warp & 3;
     E.m = (warp & 3) * 32 + lane;
     E.image = image;
     E.n_saved = p.n_saved;
+    E.saved_tmem = p.saved_tmem;
     E.saved_cta = reinterpret_cast<float4*>(scratch + (size_t)blockIdx.x * (p.scratch_per_cta / 4));
     auto select_slot = [&](int s) {
       E.saved = E.saved_cta + (size_t)s * p.n_saved * (kTrMaxN / 4) * 128;
@@ -666,8 +736,8 @@ __global__ void __launch_bounds__(kTrThreads, 1)
           int got = 0;
           if (lane == 0) got = wait_phase_abort(b_accf + 8u * s, s ? ph1 : ph0, abort_flag, kWaitCycles) ? 1 : 0;
           got = __shfl_sync(0xffffffffu, got, 0);
-          // The epilogue warps leave together (none is left at a named barrier).
-          if (epi_sync_or(!got)) {
+          // The warps of a lane quarter leave together (none is left at a named barrier).
+          if (epi_sync_or(E.lq, !got)) {
             ok = false;
             break;
           }

@@ -16,12 +16,17 @@
 // Work unit ("job"): one Matvec for one tile of 128 batch columns,
 // D[128 x N<=128] = A[128 x K<=128] * W[K x N], A and W split exactly into
 // bf16 parts (x = x0 + x1 + x2) and the six products of order <= 2
-// accumulated in two TMEM accumulators (main: x0*w0, correction: the rest).
+// accumulated in TMEM, the five small ones first: the tensor core's fp32
+// accumulation truncates, and summing the small products before the
+// dominant x0*w0 ones keeps their truncation relative to their own size.
 // The weights stream through a two-stage shared-memory ring in chunks of one
-// part of one K block of 64 (N rows x 128 B).  Two tiles are in flight per
-// CTA and their jobs alternate Matvec by Matvec, so one tile's epilogue
-// overlaps the other's MMAs.  Saved states live in a per-CTA global scratch
-// area (L2-resident: 64 KB per tile slot and saved state).
+// part of one K block of 64 (N rows x 128 B): per layer parts 2 and 1 of
+// each K block, then the part-0 chunks, held until the x0*w0 products.  Two
+// tiles are in flight per CTA and their jobs alternate Matvec by Matvec, so
+// one tile's epilogue overlaps the other's MMAs.  A single saved state lives
+// in TMEM next to its tile's accumulators (128 columns per slot); models with
+// two keep them in a per-CTA global scratch area (L2-resident: 64 KB per
+// tile slot and saved state).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -44,7 +49,8 @@ constexpr int kTrEpiWarps = 16;                 // epilogue warps: 4 TMEM lane q
 constexpr int kTrProducerWarp = kTrEpiWarps;
 constexpr int kTrMmaWarp = kTrEpiWarps + 1;
 constexpr int kTrThreads = (kTrEpiWarps + 2) * 32;
-constexpr uint32_t kTrSlotTmem = 256;           // TMEM columns per slot: main + correction accumulators
+constexpr uint32_t kTrSlotTmem = 256;           // TMEM columns per slot: accumulators + saved state
+constexpr uint32_t kTrAccCols = 128;            // accumulator columns of a job (its main groups)
 constexpr uint32_t kTrPartBytes = 2 * 128 * 128;  // one operand part: 2 K blocks x 128 rows x 128 B
 constexpr int kTrMaxParts = 3;
 
@@ -70,8 +76,8 @@ struct TrLayer {
   int32_t k_pad, n_pad;  // K and N rounded to 16
   int32_t kblk;          // K blocks of 64
   int32_t nsteps;        // UMMA K steps of 16
-  int32_t group_steps;   // K steps per main accumulator
-  int32_t groups;        // accumulators: main groups + 1 correction (split) or main groups only
+  int32_t group_steps;   // K steps per accumulator group (4: one K block, or all)
+  int32_t groups;        // accumulator groups (1 or 2); the five smaller products go into group 0
   int32_t op_first;      // epilogue operations [op_first, op_first + n_ops)
   int32_t n_ops;
   int32_t ln;            // index (within the layer's operations) of its LayerNorm, or -1
@@ -87,7 +93,8 @@ struct TrProgram {
   int32_t n_saved;        // saved-state slots used
   uint32_t smem_bytes;    // dynamic shared memory requested
   uint64_t image_bytes;   // weight chunks + float vectors
-  uint64_t scratch_per_cta;  // bytes of saved-state scratch per CTA
+  int32_t saved_tmem;     // 1: the (single) saved state lives in TMEM beside the accumulators
+  uint64_t scratch_per_cta;  // bytes of saved-state scratch per CTA (0 with saved_tmem)
   TrLayer layers[kTrMaxLayers];
   TrOp ops[kTrMaxOps];
 };

@@ -329,10 +329,15 @@ def test_tr_cfg4(batch, oracle_lib):
 
 
 def test_tr_scratch_is_reported():
+    # one saved state: kept in TMEM beside the accumulators, no device scratch
     m = pb.Inference(configs.cfg4(batch=10).layers, dtype=pb.F32)
     assert m.kernel() == pb._abi.KERNEL_TENSOR_RESID
+    assert m.scratch_bytes() == 0
+    # two saved states: a global scratch area per CTA
+    m2 = pb.Inference(resid_model(np.random.default_rng(3)), dtype=pb.F32)
+    assert m2.kernel() == pb._abi.KERNEL_TENSOR_RESID
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    assert m.scratch_bytes() == sms * 2 * 1 * 128 * 128 * 4  # two tile slots x one saved state
+    assert m2.scratch_bytes() == sms * 2 * 2 * 128 * 128 * 4  # two tile slots x two saved states
 
 
 @pytest.mark.parametrize("grid,batch", [(1, 1000), (2, 1537), (3, 4099)])
@@ -375,6 +380,28 @@ def test_tr_all_fused_operations(batch, grid, oracle_lib, monkeypatch):
     rng = np.random.default_rng(21)
     layers = resid_model(rng)
     x = rng.normal(0, 1, (24, batch)).astype(np.float32)
+    y = run_tr(layers, x, monkeypatch, grid)
+    check(y, oracle_lib.forward(layers, pb.F32, x), pb.F32, layers, x)
+
+
+@pytest.mark.parametrize("batch,grid", [(7, None), (1500, None), (2049, 2)])
+def test_tr_one_saved_state_in_tmem(batch, grid, oracle_lib, monkeypatch):
+    """One saved state (kept in TMEM): K of 48, 64, 112 (two accumulator
+    groups at width 64), Save_State followed by a Binop_Add of the same state
+    in one epilogue, and a state saved again after its Binop_Add."""
+    rng = np.random.default_rng(5)
+    ln = lambda n: pb.LayerNorm(rng.normal(1, 0.2, n), rng.normal(0, 0.2, n))  # noqa: E731
+    layers = [pb.Matvec(rng.normal(0, 0.15, (48, 64))), pb.Bias(rng.normal(0, 0.1, 64)), pb.Save_State(64, 2),
+              ln(64),
+              pb.Matvec(rng.normal(0, 0.12, (64, 112))), pb.Bias(rng.normal(0, 0.1, 112)), pb.Gelu(112),
+              pb.Matvec(rng.normal(0, 0.1, (112, 64))), pb.Bias(rng.normal(0, 0.1, 64)), pb.Binop_Add(64, 2),
+              pb.Save_State(64, 2), pb.Binop_Add(64, 2), ln(64),
+              pb.Matvec(rng.normal(0, 0.12, (64, 64))), pb.Silu(64), pb.Binop_Add(64, 2),
+              pb.Matvec(rng.normal(0, 0.2, (64, 5))), pb.Bias(rng.normal(0, 0.1, 5))]
+    m = pb.Inference(layers, dtype=pb.F32)
+    assert m.kernel() == pb._abi.KERNEL_TENSOR_RESID
+    assert m.scratch_bytes() == 0
+    x = rng.normal(0, 1, (48, batch)).astype(np.float32)
     y = run_tr(layers, x, monkeypatch, grid)
     check(y, oracle_lib.forward(layers, pb.F32, x), pb.F32, layers, x)
 
