@@ -473,8 +473,9 @@ std::string tc_jit_source(const TcProgram& p) {
   arr("kAct", [](const TcLayer& L) { return L.act; });
   arr("kFl", [](const TcLayer& L) { return L.act_flags; });
   arr("kB", [](const TcLayer& L) { return L.has_bias; });
+  arr("kBM", [](const TcLayer& L) { return L.bias_mma; });
   o << "    L.k_pad = kK[l]; L.n_pad = kN[l]; L.nout = kOut[l]; L.groups = kG[l]; L.group_steps = kGS[l];\n"
-    << "    L.act = kAct[l]; L.act_flags = kFl[l]; L.has_bias = kB[l];\n"
+    << "    L.act = kAct[l]; L.act_flags = kFl[l]; L.has_bias = kB[l]; L.bias_mma = kBM[l];\n"
     << "  }\n};\n}  // namespace tck\n}  // namespace ponni_b200\n"
     << "extern \"C\" __global__ void __launch_bounds__(" << bound << ", 1)\n"
     << "ponni_tc_jit(const __grid_constant__ ponni_b200::TcProgram p, const unsigned char* __restrict__ image,\n"

@@ -171,9 +171,16 @@ __device__ __forceinline__ int wg_sync_or(int wg, int pred) {
 // descriptors of each operand are built once per layer; the K steps then only
 // add the step offset to the 14-bit start-address field (>> 4), which never
 // carries out of the field for shared-memory addresses.
+// No-swizzle K-major descriptor (8-row core matrices of 16 bytes: `lbo`
+// between the two K halves of a 16-element K step, `sbo` between row groups).
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
 template <bool SPLIT>
 __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint32_t d_tmem, const uint32_t* s_a,
-                                            uint32_t s_image, uint32_t stage) {
+                                            uint32_t s_image, uint32_t stage, uint32_t s_ones, uint32_t s_zero) {
   const int nsteps = L.k_pad / 16;  // UMMA K = 16 for 16-bit operands (32 bytes)
   const uint64_t b_step_kb = (uint64_t)L.n_pad * 8;  // (n_pad * 128) >> 4 per K block
   const uint32_t gstep = (uint32_t)L.group_steps, n_pad = (uint32_t)L.n_pad;
@@ -209,20 +216,28 @@ __device__ __forceinline__ void issue_layer(const TcLayer& L, bool layer0, uint3
     }
   } else {
     const uint64_t b0 = smem_desc(s_image + L.w_off[0], 16, 1024);
+    // The bias first: D = ones x bias block (every row of A is e_0).
+    uint32_t acc0 = 0;
+    if (L.bias_mma) {
+      const uint32_t s_bias = s_image + L.bias_off;
+      umma_f16_warp(d, smem_desc_plain(s_ones, s_zero - s_ones, 0), smem_desc_plain(s_bias, s_zero - s_bias, 128),
+                    idesc, 0u);
+      acc0 = 1;
+    }
     if (layer0) {
       // The staged input tile is the MN-major layer-0 operand: one K step =
       // 32 bytes of K for 128 rows = 4096 bytes.
       const uint64_t a0 = smem_desc(stage, 1024, 2048);
       for (int s = 0; s < nsteps; ++s) {
         const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
-        umma_f16_warp(d, a0 + (uint64_t)s * 256, b0 + bo, L.idesc_mn, s > 0 ? 1u : 0u);
+        umma_f16_warp(d, a0 + (uint64_t)s * 256, b0 + bo, L.idesc_mn, (s > 0 || acc0) ? 1u : 0u);
       }
     } else {
       const uint64_t a0 = smem_desc(s_a[0], 16, 1024);
       for (int s = 0; s < nsteps; ++s) {
         const uint64_t ao = (uint64_t)(s >> 2) * 1024 + (uint64_t)(s & 3) * 2;
         const uint64_t bo = (uint64_t)(s >> 2) * b_step_kb + (uint64_t)(s & 3) * 2;
-        umma_f16_warp(d, a0 + ao, b0 + bo, idesc, s > 0 ? 1u : 0u);
+        umma_f16_warp(d, a0 + ao, b0 + bo, idesc, (s > 0 || acc0) ? 1u : 0u);
       }
     }
   }
@@ -368,7 +383,7 @@ __device__ __forceinline__ void tc_forward_body(const TcProgram& p, const unsign
       if (lt < 32) {  // the slot's first warp issues (one elected lane per MMA) and waits
         TC_PROF_T(t_issue);
         tc_fence_after();
-        issue_layer<SPLIT>(L, l == 0, tmem_base, s_a, s_image, stage);
+        issue_layer<SPLIT>(L, l == 0, tmem_base, s_a, s_image, stage, s_image + p.ones_off, s_image + p.zero_off);
         // (the wait-bound test build drops the first layer's signal of the first tile)
         if (!(PONNI_B200_SKIP_ARRIVE() && l == 0 && tile == (int64_t)blockIdx.x * nslots + wg)) umma_commit_warp(s_bar);
         TC_PROF_ADD(3, t_issue);

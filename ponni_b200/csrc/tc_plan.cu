@@ -102,13 +102,39 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
     L.idesc_mn = make_idesc(dt, L.n_pad, true);
     if (l + 1 < blocks.size()) max_w32 = std::max(max_w32, (int)round_up(L.n_pad, 32));
   }
-  // Image: biases first (float, padded to 32 columns), then weights at
-  // 1024-byte aligned offsets.
+  // Image: biases first, then weights at 1024-byte aligned offsets.
+  // fp32 (split) models: float biases padded to 32 columns, added in the
+  // epilogue.  16-bit models: the bias is one more UMMA of K = 16 whose A is
+  // a column of ones and whose B holds the bias in column 0, both in the
+  // no-swizzle K-major layout (core matrices of 8 rows x 16 bytes).  Only the
+  // first K half (elements 0-7) of each row is stored: the ones block is one
+  // core matrix that every row group of A reads (row-group stride 0), a bias
+  // block is n_pad / 8 core matrices (row-group stride 128 bytes), and the
+  // second K half of both points into one shared block of zeros.  The
+  // epilogue then neither loads nor adds the bias.
   size_t off = 0;
+  bool any_bias = false;
+  for (const auto& b : blocks) any_bias = any_bias || b.bias != nullptr;
+  if (!split && any_bias) {
+    p.ones_off = 0;
+    off = 128;
+  }
+  int max_np = 0;
   for (int l = 0; l < p.n_layers; ++l) {
     TcLayer& L = p.layers[l];
     L.bias_off = (uint32_t)off;
-    off += round_up(round_up(L.n_pad, 32) * 4, 16);
+    if (split) {
+      off += round_up(round_up(L.n_pad, 32) * 4, 16);
+    } else if (L.has_bias) {
+      L.has_bias = 0;
+      L.bias_mma = 1;
+      off += (size_t)L.n_pad * 16;
+      max_np = std::max(max_np, L.n_pad);
+    }
+  }
+  if (!split && any_bias) {
+    p.zero_off = (uint32_t)off;
+    off += (size_t)max_np * 16;
   }
   off = round_up(off, 1024);
   for (int l = 0; l < p.n_layers; ++l) {
@@ -122,14 +148,26 @@ bool tc_plan(const ponni_b200_model* m, TcProgram& p, std::vector<unsigned char>
   }
   p.image_bytes = (uint32_t)round_up(off, 1024);
   image.assign(p.image_bytes, 0);
+  if (!split && any_bias) {
+    // ones block: rows 0..7, K = 0 is 1.0 in the model's 16-bit type
+    const uint16_t one = dt == PONNI_B200_F16 ? 0x3C00u : 0x3F80u;
+    for (int r = 0; r < 8; ++r) memcpy(image.data() + p.ones_off + (size_t)r * 16, &one, 2);
+  }
   for (int l = 0; l < p.n_layers; ++l) {
     const TcLayer& L = p.layers[l];
     const Layer& mv = *blocks[l].mv;
-    if (blocks[l].bias) {
+    if (blocks[l].bias && split) {
       float* b = reinterpret_cast<float*>(image.data() + L.bias_off);
       for (int f = 0; f < L.nout; ++f) {
         b[f] = (float)load_scalar(dt, blocks[l].bias->params.data() + f * msz);
         if (rec) rec->add(blocks[l].bias->params.data() + f * msz, PIMG_TC, PENC_F32, L.bias_off + 4 * (size_t)f);
+      }
+    } else if (blocks[l].bias) {
+      // bias[n] at K = 0 of row n: row group n / 8, row n % 8 of its core matrix
+      for (int f = 0; f < L.nout; ++f) {
+        const size_t o = L.bias_off + (size_t)(f >> 3) * 128 + (size_t)(f & 7) * 16;
+        memcpy(image.data() + o, blocks[l].bias->params.data() + f * msz, msz);
+        if (rec) rec->add(blocks[l].bias->params.data() + f * msz, PIMG_TC, PENC_MODEL, o);
       }
     }
     for (int k = 0; k < L.nin; ++k) {

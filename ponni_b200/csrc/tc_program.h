@@ -35,8 +35,10 @@ struct TcLayer {
   int32_t n_pad;         // N rounded to 16 (UMMA N for M=128)
   int32_t act, act_flags;
   float s0, s1;          // activation scalars
-  int32_t has_bias;
-  uint32_t bias_off;     // byte offset of float bias[n_pad] in the staged image
+  int32_t has_bias;      // the epilogue adds float bias[n_pad] (fp32 split models)
+  uint32_t bias_off;     // byte offset of that float bias in the staged image
+  int32_t bias_mma;      // 16-bit models: the bias enters the accumulator through one extra UMMA
+                         // (A = a column of ones, B = the bias block at bias_off)
   uint32_t w_off[3];     // byte offsets of the K-major B operand parts (1, or 3 for split fp32)
   uint32_t idesc;        // UMMA instruction descriptor (A K-major)
   uint32_t idesc_mn;     // same with A MN-major (layer 0)
@@ -50,6 +52,8 @@ struct TcProgram {
   int32_t nin, nout;
   int32_t nparts;        // operand parts: 3 (fp32 split into bf16 b0+b1+b2) or 1
   uint32_t image_bytes;  // staged parameter image (multiple of 16)
+  uint32_t ones_off;     // 16-bit models with a bias: byte offset of the ones block (A of the bias UMMA)
+  uint32_t zero_off;     //   and of the zero block that the second K half of every bias UMMA operand reads
   uint32_t a_bytes;      // one activation operand buffer (one part)
   uint32_t stage_bytes;  // one input staging buffer (one per slot)
   uint32_t slot_bytes;   // shared memory of one slot: parts x a_bytes + stage_bytes
