@@ -74,6 +74,23 @@ def test_tc_cfg3_16bit(dtype, batch, oracle_lib):
     check_acc32(y, cfg.layers, dtype, x, oracle_lib)
 
 
+@pytest.mark.parametrize("dtype", [pb.F16, pb.BF16])
+def test_tc_cfg3_nan_inputs_relu(dtype, oracle_lib):
+    """A NaN input makes a column's layer-0 pre-activations NaN; ReLU maps
+    them to 0 as the reference's x > 0 ? x : 0 does, so the outputs stay
+    finite and equal the oracle's."""
+    cfg = configs.cfg3(batch=300)
+    xf = K.as_float(configs.host_inputs(cfg, 300), cfg.dtype).astype(np.float32)
+    xf[:, 7] = np.nan
+    xf[3, 100] = np.nan
+    x = pb.to_dtype_bytes(xf, dtype)
+    y = K.as_float(run_tc(cfg.layers, dtype, x), dtype)
+    assert np.all(np.isfinite(y))
+    a32 = K.as_float(oracle_lib.forward(cfg.layers, dtype, x, acc32=True), dtype)
+    assert np.all(np.isfinite(a32))
+    assert K.normwise_err(y, a32) <= {pb.F16: 2e-3, pb.BF16: 1.2e-2}[dtype]
+
+
 @pytest.mark.parametrize("dtype", [pb.F32, pb.F16, pb.BF16])
 def test_tc_odd_widths_all_activations(dtype, oracle_lib):
     rng = np.random.default_rng(11)
