@@ -254,8 +254,9 @@ int64_t ponni_b200_internal_state_capacity(const ponni_b200_model* model);
 int ponni_b200_planned_temporary_size(const ponni_b200_model* model, int which);
 int ponni_b200_saved_state_size(const ponni_b200_model* model, int index);
 int ponni_b200_num_saved_states(const ponni_b200_model* model);
-/* Bytes of device scratch currently allocated (0: every supported program
- * keeps its intermediate states on chip). */
+/* Bytes of device scratch currently allocated: 0 unless the program is an
+ * fp32 residual chain with two distinct saved states (the residual
+ * tensor-core kernel keeps a single saved state on chip). */
 int64_t ponni_b200_scratch_bytes(const ponni_b200_model* model);
 
 /* Trainable parameters in tuple (declaration) order, model dtype, host memory. */
