@@ -331,7 +331,7 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
     // through TMEM: each warp writes its pair into the first two of its own,
     // already read, accumulator columns; one barrier; each warp reads the
     // pairs of the row's quarters.
-    const uint32_t corr_row = E.tmem_row;
+    const uint32_t xrow = E.tmem_row;  // exchange columns: the first two of each warp's own, already read, columns
     if (active) {
       float qmean, qm2;
       if (nv >= 32) {
@@ -362,7 +362,7 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
             qm2 = __fadd_rn(qm2, __fmul_rn(d, d));
           }
       }
-      tmem_st2(corr_row + (uint32_t)c0, qmean, qm2);
+      tmem_st2(xrow + (uint32_t)c0, qmean, qm2);
     }
     tc_fence_before();
     epi_sync(E.lq);
@@ -373,7 +373,7 @@ __device__ __forceinline__ void tr_epilogue(const TrProgram& p, int l, const TrE
       uint32_t ta[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q)  // quarters past n_pad read quarter 0 (ignored below)
-        ta[q] = corr_row + (uint32_t)(32 * q < n_pad ? 32 * q : 0);
+        ta[q] = xrow + (uint32_t)(32 * q < n_pad ? 32 * q : 0);
       tmem_ld2x4(ta, qm, q2);
       const float n = (float)nout;
       float tot = 0.f;
